@@ -1,0 +1,176 @@
+/*
+ * b200attn -- C ABI of the B200 (sm_100a) GQA attention hot path.
+ *
+ * Drop-in for the attention entry points of MarcVivas/llm-inference's
+ * include/kernels/kernels.hpp. Every reference launcher has one extern "C"
+ * symbol here with the same parameter order and meaning; the differences are
+ * only those a C ABI needs:
+ *   - __half* becomes void* (IEEE binary16 payload, row-major),
+ *   - hipStream_t / hipGraphExec_t / hipGraphNode_t become the CUDA handles
+ *     below (the same types as cudaStream_t / cudaGraphExec_t /
+ *     cudaGraphNode_t, declared here without the CUDA headers),
+ *   - every call returns an int status instead of void (B2_OK or
+ *     B2_NOTHING_TO_DO on success, a negative B2_ERR_* otherwise); nothing
+ *     exits the process or throws across this boundary,
+ *   - prefill takes the stream the reference launcher lacks.
+ * include/kernels/kernels.hpp in this repository re-declares the reference's
+ * C++ names and default arguments on top of these symbols.
+ *
+ * Ownership: the caller owns every buffer (Q/K/V activations, the KV cache,
+ * the RoPE tables, outputs, the decode partial workspace). No call allocates
+ * device memory, synchronises, or reads device memory from the host, so every
+ * launcher can be captured into a CUDA graph.
+ */
+#ifndef B200ATTN_H
+#define B200ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same underlying types as cudaStream_t, cudaGraphExec_t, cudaGraphNode_t. */
+typedef struct CUstream_st* b2_stream_t;
+typedef struct CUgraphExec_st* b2_graph_exec_t;
+typedef struct CUgraphNode_st* b2_graph_node_t;
+
+/* Status codes. */
+#define B2_OK 0
+#define B2_NOTHING_TO_DO 1       /* a case the reference launcher silently skips */
+#define B2_ERR_INVALID_ARG (-1)  /* null buffer, bad GQA config the kernel cannot run */
+#define B2_ERR_UNSUPPORTED (-2)  /* shape outside what the kernels implement */
+#define B2_ERR_ALIGNMENT (-3)    /* pointer/stride alignment a TMA path needs */
+#define B2_ERR_CUDA (-4)         /* a CUDA runtime call failed; see b2_last_cuda_error */
+#define B2_ERR_WORKSPACE (-5)    /* workspace smaller than the call needs */
+#define B2_ERR_GRAPH (-6)        /* capture query / node patch failed */
+
+/* Tokens per flash-decode chunk; the reference's KV_CHUNK macro
+ * (include/kernels/kernels.hpp:103, 12 there). Partial workspaces are sized
+ * [num_heads][ceil(kv_len / b2_kv_chunk())]. */
+int b2_kv_chunk(void);
+
+/* Floats of decode workspace the reference engine allocates for a cache of
+ * max_kv_len tokens: num_heads * ceil(max_kv_len / KV_CHUNK) * (head_dim + 2)
+ * (include/model_inference.hpp:192-198). */
+size_t b2_decode_workspace_floats(size_t num_heads, size_t head_dim, size_t max_kv_len);
+
+const char* b2_status_string(int status);
+int b2_last_cuda_error(void);            /* cudaError_t of the last B2_ERR_CUDA */
+uint64_t b2_kernel_launch_count(void);   /* kernels this library has launched */
+
+/* Host-side RoPE tables, include/rope_cache.hpp:49-76 (compute_inverse_frequencies,
+ * fill_host_tables): cos/sin[pos][i] = fp16(cos/sin(float(pos) * inv_freq[i])),
+ * inv_freq[i] = 1 / theta^(2i/head_dim), FP32 host math. Tables are
+ * [max_seq_len][head_dim/2] binary16. Pure host code; no device call. */
+int b2_fill_rope_tables(size_t max_seq_len, size_t head_dim, float rope_theta,
+                        uint16_t* host_cos, uint16_t* host_sin);
+
+/* include/kernels/kernels.hpp:47-60 launch_rope (src/kernels/rope.hip.cpp:198-205):
+ * rotate-half RoPE on Q and K in place at positions start_pos + t. */
+int b2_launch_rope(void* d_q, void* d_k, const void* d_cos, const void* d_sin,
+                   size_t seq_len, size_t num_heads, size_t num_kv_heads,
+                   size_t head_dim, size_t q_stride, size_t k_stride,
+                   size_t start_pos, b2_stream_t stream);
+
+/* include/kernels/kernels.hpp:62-80 launch_rope_and_store_kv
+ * (src/kernels/rope.hip.cpp:138-196): with apply_rotation, Q is rotated in
+ * place and rotated K plus unchanged V are written to cache rows
+ * start_pos + t (row stride num_kv_heads * head_dim); without it K and V are
+ * copied verbatim (NoPE layers) and Q is untouched. K/V sources are never
+ * modified when a cache is given. d_k_cache == NULL with apply_rotation
+ * rotates K in place (the launch_rope path). Strides are elements between
+ * tokens; V uses k_stride; 0 means packed. */
+int b2_launch_rope_and_store_kv(void* d_q, void* d_k, const void* d_v,
+                                void* d_k_cache, void* d_v_cache,
+                                const void* d_cos, const void* d_sin,
+                                size_t seq_len, size_t num_heads, size_t num_kv_heads,
+                                size_t head_dim, size_t q_stride, size_t k_stride,
+                                size_t start_pos, bool apply_rotation,
+                                b2_stream_t stream);
+
+/* include/kernels/kernels.hpp:81-86 update_rope_and_store_kv_node
+ * (src/kernels/rope.hip.cpp:208-241): re-point a captured RoPE/append node of
+ * graph_exec at a new start_pos. apply_rotation must match the capture. */
+int b2_update_rope_and_store_kv_node(b2_graph_exec_t graph_exec, b2_graph_node_t node,
+                                     size_t start_pos, bool apply_rotation);
+
+/* include/kernels/kernels.hpp:88-99 launch_causal_attention_prefill
+ * (src/kernels/causal_attention.hip.cpp:376-451): out[t][h*d + c] (packed,
+ * stride num_heads*head_dim) = softmax_{j<=t}(q_t . k_j / sqrt(d)) V for
+ * kv head h / (num_heads / num_kv_heads). start_pos = 0, kv_len = seq_len.
+ * Head_dim 128 with 16-byte aligned rows runs the tcgen05/TMA kernel; other
+ * shapes run a SIMT kernel. */
+int b2_launch_causal_attention_prefill(const void* d_q, const void* d_k, const void* d_v,
+                                       void* d_out, size_t seq_len, size_t num_heads,
+                                       size_t num_kv_heads, size_t head_dim,
+                                       size_t q_stride, size_t kv_stride,
+                                       b2_stream_t stream);
+
+/* include/kernels/kernels.hpp:104-125 launch_causal_attention_decode
+ * (src/kernels/causal_attention.hip.cpp:840-921): one query token over
+ * kv_cache_len cached tokens, split into KV_CHUNK-token chunks whose (o, m, l)
+ * partials go to d_partial_out [H][chunks][d], d_partial_max [H][chunks],
+ * d_partial_weight_sum [H][chunks], then merged into d_out [H][d] fp16.
+ * Q is one packed [num_heads][head_dim] vector at d_q (q_stride and
+ * start_pos are accepted and unused, as in the reference). When
+ * attention_node / merge_node are non-null the stream must be capturing and
+ * they receive the two captured kernel nodes. */
+int b2_launch_causal_attention_decode(const void* d_q, const void* d_k_cache,
+                                      const void* d_v_cache, void* d_out,
+                                      float* d_partial_out, float* d_partial_max,
+                                      float* d_partial_weight_sum,
+                                      size_t query_len, size_t kv_cache_len,
+                                      size_t start_pos, size_t num_heads,
+                                      size_t num_kv_heads, size_t head_dim,
+                                      size_t q_stride, size_t kv_stride,
+                                      b2_stream_t stream,
+                                      b2_graph_node_t* attention_node,
+                                      b2_graph_node_t* merge_node);
+
+/* include/kernels/kernels.hpp:127-146 launch_causal_attention_decode_vectorized
+ * (src/kernels/causal_attention.hip.cpp:923-972). Same contract as
+ * b2_launch_causal_attention_decode (both run the same kernels here). */
+int b2_launch_causal_attention_decode_vectorized(const void* d_q, const void* d_k_cache,
+                                                 const void* d_v_cache, void* d_out,
+                                                 float* d_partial_out, float* d_partial_max,
+                                                 float* d_partial_weight_sum,
+                                                 size_t query_len, size_t kv_cache_len,
+                                                 size_t start_pos, size_t num_heads,
+                                                 size_t num_kv_heads, size_t head_dim,
+                                                 size_t q_stride, size_t kv_stride,
+                                                 b2_stream_t stream,
+                                                 b2_graph_node_t* attention_node,
+                                                 b2_graph_node_t* merge_node);
+
+/* include/kernels/kernels.hpp:190-194 update_causal_attention_decode_node
+ * (src/kernels/causal_attention.hip.cpp:975-1001): patch kv_cache_len (and
+ * the chunk count / grid) of a captured split-KV node. */
+int b2_update_causal_attention_decode_node(b2_graph_exec_t graph_exec, b2_graph_node_t node,
+                                           size_t kv_cache_len);
+
+/* include/kernels/kernels.hpp:148-152 update_merge_attention_decode_node
+ * (src/kernels/causal_attention.hip.cpp:1003-1026): patch the chunk count of a
+ * captured merge node. */
+int b2_update_merge_attention_decode_node(b2_graph_exec_t graph_exec, b2_graph_node_t node,
+                                          size_t kv_cache_len);
+
+/* include/kernels/kernels.hpp:157-166 launch_merge_attention_decode_tiled
+ * (declared there, defined nowhere): merge caller-provided partials
+ * [H][chunks][d] / [H][chunks] / [H][chunks] into d_out [H][d] fp16, warps
+ * across chunks and lanes across output dimensions. */
+int b2_launch_merge_attention_decode_tiled(const float* d_partial_output,
+                                           const float* d_partial_max,
+                                           const float* d_partial_weight_sum,
+                                           void* d_out, size_t num_heads,
+                                           size_t num_kv_chunks, size_t head_dim,
+                                           b2_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200ATTN_H */

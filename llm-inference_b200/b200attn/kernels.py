@@ -1,0 +1,158 @@
+"""The reference's attention launchers (include/kernels/kernels.hpp), in Python.
+
+Same names, argument order, meaning and defaults as the C++ declarations; each
+forwards to the matching ``b2_*`` C-ABI symbol of libb200attn.so. Buffers are
+device pointers given as ``torch.Tensor`` (its ``data_ptr()``) or ``int``;
+streams are ``torch.cuda.Stream``, a raw ``int`` handle, or ``None`` for the
+legacy default stream (the reference's ``nullptr`` default).
+
+Errors: the reference launchers return ``void`` and silently skip empty or
+invalid GQA configurations; these functions do the same (return normally).
+Every other failure raises ``B2Error`` where the reference would have exited
+the process through HIP_CHECK (include/gpu_utils.hpp:7-14).
+"""
+from __future__ import annotations
+
+import ctypes
+
+from ._lib import B2Error, check, lib
+
+__all__ = [
+    "B2Error", "launch_rope", "launch_rope_and_store_kv", "update_rope_and_store_kv_node",
+    "launch_causal_attention_prefill", "launch_causal_attention_decode",
+    "launch_causal_attention_decode_vectorized", "update_causal_attention_decode_node",
+    "update_merge_attention_decode_node", "launch_merge_attention_decode_tiled",
+    "decode_workspace_floats", "kernel_launch_count",
+]
+
+
+def _ptr(x):
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    dp = getattr(x, "data_ptr", None)
+    if dp is None:
+        raise TypeError(f"expected a device tensor or int pointer, got {type(x)}")
+    if getattr(x, "is_cuda", True) is False:
+        raise ValueError("b200attn launchers take device buffers; got a host tensor")
+    return dp()
+
+
+def _stream(s):
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream
+
+
+def _kv_chunk() -> int:
+    return int(lib().b2_kv_chunk())
+
+
+def __getattr__(name):
+    if name == "KV_CHUNK":
+        return _kv_chunk()
+    raise AttributeError(name)
+
+
+def decode_workspace_floats(num_heads: int, head_dim: int, max_kv_len: int) -> int:
+    """include/model_inference.hpp:192-198 sizing: H * ceil(max/KV_CHUNK) * (d+2)."""
+    return int(lib().b2_decode_workspace_floats(num_heads, head_dim, max_kv_len))
+
+
+def kernel_launch_count() -> int:
+    return int(lib().b2_kernel_launch_count())
+
+
+def launch_rope(d_q, d_k, d_cos, d_sin, seq_len, num_heads, num_kv_heads, head_dim,
+                q_stride, k_stride, start_pos=0, stream=None):
+    """kernels.hpp:47-60 -- RoPE on Q and K in place."""
+    check(lib().b2_launch_rope(_ptr(d_q), _ptr(d_k), _ptr(d_cos), _ptr(d_sin), seq_len, num_heads,
+                               num_kv_heads, head_dim, q_stride, k_stride, start_pos, _stream(stream)),
+          "launch_rope")
+
+
+def launch_rope_and_store_kv(d_q, d_k, d_v, d_k_cache, d_v_cache, d_cos, d_sin, seq_len, num_heads,
+                             num_kv_heads, head_dim, q_stride, k_stride, start_pos, apply_rotation,
+                             stream=None):
+    """kernels.hpp:62-80 -- RoPE Q in place, rotated K + V (or verbatim K/V) into the cache."""
+    check(lib().b2_launch_rope_and_store_kv(
+        _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_cos), _ptr(d_sin),
+        seq_len, num_heads, num_kv_heads, head_dim, q_stride, k_stride, start_pos, bool(apply_rotation),
+        _stream(stream)), "launch_rope_and_store_kv")
+
+
+def update_rope_and_store_kv_node(graph_exec, node, start_pos, apply_rotation):
+    """kernels.hpp:81-86."""
+    check(lib().b2_update_rope_and_store_kv_node(int(graph_exec), int(node), start_pos, bool(apply_rotation)),
+          "update_rope_and_store_kv_node")
+
+
+def launch_causal_attention_prefill(d_q, d_k, d_v, d_out, seq_len, num_heads, num_kv_heads, head_dim,
+                                    q_stride=0, kv_stride=0, stream=None):
+    """kernels.hpp:88-99 (plus the stream the reference lacks)."""
+    check(lib().b2_launch_causal_attention_prefill(
+        _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_out), seq_len, num_heads, num_kv_heads, head_dim,
+        q_stride, kv_stride, _stream(stream)), "launch_causal_attention_prefill")
+
+
+def _decode(fn, name, d_q, d_k_cache, d_v_cache, d_out, d_partial_out, d_partial_max,
+            d_partial_weight_sum, query_len, kv_cache_len, start_pos, num_heads, num_kv_heads,
+            head_dim, q_stride, kv_stride, stream, capture_nodes):
+    an = ctypes.c_void_p()
+    mn = ctypes.c_void_p()
+    check(fn(_ptr(d_q), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_out), _ptr(d_partial_out),
+             _ptr(d_partial_max), _ptr(d_partial_weight_sum), query_len, kv_cache_len, start_pos,
+             num_heads, num_kv_heads, head_dim, q_stride, kv_stride, _stream(stream),
+             ctypes.byref(an) if capture_nodes else None,
+             ctypes.byref(mn) if capture_nodes else None), name)
+    if capture_nodes:
+        return an.value, mn.value
+    return None
+
+
+def launch_causal_attention_decode(d_q, d_k_cache, d_v_cache, d_out, d_partial_out, d_partial_max,
+                                   d_partial_weight_sum, query_len, kv_cache_len, start_pos, num_heads,
+                                   num_kv_heads, head_dim, q_stride, kv_stride, stream=None,
+                                   capture_nodes=False):
+    """kernels.hpp:104-125. With capture_nodes=True (stream capturing) returns the
+    (attention_node, merge_node) handles the reference writes through its out-pointers."""
+    return _decode(lib().b2_launch_causal_attention_decode, "launch_causal_attention_decode", d_q,
+                   d_k_cache, d_v_cache, d_out, d_partial_out, d_partial_max, d_partial_weight_sum,
+                   query_len, kv_cache_len, start_pos, num_heads, num_kv_heads, head_dim, q_stride,
+                   kv_stride, stream, capture_nodes)
+
+
+def launch_causal_attention_decode_vectorized(d_q, d_k_cache, d_v_cache, d_out, d_partial_out,
+                                              d_partial_max, d_partial_weight_sum, query_len,
+                                              kv_cache_len, start_pos, num_heads, num_kv_heads,
+                                              head_dim, q_stride=0, kv_stride=0, stream=None,
+                                              capture_nodes=False):
+    """kernels.hpp:127-146."""
+    return _decode(lib().b2_launch_causal_attention_decode_vectorized,
+                   "launch_causal_attention_decode_vectorized", d_q, d_k_cache, d_v_cache, d_out,
+                   d_partial_out, d_partial_max, d_partial_weight_sum, query_len, kv_cache_len,
+                   start_pos, num_heads, num_kv_heads, head_dim, q_stride, kv_stride, stream,
+                   capture_nodes)
+
+
+def update_causal_attention_decode_node(graph_exec, node, kv_cache_len):
+    """kernels.hpp:190-194."""
+    check(lib().b2_update_causal_attention_decode_node(int(graph_exec), int(node), kv_cache_len),
+          "update_causal_attention_decode_node")
+
+
+def update_merge_attention_decode_node(graph_exec, node, kv_cache_len):
+    """kernels.hpp:148-152."""
+    check(lib().b2_update_merge_attention_decode_node(int(graph_exec), int(node), kv_cache_len),
+          "update_merge_attention_decode_node")
+
+
+def launch_merge_attention_decode_tiled(d_partial_output, d_partial_max, d_partial_weight_sum, d_out,
+                                        num_heads, num_kv_chunks, head_dim, stream=None):
+    """kernels.hpp:157-166 (declared, never defined, in the reference)."""
+    check(lib().b2_launch_merge_attention_decode_tiled(
+        _ptr(d_partial_output), _ptr(d_partial_max), _ptr(d_partial_weight_sum), _ptr(d_out),
+        num_heads, num_kv_chunks, head_dim, _stream(stream)), "launch_merge_attention_decode_tiled")

@@ -1,0 +1,93 @@
+"""Build libb200attn.so (the C-ABI CUDA library) in-tree for sm_100a.
+
+    python llm-inference_b200/build.py [--force] [--verbose]
+
+Each CUDA translation unit under csrc/ is compiled by nvcc with
+``-gencode arch=compute_100a,code=sm_100a`` into _build/, then linked with the
+static CUDA runtime into b200attn/libb200attn.so. ptxas resource usage
+(registers, spills, shared memory) is kept in _build/ptxas.log.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_ROOT = os.path.dirname(os.path.abspath(__file__))
+REPO_ROOT = os.path.dirname(PKG_ROOT)
+CSRC = os.path.join(PKG_ROOT, "csrc")
+BUILD = os.path.join(PKG_ROOT, "_build")
+INCLUDE = os.path.join(REPO_ROOT, "include")
+LIB = os.path.join(PKG_ROOT, "b200attn", "libb200attn.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", *ARCH, "-Xcompiler", "-fPIC,-O3",
+              "-Xptxas", "-v", f"-I{INCLUDE}", f"-I{CSRC}"]
+
+
+def _nvcc() -> str:
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: the b200attn CUDA library cannot be built")
+
+
+def sources() -> list[str]:
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
+def _headers() -> list[str]:
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
+    hs += [os.path.join(INCLUDE, "b200attn.h")]
+    return hs
+
+
+def _compile(src: str, verbose: bool) -> tuple[str, str]:
+    obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+    cmd = [_nvcc(), *NVCC_FLAGS, "-c", src, "-o", obj]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{res.stdout}\n{res.stderr}")
+    return obj, res.stderr
+
+
+def needs_build() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    return any(os.path.getmtime(p) > t for p in sources() + _headers() + [os.path.abspath(__file__)])
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not needs_build():
+        return LIB
+    os.makedirs(BUILD, exist_ok=True)
+    srcs = sources()
+    with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
+        results = list(ex.map(lambda s: _compile(s, verbose), srcs))
+    with open(os.path.join(BUILD, "ptxas.log"), "w") as f:
+        for (obj, log), src in zip(results, srcs):
+            f.write(f"== {os.path.basename(src)}\n{log}\n")
+    tmp = LIB + f".tmp{os.getpid()}"
+    cmd = [_nvcc(), "-shared", *ARCH, "-o", tmp, *[o for o, _ in results]]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    args = ap.parse_args()
+    print(build(force=args.force, verbose=args.verbose))
+    sys.exit(0)

@@ -1,0 +1,63 @@
+// Shared helpers of the b200attn CUDA library (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b200attn.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
+#error "b200attn is built for sm_100a only"
+#endif
+
+namespace b2 {
+
+// Library-wide bookkeeping (b2_status.cu).
+void note_cuda_error(cudaError_t e);
+void count_launch(uint64_t n = 1);
+
+// Turn the launch status of the kernel just enqueued into a b2 status.
+inline int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return B2_ERR_CUDA;
+    }
+    count_launch();
+    return B2_OK;
+}
+
+inline int cuda_status(cudaError_t e) {
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return B2_ERR_CUDA;
+    }
+    return B2_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The node most recently added to a capturing stream (the CUDA form of the
+// reference's last_captured_node, include/gpu_utils.hpp:45-58).
+int last_captured_node(cudaStream_t stream, cudaGraphNode_t* node);
+
+// Read a captured kernel node's parameters, check that it runs `expected`
+// (one of this library's kernels) and return its parameter block.
+int node_kernel_params(cudaGraphNode_t node, const void* const* expected, int n_expected,
+                       cudaKernelNodeParams* params);
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+}  // namespace b2

@@ -1,0 +1,87 @@
+#!/usr/bin/env python3
+"""Regenerate the golden vectors in this directory.
+
+The reference engine's own fixtures (tests/reference/*.bin) come from its
+fixture generator, python/reference.py:40-96 (``save_activations``), run on
+the HF SmolLM3-3B checkpoint; neither the fixtures nor the checkpoint are
+available. This script runs that same, unmodified ``save_activations`` on a
+seeded random-init SmolLM3 model of the same attention geometry (16 query
+heads, 4 KV heads, head_dim 128, RoPE theta 5e6, FP16 on CPU) and keeps the
+dumps on the attention hot path:
+
+    layer0_q_proj_out.bin  layer0_k_proj_out.bin  layer0_v_proj_out.bin
+    layer0_q_rope.bin      layer0_k_rope.bin      layer0_attn_out.bin
+
+Each is raw little-endian FP16 exactly as python/reference.py:18-22 writes
+it. ``meta.json`` records the geometry, seed and library versions.
+
+It needs the reference checkout (set REFERENCE_ROOT, default the read-only
+mount this build was made against) and runs on CPU only. Nothing on a GPU box
+runs it; the tests read only the committed outputs.
+"""
+from __future__ import annotations
+
+import json
+import os
+import shutil
+import sys
+import tempfile
+from pathlib import Path
+
+KEEP = ["layer0_q_proj_out", "layer0_k_proj_out", "layer0_v_proj_out",
+        "layer0_q_rope", "layer0_k_rope", "layer0_attn_out"]
+
+
+class _TokenizerStub:
+    """save_activations only calls tokenizer.decode on the greedy token."""
+
+    def decode(self, ids):
+        return " ".join(str(i) for i in ids)
+
+
+def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None) -> None:
+    ref_root = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+    sys.path.insert(0, str(ref_root / "python"))
+    import torch
+    import transformers
+    from transformers import SmolLM3Config, SmolLM3ForCausalLM
+
+    import reference  # python/reference.py of the reference checkout
+
+    torch.manual_seed(seed)
+    config = SmolLM3Config(
+        vocab_size=1024, hidden_size=2048, intermediate_size=512,
+        num_hidden_layers=1, num_attention_heads=16, num_key_value_heads=4,
+        max_position_embeddings=4096, initializer_range=0.04,
+        rope_parameters={"rope_type": "default", "rope_theta": 5.0e6},
+        tie_word_embeddings=True, pad_token_id=0, bos_token_id=1, eos_token_id=2,
+    )
+    # _from_config(dtype=fp16) builds the model the way from_pretrained(
+    # torch_dtype=fp16) does (python/reference.py:137-143): weights in FP16,
+    # the rotary inv_freq buffer left in FP32.
+    model = SmolLM3ForCausalLM._from_config(config, dtype=torch.float16).eval()
+    assert model.model.rotary_emb.inv_freq.dtype == torch.float32
+    gen = torch.Generator().manual_seed(seed + 1)
+    input_ids = torch.randint(0, config.vocab_size, (1, seq_len), generator=gen)
+
+    out = Path(out_dir) if out_dir else Path(__file__).resolve().parent
+    with tempfile.TemporaryDirectory() as tmp:
+        reference.save_activations(model, _TokenizerStub(), Path(tmp), seq_len, input_ids)
+        for name in KEEP:
+            shutil.copyfile(Path(tmp) / f"{name}.bin", out / f"{name}.bin")
+    meta = {
+        "generator": "python/reference.py save_activations (reference checkout, unmodified)",
+        "model": "SmolLM3ForCausalLM, random init (initializer_range 0.04), 1 layer, fp16, CPU",
+        "seq_len": seq_len, "num_heads": 16, "num_kv_heads": 4, "head_dim": 128,
+        "rope_theta": 5.0e6, "seed": seed,
+        "torch": torch.__version__, "transformers": transformers.__version__,
+        "reference_pins": {"torch": "2.14.0+rocm (python/requirements.txt:79)",
+                           "transformers": "5.17.0 (python/requirements.txt:82)"},
+        "files": {name: f"{name}.bin" for name in KEEP},
+    }
+    (out / "meta.json").write_text(json.dumps(meta, indent=2) + "\n")
+    print(f"wrote {len(KEEP)} fixtures to {out}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+"""Split-KV flash-decode + merge on the GPU vs the CPU oracle and the golden
+vectors. Restates tests/test_causal_attention.cpp:80-228."""
+import numpy as np
+import pytest
+
+import b200attn
+import oracle
+from _gpu import Graph, bits, dev, host
+from _util import assert_attention_close, golden, max_abs, seeded_f16, tensor_close_mismatches
+from test_oracle import KAT_LENGTHS, _kat_expected, _kat_inputs
+
+pytestmark = pytest.mark.gpu
+CHUNK = 256
+
+
+def _sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+def _workspace(heads, kv_len, head_dim):
+    import torch
+    chunks = (kv_len + CHUNK - 1) // CHUNK
+    po = torch.full((heads * chunks * head_dim,), float("nan"), dtype=torch.float32, device="cuda")
+    pm = torch.full((heads * chunks,), float("nan"), dtype=torch.float32, device="cuda")
+    pl = torch.full((heads * chunks,), float("nan"), dtype=torch.float32, device="cuda")
+    return po, pm, pl
+
+
+def _decode(entry, q, k, v, kv_len, H, KVH, d, kv_stride, guard=1):
+    """Run a decode entry point with -123 guards around the output; return output, guards, partials."""
+    out = np.full(H * d + 2 * guard, -123.0, np.float16)
+    dout = dev(out)
+    po, pm, pl = _workspace(H, kv_len, d)
+    entry(dev(q), dev(k), dev(v), dout[guard:], po, pm, pl, 1, kv_len, kv_len - 1, H, KVH, d, 0, kv_stride)
+    _sync()
+    res = host(dout)
+    return res[guard:guard + H * d], np.concatenate([res[:guard], res[guard + H * d:]]), (po, pm, pl)
+
+
+ENTRIES = {
+    "decode": lambda *a: b200attn.launch_causal_attention_decode(*a),
+    "vectorized": lambda *a: b200attn.launch_causal_attention_decode_vectorized(*a),
+}
+
+
+@pytest.mark.parametrize("entry", ["decode", "vectorized"])
+@pytest.mark.parametrize("head_dim", [32, 128])
+@pytest.mark.parametrize("kv_heads", [1, 2, 4])
+@pytest.mark.parametrize("padded", [False, True])
+def test_flash_decode_known_answer(cuda, entry, head_dim, kv_heads, padded):
+    """tests/test_causal_attention.cpp:152-228, with KV_CHUNK boundaries added."""
+    heads = 4
+    for length in KAT_LENGTHS + [255, 511, 1025]:
+        q, k, v, stride = _kat_inputs(head_dim, kv_heads, length, padded)
+        exp = _kat_expected(q, k, v, heads, kv_heads, head_dim, length, stride)
+        got, guards, _ = _decode(ENTRIES[entry], q, k, v, length, heads, kv_heads, head_dim,
+                                 stride if padded else 0)
+        assert np.all(guards == np.float16(-123.0))
+        assert np.all(np.isfinite(got.astype(np.float32)))
+        assert tensor_close_mismatches(got, exp, 2e-3, 2e-3) == 0, (length,)
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_decode_matches_golden_prefill_rows(cuda, interleaved):
+    """tests/test_causal_attention.cpp:80-150: decode at kv_len p+1 == prefill row p;
+    future cache rows hold 123, output guards -123."""
+    meta, g = golden()
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    q_dim, kv_dim = H * d, KVH * d
+    cache_k = np.full((S + 2, kv_dim), 123.0, np.float16)
+    cache_v = cache_k.copy()
+    cache_k[:S] = g["k_rope"]
+    cache_v[:S] = g["v"]
+    dk, dv = dev(cache_k), dev(cache_v)
+    for p in range(S):
+        stride = q_dim + 2 * kv_dim if interleaved else q_dim
+        qin = np.full(stride, -123.0, np.float16)
+        qin[:q_dim] = g["q_rope"][p]
+        out = np.full(3 * q_dim, -123.0, np.float16)
+        dout = dev(out)
+        po, pm, pl = _workspace(H, p + 1, d)
+        b200attn.launch_causal_attention_decode(dev(qin), dk, dv, dout[q_dim:], po, pm, pl, 1, p + 1, p, H, KVH, d,
+                                                stride if interleaved else 0, 0)
+        _sync()
+        res = host(dout)
+        got = res[q_dim:2 * q_dim]
+        assert tensor_close_mismatches(got, g["attn"][p], 2e-2, 2e-2) == 0, p
+        np.testing.assert_array_equal(bits(res[:q_dim]), bits(out[:q_dim]))
+        np.testing.assert_array_equal(bits(res[2 * q_dim:]), bits(out[2 * q_dim:]))
+        _, o32 = oracle.decode_attention(g["q_rope"][p], g["k_rope"], g["v"], p + 1, H, KVH, d)
+        assert_attention_close(got, o32.reshape(-1))
+
+
+def test_decode_partials_match_oracle(cuda):
+    """The workspace holds the reference's partial semantics: o [H][chunks][d],
+    m (natural log units) and l [H][chunks]."""
+    H, KVH, d, L = 16, 4, 128, 1000
+    q = seeded_f16(H * d, 1)
+    k = seeded_f16((L, KVH * d), 2)
+    v = seeded_f16((L, KVH * d), 3)
+    _, _, (po, pm, pl) = _decode(ENTRIES["decode"], q, k, v, L, H, KVH, d, 0)
+    ro, rm, rl = oracle.decode_partials(q, k, v, L, H, KVH, d, 0, CHUNK)
+    chunks = ro.shape[1]
+    gm, gl = host(pm).reshape(H, chunks), host(pl).reshape(H, chunks)
+    go = host(po).reshape(H, chunks, d)
+    np.testing.assert_allclose(gm, rm, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(gl, rl, rtol=1e-3, atol=1e-4)
+    np.testing.assert_allclose(go, ro, rtol=1e-2, atol=2e-3 * np.abs(ro).max())
+
+
+def test_config2_append_then_decode(cuda):
+    """cache 4096 tokens ~N(0,1), the new token RoPE'd at 4096 and
+    appended, kv_len 4097, chunk 256 (17 chunks) + merge -- against the oracle."""
+    import torch
+    H, KVH, d, past = 16, 4, 128, 4096
+    total = H * d + 2 * KVH * d
+    cos, sin = b200attn.rope_tables_host(past + 64, d, 5.0e6)
+    cache = b200attn.KVCache(1, past + 64, KVH, d, device=cuda)
+    hist_k = seeded_f16((past, KVH * d), 11)
+    hist_v = seeded_f16((past, KVH * d), 12)
+    cache.get_k_cache(0)[:past] = dev(hist_k)
+    cache.get_v_cache(0)[:past] = dev(hist_v)
+    qkv = seeded_f16((1, total), 13)
+    dqkv = dev(qkv)
+    b200attn.launch_rope_and_store_kv(dqkv, dqkv[:, H * d:], dqkv[:, H * d + KVH * d:], cache.get_k_cache(0),
+                                      cache.get_v_cache(0), dev(cos), dev(sin), 1, H, KVH, d, total, total, past, True)
+    ws = torch.empty(b200attn.decode_workspace_floats(H, d, past + 64), dtype=torch.float32, device=cuda)
+    chunks = (past + 1 + 255) // 256
+    po, pm, pl = ws[:H * chunks * d], ws[H * chunks * d:H * chunks * (d + 1)], ws[H * chunks * (d + 1):]
+    out = torch.empty(H * d, dtype=torch.float16, device=cuda)
+    b200attn.launch_causal_attention_decode_vectorized(dqkv, cache.get_k_cache(0), cache.get_v_cache(0), out, po, pm,
+                                                       pl, 1, past + 1, past, H, KVH, d, total, KVH * d)
+    _sync()
+    # oracle: same append, then attention over 4097 tokens
+    oq, ok = qkv[0, :H * d].copy(), qkv[0, H * d:H * d + KVH * d].copy()
+    kc = np.zeros((past + 64, KVH * d), np.float16)
+    vc = kc.copy()
+    kc[:past], vc[:past] = hist_k, hist_v
+    oracle.rope_and_store_kv(oq, ok, np.ascontiguousarray(qkv[0, H * d + KVH * d:]), kc, vc, cos, sin, 1, H, KVH, d,
+                             H * d, KVH * d, past, True)
+    np.testing.assert_array_equal(bits(host(cache.get_k_cache(0))[:past + 1]), bits(kc[:past + 1]))
+    np.testing.assert_array_equal(bits(host(dqkv)[0, :H * d]), bits(oq))
+    _, o32 = oracle.decode_attention(oq, kc, vc, past + 1, H, KVH, d)
+    assert_attention_close(host(out), o32.reshape(-1))
+
+
+@pytest.mark.parametrize("kv_len", [65536, 65536 + 63])
+def test_long_context_64k_one_layer(cuda, kv_len):
+    """BASELINE config 4 size: 64K cached tokens ~N(0, 0.5), one layer, vs the oracle."""
+    import torch
+    H, KVH, d = 16, 4, 128
+    k = seeded_f16((kv_len, KVH * d), 21, std=0.5)
+    v = seeded_f16((kv_len, KVH * d), 22, std=0.5)
+    q = seeded_f16(H * d, 23, std=0.5)
+    got, guards, _ = _decode(ENTRIES["vectorized"], q, k, v, kv_len, H, KVH, d, 0)
+    assert np.all(guards == np.float16(-123.0))
+    _, o32 = oracle.decode_attention(q, k, v, kv_len, H, KVH, d)
+    assert_attention_close(got, o32.reshape(-1))
+
+
+def test_decode_group8_and_strided_cache(cuda):
+    """Group size 8 (all MMA columns live) and a cache row stride of 3072 (interleaved rows)."""
+    H, KVH, d, L = 16, 2, 128, 777
+    stride = 3072
+    q = seeded_f16(H * d, 31)
+    k = seeded_f16(L * stride, 32)
+    v = seeded_f16(L * stride, 33)
+    got, _, _ = _decode(ENTRIES["decode"], q, k, v, L, H, KVH, d, stride)
+    _, o32 = oracle.decode_attention(q, k, v, L, H, KVH, d, stride)
+    assert_attention_close(got, o32.reshape(-1))
+
+
+def test_merge_tiled_on_oracle_partials(cuda):
+    """launch_merge_attention_decode_tiled (kernels.hpp:157-166) on caller partials."""
+    import torch
+    H, d = 16, 128
+    for chunks in (1, 3, 17, 257, 1000):
+        rng = np.random.default_rng(chunks)
+        pm = rng.normal(0, 3, (H, chunks)).astype(np.float32)
+        pl = rng.uniform(0.5, 50, (H, chunks)).astype(np.float32)
+        po = rng.normal(0, 5, (H, chunks, d)).astype(np.float32)
+        out = torch.empty(H * d, dtype=torch.float16, device=cuda)
+        b200attn.launch_merge_attention_decode_tiled(dev(po), dev(pm), dev(pl), out, H, chunks, d)
+        _sync()
+        _, ref32 = oracle.merge_partials(po, pm, pl)
+        assert max_abs(host(out), ref32.reshape(-1)) <= 2e-3 * max(1.0, float(np.abs(ref32).max()))
+
+
+def test_decode_graph_capture_and_node_updates(cuda):
+    """include/model_inference.hpp:96-123: capture once at kv_len L0, then patch
+    kv_len with update_causal_attention_decode_node / update_merge_attention_decode_node
+    (causal_attention.hip.cpp:975-1026) and replay."""
+    import torch
+    H, KVH, d, max_len = 16, 4, 128, 2000
+    k = dev(seeded_f16((max_len, KVH * d), 41))
+    v = dev(seeded_f16((max_len, KVH * d), 42))
+    q = dev(seeded_f16(H * d, 43))
+    ws = torch.empty(b200attn.decode_workspace_floats(H, d, max_len), dtype=torch.float32, device=cuda)
+    cmax = (max_len + 255) // 256
+    po, pm, pl = ws[:H * cmax * d], ws[H * cmax * d:H * cmax * (d + 1)], ws[H * cmax * (d + 1):]
+    out = torch.zeros(H * d, dtype=torch.float16, device=cuda)
+    gph = Graph()
+    with gph:
+        an, mn = b200attn.launch_causal_attention_decode_vectorized(q, k, v, out, po, pm, pl, 1, 300, 299, H, KVH, d,
+                                                                    0, 0, stream=gph.stream, capture_nodes=True)
+    assert an and mn and an != mn
+    for kv_len in (300, 301, 512, 513, 1999, 7):
+        b200attn.update_causal_attention_decode_node(gph.exec_handle, an, kv_len)
+        b200attn.update_merge_attention_decode_node(gph.exec_handle, mn, kv_len)
+        gph.launch()
+        _, o32 = oracle.decode_attention(host(q), host(k), host(v), kv_len, H, KVH, d)
+        assert_attention_close(host(out), o32.reshape(-1))
+    # a node of another kind is rejected, not corrupted
+    with pytest.raises(b200attn.B2Error):
+        b200attn.update_merge_attention_decode_node(gph.exec_handle, an, 10)
+    gph.close()

@@ -1,0 +1,110 @@
+"""Causal GQA prefill on the GPU vs the CPU oracle and the golden vectors.
+Restates tests/test_causal_attention.cpp:15-78 and tests/test_qkv_gemm.cpp:87-117."""
+import numpy as np
+import pytest
+
+import b200attn
+import oracle
+from _gpu import bits, dev, host
+from _util import assert_attention_close, golden, seeded_f16, tensor_close_mismatches
+
+pytestmark = pytest.mark.gpu
+
+
+def _sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+def _prefill(q, k, v, S, H, KVH, d, q_stride=0, kv_stride=0, guard_rows=1):
+    """Run prefill with guard rows of -123 above and below the packed output."""
+    out = np.full(((S + 2 * guard_rows), H * d), -123.0, np.float16)
+    dout = dev(out)
+    b200attn.launch_causal_attention_prefill(dev(q), dev(k), dev(v), dout[guard_rows:], S, H, KVH, d, q_stride,
+                                             kv_stride)
+    _sync()
+    res = host(dout)
+    np.testing.assert_array_equal(bits(res[:guard_rows]), bits(out[:guard_rows]))
+    np.testing.assert_array_equal(bits(res[guard_rows + S:]), bits(out[guard_rows + S:]))
+    return res[guard_rows:guard_rows + S]
+
+
+def test_prefill_matches_golden_from_cache(cuda):
+    """K/V in a real KVCache (max_seq = S + 2, trailing rows 123), Q packed (:15-78)."""
+    meta, g = golden()
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    cache = b200attn.KVCache(1, S + 2, KVH, d, device=cuda)
+    cache.buffer.fill_(123.0)
+    cache.get_k_cache(0)[:S] = dev(g["k_rope"])
+    cache.get_v_cache(0)[:S] = dev(g["v"])
+    out = dev(np.zeros((S, H * d), np.float16))
+    b200attn.launch_causal_attention_prefill(dev(g["q_rope"]), cache.get_k_cache(0), cache.get_v_cache(0), out, S, H,
+                                             KVH, d, H * d, KVH * d)
+    _sync()
+    got = host(out)
+    assert tensor_close_mismatches(got, g["attn"], 2e-2, 2e-2) == 0
+    _, o32 = oracle.causal_attention(g["q_rope"], g["k_rope"], g["v"], S, H, KVH, d)
+    assert_attention_close(got, o32)
+
+
+def test_prefill_on_interleaved_qkv_rows(cuda):
+    """tests/test_qkv_gemm.cpp:87-117: RoPE then prefill straight on [Q|K|V] rows, stride 3072."""
+    meta, g = golden()
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    total = H * d + 2 * KVH * d
+    qkv = dev(np.concatenate([g["q"], g["k"], g["v"]], axis=1))
+    cos, sin = b200attn.rope_tables_host(4096, d, meta["rope_theta"])
+    b200attn.launch_rope(qkv, qkv[:, H * d:], dev(cos), dev(sin), S, H, KVH, d, total, total)
+    out = dev(np.zeros((S, H * d), np.float16))
+    b200attn.launch_causal_attention_prefill(qkv, qkv[:, H * d:], qkv[:, H * d + KVH * d:], out, S, H, KVH, d, total,
+                                             total)
+    _sync()
+    got = host(out)
+    assert tensor_close_mismatches(got, g["attn"], 2e-2, 2e-2) == 0
+    _, o32 = oracle.causal_attention(g["q_rope"], g["k_rope"], g["v"], S, H, KVH, d)
+    assert_attention_close(got, o32)
+
+
+@pytest.mark.parametrize("S", [1, 2, 17, 127, 128, 129, 254, 255, 256, 257, 300, 1000])
+def test_prefill_random_vs_oracle(cuda, S):
+    H, KVH, d = 16, 4, 128
+    q = seeded_f16((S, H * d), 100 + S)
+    k = seeded_f16((S, KVH * d), 200 + S)
+    v = seeded_f16((S, KVH * d), 300 + S)
+    got = _prefill(q, k, v, S, H, KVH, d)
+    _, o32 = oracle.causal_attention(q, k, v, S, H, KVH, d)
+    assert_attention_close(got, o32)
+
+
+@pytest.mark.parametrize("S", [2048, 4097])
+def test_prefill_long_sampled_rows(cuda, S):
+    """Longer sequences: every row is finite, sampled rows (incl. first/last/tile edges) match."""
+    H, KVH, d = 16, 4, 128
+    q = seeded_f16((S, H * d), 7 + S)
+    k = seeded_f16((S, KVH * d), 8 + S)
+    v = seeded_f16((S, KVH * d), 9 + S)
+    got = _prefill(q, k, v, S, H, KVH, d)
+    assert np.all(np.isfinite(got.astype(np.float32)))
+    rng = np.random.default_rng(S)
+    rows = sorted(set([0, 1, 127, 128, 129, S // 2, S - 129, S - 128, S - 2, S - 1] +
+                      list(rng.integers(0, S, 40))))
+    _, o32 = oracle.causal_attention(q, k, v, S, H, KVH, d, rows=rows)
+    assert_attention_close(got[rows], o32)
+
+
+@pytest.mark.parametrize("shape", [
+    # (S, H, KVH, d, q_pad, kv_pad): SIMT path shapes
+    (37, 4, 2, 32, 0, 0),
+    (65, 8, 1, 64, 3, 5),
+    (40, 16, 4, 128, 1, 17),
+    (33, 6, 3, 96, 0, 0),
+])
+def test_prefill_other_shapes_vs_oracle(cuda, shape):
+    S, H, KVH, d, qp, kp = shape
+    qs, ks = H * d + qp, KVH * d + kp
+    q = seeded_f16(S * qs, 1 + S)
+    k = seeded_f16(S * ks, 2 + S)
+    v = seeded_f16(S * ks, 3 + S)
+    got = _prefill(q, k, v, S, H, KVH, d, qs, ks)
+    _, o32 = oracle.causal_attention(q, k, v, S, H, KVH, d, qs, ks)
+    assert_attention_close(got, o32)

@@ -1,0 +1,369 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 GQA attention hot path.
+
+Workload (long-context decode): batch 1, a 65,536-token
+FP16 KV cache ~N(0, 0.5) per layer, 16 query / 4 KV heads, head_dim 128,
+36 layers. One step = one generated token through all 36 layers: per layer
+RoPE of the new token (NoPE on every 4th layer) + KV-cache append at
+position 65,536 + step, split-KV flash-decode over kv_len = position + 1
+(KV_CHUNK 256) and the partial merge.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+value : whole-job KV-read throughput in GB/s with the inputs resident in HBM;
+        one captured CUDA graph per step (device-resident positions), CUDA
+        events on the launching stream, max over ranks.
+e2e   : the same metric through the reference-facing C-ABI calls
+        (launch_rope_and_store_kv + launch_causal_attention_decode_vectorized
+        per layer) with the step's Q/K/V rows copied from pinned host memory
+        and the attention outputs copied back every step.
+Algorithmic bytes per layer-step: K+V read 2*kv_len*512*2 + Q 4 KiB +
+output 4 KiB + appended K/V row 2 KiB (partial-workspace traffic excluded).
+
+--impl reference times the reference algorithm's CPU implementation (the
+C oracle restating it, all host threads) on a bounded sample of the same
+workload (one layer-step at the same kv_len per step) and prints the same line.
+
+N > 1 (torchrun): the 64K KV range of every layer is split into N contiguous
+ranges, one per rank; the rank holding the tail appends the new token; each
+rank reduces its range to one (o, m, l) partial per head, the partials are
+all-gathered over NCCL and merged on every rank (strong scaling: total work
+fixed).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "llm-inference_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+H, KVH, D, LAYERS, PAST = 16, 4, 128, 36, 65536
+KV_DIM = KVH * D
+Q_DIM = H * D
+QKV = Q_DIM + 2 * KV_DIM
+SEED = 2024
+METRIC = "GQA attn: decode KV-read HBM GB/s, prefill TFLOP/s, % B200 roofline @1-8 GPU"
+WORKLOAD = ("config4: long-context decode, batch 1, KV 65536 tokens ~N(0,0.5) FP16, 16/4 heads, head_dim 128, "
+            "36 layers x 1 token per step (RoPE+append+split-KV decode+merge), KV_CHUNK 256")
+
+
+def layer_bytes(kv_len: int) -> int:
+    return 2 * kv_len * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + 2 * KV_DIM * 2
+
+
+def step_bytes(kv_len: int) -> int:
+    return LAYERS * layer_bytes(kv_len)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons during the timed region."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, interval: float = 0.01):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.interval = interval
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            p = torch.cuda.get_device_properties(device_index)
+            try:  # NVML numbers all GPUs; match the CUDA device by PCI address
+                bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.reason_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.ok = True
+        except Exception as e:  # NVML absent: report no clocks rather than fail the bench
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = self.reason_fn(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+        return False
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": len(self.samples)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_decode_sample(kv_len: int, threads: int, rng_seed: int = 7, budget_s: float = 12.0, min_reps: int = 2):
+    """Oracle RoPE+append + decode attention for one layer-step at kv_len, repeated
+    until budget_s; returns (GB/s, reps, seconds)."""
+    import numpy as np
+    import oracle
+    rng = np.random.default_rng(rng_seed)
+    k = (rng.standard_normal((kv_len, KV_DIM), dtype=np.float32) * 0.5).astype(np.float16)
+    v = (rng.standard_normal((kv_len, KV_DIM), dtype=np.float32) * 0.5).astype(np.float16)
+    qkv = rng.standard_normal(QKV, dtype=np.float32).astype(np.float16)
+    cos, sin = oracle.rope_tables(kv_len, D, 5.0e6)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        q = qkv[:Q_DIM].copy()
+        kn = qkv[Q_DIM:Q_DIM + KV_DIM].copy()
+        vn = qkv[Q_DIM + KV_DIM:].copy()
+        oracle.rope_and_store_kv(q, kn, vn, k, v, cos, sin, 1, H, KVH, D, Q_DIM, KV_DIM, kv_len - 1, True)
+        oracle.decode_attention(q, k, v, kv_len, H, KVH, D, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if reps >= min_reps and el >= budget_s:
+            break
+    return layer_bytes(kv_len) * reps / el / 1e9, reps, el
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference algorithm's CPU implementation (C oracle)."""
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+    threads = os.cpu_count() or 1
+    kv_len = PAST + 1
+    rng = np.random.default_rng(7)
+    k = (rng.standard_normal((kv_len + args.warmup + args.steps, KV_DIM), dtype=np.float32) * 0.5).astype(np.float16)
+    v = (rng.standard_normal(k.shape, dtype=np.float32) * 0.5).astype(np.float16)
+    qkv = rng.standard_normal(QKV, dtype=np.float32).astype(np.float16)
+    cos, sin = oracle.rope_tables(k.shape[0], D, 5.0e6)
+
+    def one(step):
+        pos = PAST + step
+        q = qkv[:Q_DIM].copy()
+        kn = qkv[Q_DIM:Q_DIM + KV_DIM].copy()
+        vn = qkv[Q_DIM + KV_DIM:].copy()
+        oracle.rope_and_store_kv(q, kn, vn, k, v, cos, sin, 1, H, KVH, D, Q_DIM, KV_DIM, pos, (step + 1) % 4 != 0)
+        oracle.decode_attention(q, k, v, pos + 1, H, KVH, D, threads=threads)
+        return layer_bytes(pos + 1)
+
+    for s in range(args.warmup):
+        one(s)
+    total, t0 = 0, time.perf_counter()
+    for s in range(args.steps):
+        total += one(s)
+    el = time.perf_counter() - t0
+    val = total / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, f64 accumulate",
+        "data": "synthetic (seeded numpy), KV ~N(0,0.5)",
+        "config": {"workload": WORKLOAD, "sample": "one layer-step per step (RoPE+append+decode at kv_len "
+                   "65537+step) instead of 36 layers", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} layer-steps of the 64K decode, C oracle, {threads} OpenMP threads"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def run_b200(args, rank, world):
+    import numpy as np
+    import torch
+    import b200attn
+    from b200attn import dist as bdist
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    plan = bdist.split_kv_plan(PAST, world, rank)
+    capacity = plan.local_capacity(args.warmup + args.steps + 1)   # local cache rows
+    max_global = PAST + args.warmup + args.steps + 1
+
+    # ---- state: KV cache (local slice), RoPE tables, per-layer QKV rows, outputs
+    gen = torch.Generator(device=dev).manual_seed(SEED + rank)
+    cache = b200attn.KVCache(LAYERS, capacity, KVH, D, device=dev)
+    for l in range(LAYERS):
+        for t in (cache.get_k_cache(l), cache.get_v_cache(l)):
+            t.normal_(0.0, 0.5, generator=gen)
+    cos, sin = b200attn.rope_tables_host(max_global, D, 5.0e6)
+    d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    hgen = np.random.default_rng(SEED)     # identical Q/K/V rows on every rank
+    qkv_host = torch.from_numpy(hgen.standard_normal((LAYERS, QKV), dtype=np.float32).astype(np.float16)).pin_memory()
+    qkv = qkv_host.to(dev)
+    out = torch.zeros((LAYERS, Q_DIM), dtype=torch.float16, device=dev)
+    out_host = torch.zeros_like(out, device="cpu").pin_memory()
+    step_state = bdist.DecodeStepState(plan, H, KVH, D, LAYERS, capacity, max_global, dev)
+
+    stream = torch.cuda.Stream(device=dev)
+    group = None
+    if world > 1:
+        import torch.distributed as tdist
+        group = tdist.group.WORLD
+
+    def enqueue_step(s):
+        bdist.enqueue_decode_step(step_state, cache, qkv, out, d_cos, d_sin, s, group)
+
+    # ---- capture one step as a CUDA graph (device-resident positions)
+    step_state.reset_position(PAST)
+    with torch.cuda.stream(stream):
+        enqueue_step(stream)         # eager warm-up of every launch (and NCCL) once
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = b200attn.kernel_launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        enqueue_step(torch.cuda.current_stream())
+    launches_per_step = b200attn.kernel_launch_count() - n0
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as tdist
+            tdist.barrier()
+
+    # ---- value: graph replays, inputs resident
+    # graph.replay() launches on the current stream: make it `stream` and time there
+    step_state.reset_position(PAST)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    step_state.reset_position(PAST)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks, torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    ms = bdist.max_over_ranks(ms, dev) if world > 1 else ms
+    total_bytes = sum(step_bytes(PAST + 1 + s) for s in range(args.steps))
+    value = total_bytes / (ms / 1e3) / 1e9
+
+    # ---- roofline: decode (split + merge) per layer, CUDA events on its stream
+    peak, peak_kind = load_peaks()
+    dec_ms = bdist.time_decode_launches(step_state, cache, qkv, out, stream, reps=3)
+    kv_len_local = plan.local_len(PAST + 1)
+    dec_bytes = 2 * kv_len_local * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2
+    achieved = dec_bytes / (dec_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+
+    # ---- e2e: reference-facing C-ABI calls, host buffers in and out every step
+    e2e = None
+    if world == 1:
+        e2e = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup, args.steps,
+                               stream, step_state)
+
+    # ---- CPU baseline (rank 0, N=1): bounded sample
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        gbs, reps, el = cpu_decode_sample(PAST + 1, threads)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{reps} layer-steps of the 64K decode (RoPE+append+attention) in {el:.1f} s, "
+                         f"C oracle, {threads} OpenMP threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
+            "data": "synthetic: KV ~N(0,0.5) (torch CUDA generator, seed 2024+rank), Q/K/V rows ~N(0,1) seeded",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": PAST, "layers": LAYERS,
+                       "parallelism": f"kv-split{world}" if world > 1 else "single-gpu",
+                       "l2": "inputs larger than L2 (4.8 GB of KV per step)",
+                       "step_graph": f"one CUDA graph per step, {launches_per_step} kernels"},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "decode_split_mma_kernel + merge_partials_kernel",
+                         "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "avg_launch_us": round(dec_ms * 1e3, 3),
+                         "algorithmic_bytes_per_launch": dec_bytes},
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    graph.reset()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_b200(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as tdist
+            tdist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -62,6 +62,10 @@ size_t b2_decode_workspace_floats(size_t num_heads, size_t head_dim, size_t max_
 const char* b2_status_string(int status);
 int b2_last_cuda_error(void);            /* cudaError_t of the last B2_ERR_CUDA */
 uint64_t b2_kernel_launch_count(void);   /* kernels this library has launched */
+/* OR of the device-side error bits on the current device: bit 0 = a bounded
+ * wait inside a kernel (TMA copy / pipeline barrier) ran out of time and the
+ * kernel stopped early. 0 when every kernel completed normally. */
+unsigned int b2_device_error_word(void);
 
 /* Host-side RoPE tables, include/rope_cache.hpp:49-76 (compute_inverse_frequencies,
  * fill_host_tables): cos/sin[pos][i] = fp16(cos/sin(float(pos) * inv_freq[i])),
@@ -169,6 +173,74 @@ int b2_launch_merge_attention_decode_tiled(const float* d_partial_output,
                                            void* d_out, size_t num_heads,
                                            size_t num_kv_chunks, size_t head_dim,
                                            b2_stream_t stream);
+
+/* ---- Graph-static decode step (no per-step node patching) ----------------
+ * The reference captures its decode step into a HIP graph once and patches
+ * 3 kernel nodes per layer before every token
+ * (include/model_inference.hpp:96-123). These variants read the position
+ * from device memory instead, so one captured graph serves every step; the
+ * caller advances the device position (b2_advance_position) inside the graph
+ * or between launches. Results equal the host-length launchers. */
+
+/* b2_launch_rope_and_store_kv with start_pos = d_start_pos[0] read at launch.
+ * Tokens whose position start_pos + t >= max_seq_len are skipped (no table
+ * read, no cache write); a negative position skips the launch's work. */
+int b2_launch_rope_and_store_kv_devpos(void* d_q, void* d_k, const void* d_v,
+                                       void* d_k_cache, void* d_v_cache,
+                                       const void* d_cos, const void* d_sin,
+                                       size_t seq_len, size_t num_heads, size_t num_kv_heads,
+                                       size_t head_dim, size_t q_stride, size_t k_stride,
+                                       const int32_t* d_start_pos, size_t max_seq_len,
+                                       bool apply_rotation, b2_stream_t stream);
+
+/* b2_launch_causal_attention_decode with kv_len = clamp(d_kv_len[0] +
+ * kv_len_bias, 0, max_kv_len) read at launch (bias 1 turns a start_pos into
+ * the decode length, include/model_inference.hpp:382). The partial workspace
+ * is laid out for max_kv_len: [H][ceil(max_kv_len/KV_CHUNK)][d] etc., i.e.
+ * b2_decode_workspace_floats(H, d, max_kv_len) floats in the reference's
+ * three arrays. kv_len 0 writes a zero output. */
+int b2_launch_causal_attention_decode_devlen(const void* d_q, const void* d_k_cache,
+                                             const void* d_v_cache, void* d_out,
+                                             float* d_partial_out, float* d_partial_max,
+                                             float* d_partial_weight_sum,
+                                             const int32_t* d_kv_len, int32_t kv_len_bias,
+                                             size_t max_kv_len, size_t num_heads,
+                                             size_t num_kv_heads, size_t head_dim,
+                                             size_t kv_stride, b2_stream_t stream);
+
+/* ---- KV-split decode across GPUs (one rank per GPU) ----------------------
+ * Each rank attends over its own contiguous range of the cache and reduces
+ * it to one partial per head; the partials of all ranks are exchanged (e.g.
+ * an NCCL all-gather) and merged with b2_launch_merge_partials_strided. The
+ * algebra is the reference's chunk merge (src/kernels/causal_attention.hip.cpp
+ * :719-819) applied once more, with ranks as chunks. */
+
+/* b2_launch_causal_attention_decode_devlen over this rank's range, whose
+ * merge writes the rank partial instead of an fp16 output:
+ * d_rank_o[h*head_dim + e] = sum_c e^(m_c - M) o_c[e] (fp32, unnormalised),
+ * d_rank_m[h] = M = max_c m_c (natural-log units), d_rank_l[h] =
+ * sum_c e^(m_c - M) l_c. An empty range gives M = -inf, L = 0, o = 0. */
+int b2_launch_decode_rank_partial_devlen(const void* d_q, const void* d_k_cache,
+                                         const void* d_v_cache, float* d_partial_out,
+                                         float* d_partial_max, float* d_partial_weight_sum,
+                                         const int32_t* d_kv_len, int32_t kv_len_bias,
+                                         size_t max_kv_len, size_t num_heads,
+                                         size_t num_kv_heads, size_t head_dim, size_t kv_stride,
+                                         float* d_rank_o, float* d_rank_m, float* d_rank_l,
+                                         b2_stream_t stream);
+
+/* Merge num_chunks partials per head with arbitrary strides (in floats):
+ * o of (chunk c, head h) at d_o + c*o_chunk_stride + h*o_head_stride, m and l
+ * at d_m / d_l + c*ml_chunk_stride + h*ml_head_stride. Writes d_out [H][d]
+ * fp16. With strides (d, chunks*d, 1, chunks) this is the reference merge. */
+int b2_launch_merge_partials_strided(const float* d_o, const float* d_m, const float* d_l,
+                                     void* d_out, size_t num_heads, size_t num_chunks,
+                                     size_t head_dim, size_t o_chunk_stride,
+                                     size_t o_head_stride, size_t ml_chunk_stride,
+                                     size_t ml_head_stride, b2_stream_t stream);
+
+/* d_pos[0] += delta on the stream (one thread), for device-resident positions. */
+int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream);
 
 #ifdef __cplusplus
 }

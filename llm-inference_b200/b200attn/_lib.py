@@ -30,6 +30,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_status_string": (ctypes.c_char_p, [I]),
     "b2_last_cuda_error": (I, []),
     "b2_kernel_launch_count": (U64, []),
+    "b2_device_error_word": (ctypes.c_uint, []),
     "b2_fill_rope_tables": (I, [S, S, F, P, P]),
     "b2_launch_rope": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
     "b2_launch_rope_and_store_kv": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, S, B, P]),
@@ -40,6 +41,11 @@ SIGNATURES: dict[str, tuple] = {
     "b2_update_causal_attention_decode_node": (I, [P, P, S]),
     "b2_update_merge_attention_decode_node": (I, [P, P, S]),
     "b2_launch_merge_attention_decode_tiled": (I, [P, P, P, P, S, S, S, P]),
+    "b2_launch_rope_and_store_kv_devpos": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, P, S, B, P]),
+    "b2_launch_causal_attention_decode_devlen": (I, [P, P, P, P, P, P, P, P, ctypes.c_int32, S, S, S, S, S, P]),
+    "b2_advance_position": (I, [P, ctypes.c_int32, P]),
+    "b2_launch_decode_rank_partial_devlen": (I, [P, P, P, P, P, P, P, ctypes.c_int32, S, S, S, S, S, P, P, P, P]),
+    "b2_launch_merge_partials_strided": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
 }
 
 

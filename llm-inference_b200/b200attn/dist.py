@@ -1,0 +1,250 @@
+"""Work partitioning across GPUs and the decode-step driver.
+
+The reference engine is single-GPU (include/model_inference.hpp). Across the
+GPUs of one box the attention path shards where it naturally does:
+
+* long-context decode -- the KV sequence of every layer is split into
+  contiguous ranges, one per rank (`split_kv_plan`); the rank that holds the
+  tail appends the new token; every rank reduces its range to one (o, m, l)
+  partial per head, the partials are all-gathered (NCCL) and merged with the
+  reference's chunk-merge algebra;
+* batched prefill -- independent (sequence, KV head) units (`prefill_units`);
+* ragged decode -- whole sequences, longest first (`assign_sequences`).
+
+The partition functions are pure host logic; `enqueue_decode_step` issues one
+decode step (all layers) on a stream so it can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+H_DEFAULT = 16
+
+
+@dataclasses.dataclass(frozen=True)
+class SplitPlan:
+    """Rank `rank` of `world` owns global KV rows [begin, end) of the first
+    `past` tokens; the last rank also owns every appended token."""
+    past: int
+    world: int
+    rank: int
+    begin: int
+    end: int
+
+    @property
+    def is_tail(self) -> bool:
+        return self.rank == self.world - 1
+
+    @property
+    def local_past(self) -> int:
+        return self.end - self.begin
+
+    def local_capacity(self, extra: int) -> int:
+        """Rows this rank's cache needs for `extra` appended tokens."""
+        return self.local_past + (extra if self.is_tail else 0)
+
+    def local_len(self, global_len: int) -> int:
+        """Rows of this rank's range inside a cache of global_len tokens."""
+        return max(0, min(global_len, self.end if not self.is_tail else global_len) - self.begin)
+
+
+def split_kv_plan(past: int, world: int, rank: int) -> SplitPlan:
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, rem = divmod(past, world)
+    begin = rank * base + min(rank, rem)
+    end = begin + base + (1 if rank < rem else 0)
+    return SplitPlan(past, world, rank, begin, end)
+
+
+def prefill_units(batch: int, num_kv_heads: int, world: int, rank: int) -> list[tuple[int, int]]:
+    """(sequence, kv_head) units of a batched causal prefill owned by `rank`.
+    Every unit has the same causal work, so a round-robin split balances."""
+    units = [(b, h) for b in range(batch) for h in range(num_kv_heads)]
+    return units[rank::world]
+
+
+def assign_sequences(kv_lens, world: int) -> list[list[int]]:
+    """Greedy longest-first assignment of ragged sequences to ranks, balancing
+    the total KV length (the decode cost) per rank."""
+    order = sorted(range(len(kv_lens)), key=lambda i: (-int(kv_lens[i]), i))
+    loads = [0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda j: (loads[j], j))
+        out[r].append(i)
+        loads[r] += int(kv_lens[i])
+    return [sorted(x) for x in out]
+
+
+def merge_rank_partials_reference(parts):
+    """Host restatement of the cross-rank merge for CPU tests: parts is a list of
+    (o [H][d], m [H], l [H]) numpy arrays; returns out [H][d] float64."""
+    import numpy as np
+    o = np.stack([p[0] for p in parts]).astype(np.float64)
+    m = np.stack([p[1] for p in parts]).astype(np.float64)
+    l = np.stack([p[2] for p in parts]).astype(np.float64)
+    M = m.max(axis=0)
+    w = np.exp(m - M)
+    return (w[:, :, None] * o).sum(axis=0) / (w * l).sum(axis=0)[:, None]
+
+
+# ---------------------------------------------------------------------------
+# Decode step driver (GPU). Imported lazily so the partition logic above has
+# no torch / CUDA dependency.
+
+class DecodeStepState:
+    """Device-resident positions and workspaces for a graph-static decode step."""
+
+    def __init__(self, plan: SplitPlan, num_heads, num_kv_heads, head_dim, num_layers, capacity, max_global,
+                 device):
+        import torch
+        from . import kernels as K
+        self.plan = plan
+        self.H, self.KVH, self.D, self.L = num_heads, num_kv_heads, head_dim, num_layers
+        self.capacity = capacity
+        self.max_global = max_global
+        self.device = device
+        # global position of the token being decoded (start_pos); kv_len = pos + 1
+        self.pos = torch.zeros(1, dtype=torch.int32, device=device)
+        self.local_const = torch.tensor([plan.local_past], dtype=torch.int32, device=device)
+        nfl = K.decode_workspace_floats(num_heads, head_dim, capacity)
+        self.ws = torch.empty(nfl, dtype=torch.float32, device=device)
+        chunks = (capacity + K._kv_chunk() - 1) // K._kv_chunk()
+        n = num_heads * chunks
+        self.po, self.pm, self.pl = self.ws[:n * head_dim], self.ws[n * head_dim:n * (head_dim + 1)], \
+            self.ws[n * (head_dim + 1):]
+        w = plan.world
+        per = num_heads * (head_dim + 2)
+        self.rank_part = torch.zeros((num_layers, per), dtype=torch.float32, device=device)
+        self.gathered = torch.zeros((num_layers, w * per), dtype=torch.float32, device=device)
+
+    def reset_position(self, pos: int):
+        self.pos.fill_(pos)
+
+    def kv_len_source(self):
+        """(device int, bias) giving this rank's local kv_len for the step."""
+        if self.plan.is_tail:
+            return self.pos, 1 - self.plan.begin
+        return self.local_const, 0
+
+
+def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stream, group=None):
+    """One token through every layer: RoPE + append (tail rank), decode over the
+    local KV range, exchange + merge across ranks, then advance the position."""
+    import torch
+    from . import kernels as K
+    H, KVH, D = st.H, st.KVH, st.D
+    q_dim, kv_dim = H * D, KVH * D
+    total = q_dim + 2 * kv_dim
+    plan = st.plan
+    src, bias = st.kv_len_source()
+    for l in range(st.L):
+        rotate = (l + 1) % 4 != 0          # include/model_inference.hpp:272 NoPE rule
+        row = qkv[l]
+        q, k, v = row, row[q_dim:], row[q_dim + kv_dim:]
+        if plan.is_tail:
+            # cache rows are local: global position p lives at local row p - begin
+            kc = cache.get_k_cache(l)
+            vc = cache.get_v_cache(l)
+            off = plan.begin * kv_dim * 2
+            K.launch_rope_and_store_kv_devpos(q, k, v, kc.data_ptr() - off, vc.data_ptr() - off, d_cos, d_sin, 1,
+                                              H, KVH, D, total, total, st.pos, plan.begin + st.capacity, rotate,
+                                              stream=stream)
+        elif rotate:
+            # only Q needs rotating on ranks that do not store the new token
+            K.launch_rope_and_store_kv_devpos(q, q, None, None, None, d_cos, d_sin, 1, H, 0, D, total, total,
+                                              st.pos, st.max_global, True, stream=stream)
+        if plan.world == 1:
+            K.launch_causal_attention_decode_devlen(q, cache.get_k_cache(l), cache.get_v_cache(l), out[l], st.po,
+                                                    st.pm, st.pl, src, bias, st.capacity, H, KVH, D, kv_dim,
+                                                    stream=stream)
+        else:
+            part = st.rank_part[l]
+            K.launch_decode_rank_partial_devlen(q, cache.get_k_cache(l), cache.get_v_cache(l), st.po, st.pm, st.pl,
+                                                src, bias, st.capacity, H, KVH, D, kv_dim, part[:H * D],
+                                                part[H * D:H * D + H], part[H * D + H:], stream=stream)
+            import torch.distributed as tdist
+            with torch.cuda.stream(stream if isinstance(stream, torch.cuda.Stream) else torch.cuda.current_stream()):
+                tdist.all_gather_into_tensor(st.gathered[l], part, group=group)
+            per = H * (D + 2)
+            g = st.gathered[l]
+            K.launch_merge_partials_strided(g, g[H * D:], g[H * D + H:], out[l], H, plan.world, D, per, D, per, 1,
+                                            stream=stream)
+    K.advance_position(st.pos, 1, stream=stream)
+
+
+def max_over_ranks(value: float, device) -> float:
+    import torch
+    import torch.distributed as tdist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3) -> float:
+    """Average device time (ms) of one decode launch (split + merge) over the
+    local range at kv_len = past + 1, measured with CUDA events on its stream,
+    cycling through the layers so the cache is not L2-resident."""
+    import torch
+    from . import kernels as K
+    H, KVH, D = st.H, st.KVH, st.D
+    src, bias = st.kv_len_source()
+    st.reset_position(st.plan.past)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps * st.L)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps * st.L)]
+    i = 0
+    for _ in range(reps):
+        for l in range(st.L):
+            starts[i].record(stream)
+            K.launch_causal_attention_decode_devlen(qkv[l], cache.get_k_cache(l), cache.get_v_cache(l), out[l],
+                                                    st.po, st.pm, st.pl, src, bias, st.capacity, H, KVH, D,
+                                                    KVH * D, stream=stream)
+            ends[i].record(stream)
+            i += 1
+    torch.cuda.synchronize()
+    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    return sum(times) / len(times)
+
+
+def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, steps, stream, st) -> dict:
+    """The decode metric through the reference-facing C-ABI launchers
+    (launch_rope_and_store_kv + launch_causal_attention_decode_vectorized per
+    layer, host positions), with the step's Q/K/V rows copied in from pinned
+    host memory and the outputs copied back every step."""
+    import torch
+    from . import kernels as K
+    H, KVH, D, L = st.H, st.KVH, st.D, st.L
+    q_dim, kv_dim = H * D, KVH * D
+    total = q_dim + 2 * kv_dim
+
+    def step(s):
+        pos = past + s
+        qkv.copy_(qkv_host, non_blocking=True)
+        for l in range(L):
+            row = qkv[l]
+            K.launch_rope_and_store_kv(row, row[q_dim:], row[q_dim + kv_dim:], cache.get_k_cache(l),
+                                       cache.get_v_cache(l), d_cos, d_sin, 1, H, KVH, D, total, total, pos,
+                                       (l + 1) % 4 != 0, stream=stream)
+            K.launch_causal_attention_decode_vectorized(row, cache.get_k_cache(l), cache.get_v_cache(l), out[l],
+                                                        st.po, st.pm, st.pl, 1, pos + 1, pos, H, KVH, D, total,
+                                                        kv_dim, stream=stream)
+        out_host.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for s in range(warmup):
+            step(s)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s in range(steps):
+            step(s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    nbytes = sum(L * (2 * (past + 1 + s) * kv_dim * 2 + q_dim * 2 * 2 + 2 * kv_dim * 2) for s in range(steps))
+    return {"value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": int(qkv_host.numel() * 2), "d2h_bytes_per_step": int(out_host.numel() * 2),
+            "ms_per_step": round(ms / steps, 4), "path": "C-ABI launch_rope_and_store_kv + "
+            "launch_causal_attention_decode_vectorized per layer, host start_pos, pinned H2D/D2H each step"}

@@ -22,7 +22,9 @@ __all__ = [
     "launch_causal_attention_prefill", "launch_causal_attention_decode",
     "launch_causal_attention_decode_vectorized", "update_causal_attention_decode_node",
     "update_merge_attention_decode_node", "launch_merge_attention_decode_tiled",
-    "decode_workspace_floats", "kernel_launch_count",
+    "decode_workspace_floats", "kernel_launch_count", "launch_rope_and_store_kv_devpos",
+    "launch_causal_attention_decode_devlen", "advance_position", "launch_decode_rank_partial_devlen",
+    "launch_merge_partials_strided",
 ]
 
 
@@ -156,3 +158,51 @@ def launch_merge_attention_decode_tiled(d_partial_output, d_partial_max, d_parti
     check(lib().b2_launch_merge_attention_decode_tiled(
         _ptr(d_partial_output), _ptr(d_partial_max), _ptr(d_partial_weight_sum), _ptr(d_out),
         num_heads, num_kv_chunks, head_dim, _stream(stream)), "launch_merge_attention_decode_tiled")
+
+
+# ---- graph-static decode step (device-resident positions) -------------------
+
+def launch_rope_and_store_kv_devpos(d_q, d_k, d_v, d_k_cache, d_v_cache, d_cos, d_sin, seq_len, num_heads,
+                                    num_kv_heads, head_dim, q_stride, k_stride, d_start_pos, max_seq_len,
+                                    apply_rotation, stream=None):
+    """launch_rope_and_store_kv with start_pos read from d_start_pos[0] (int32) at launch."""
+    check(lib().b2_launch_rope_and_store_kv_devpos(
+        _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_cos), _ptr(d_sin),
+        seq_len, num_heads, num_kv_heads, head_dim, q_stride, k_stride, _ptr(d_start_pos), max_seq_len,
+        bool(apply_rotation), _stream(stream)), "launch_rope_and_store_kv_devpos")
+
+
+def launch_causal_attention_decode_devlen(d_q, d_k_cache, d_v_cache, d_out, d_partial_out, d_partial_max,
+                                          d_partial_weight_sum, d_kv_len, kv_len_bias, max_kv_len, num_heads,
+                                          num_kv_heads, head_dim, kv_stride=0, stream=None):
+    """Decode with kv_len = d_kv_len[0] + kv_len_bias (clamped to max_kv_len) read at launch."""
+    check(lib().b2_launch_causal_attention_decode_devlen(
+        _ptr(d_q), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_out), _ptr(d_partial_out), _ptr(d_partial_max),
+        _ptr(d_partial_weight_sum), _ptr(d_kv_len), int(kv_len_bias), max_kv_len, num_heads, num_kv_heads,
+        head_dim, kv_stride, _stream(stream)), "launch_causal_attention_decode_devlen")
+
+
+def advance_position(d_pos, delta=1, stream=None):
+    check(lib().b2_advance_position(_ptr(d_pos), int(delta), _stream(stream)), "advance_position")
+
+
+# ---- KV-split decode across ranks --------------------------------------------
+
+def launch_decode_rank_partial_devlen(d_q, d_k_cache, d_v_cache, d_partial_out, d_partial_max,
+                                      d_partial_weight_sum, d_kv_len, kv_len_bias, max_kv_len, num_heads,
+                                      num_kv_heads, head_dim, kv_stride, d_rank_o, d_rank_m, d_rank_l,
+                                      stream=None):
+    """Reduce this rank's KV range to one (o, m, l) partial per head (fp32)."""
+    check(lib().b2_launch_decode_rank_partial_devlen(
+        _ptr(d_q), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_partial_out), _ptr(d_partial_max),
+        _ptr(d_partial_weight_sum), _ptr(d_kv_len), int(kv_len_bias), max_kv_len, num_heads, num_kv_heads,
+        head_dim, kv_stride, _ptr(d_rank_o), _ptr(d_rank_m), _ptr(d_rank_l), _stream(stream)),
+        "launch_decode_rank_partial_devlen")
+
+
+def launch_merge_partials_strided(d_o, d_m, d_l, d_out, num_heads, num_chunks, head_dim, o_chunk_stride,
+                                  o_head_stride, ml_chunk_stride, ml_head_stride, stream=None):
+    """Merge partials with arbitrary (float) strides into d_out [H][d] fp16."""
+    check(lib().b2_launch_merge_partials_strided(
+        _ptr(d_o), _ptr(d_m), _ptr(d_l), _ptr(d_out), num_heads, num_chunks, head_dim, o_chunk_stride,
+        o_head_stride, ml_chunk_stride, ml_head_stride, _stream(stream)), "launch_merge_partials_strided")

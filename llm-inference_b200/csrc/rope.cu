@@ -46,7 +46,22 @@ struct RopeArgs {
     uint32_t lanes;      // work lanes per head row
     uint32_t slots;      // head slots per token
     uint32_t start_pos;  // patched by b2_update_rope_and_store_kv_node
+    // Graph-static variant: when set, start_pos is read from device memory at
+    // launch and tokens at positions >= max_seq_len are skipped.
+    const int32_t* start_pos_dev;
+    uint32_t max_seq_len;
 };
+
+__device__ __forceinline__ bool resolve_start(const RopeArgs& a, uint32_t& start) {
+    if (a.start_pos_dev == nullptr) {
+        start = a.start_pos;
+        return true;
+    }
+    const int32_t s = __ldg(a.start_pos_dev);
+    if (s < 0) return false;
+    start = static_cast<uint32_t>(s);
+    return true;
+}
 
 __device__ __forceinline__ void rot2(float x0, float x1, float c, float s, float& o0, float& o1) {
     o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
@@ -75,6 +90,8 @@ __device__ __forceinline__ void rot8(uint4& lo, uint4& hi, uint4 cv, uint4 sv) {
 
 // Vectorised rotate (+ store) kernel: lanes = half_dim / 8.
 __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) {
+    uint32_t start;
+    if (!resolve_start(a, start)) return;
     const uint64_t per_token = static_cast<uint64_t>(a.slots) * a.lanes;
     for (uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; id < a.total_items;
          id += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
@@ -82,7 +99,8 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
         const uint32_t r = static_cast<uint32_t>(id - t * per_token);
         const uint32_t slot = r / a.lanes;
         const uint32_t e = (r - slot * a.lanes) * 8;
-        const uint64_t pos = a.start_pos + t;
+        const uint64_t pos = static_cast<uint64_t>(start) + t;
+        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
         if (slot < a.num_heads + a.num_kv_heads) {
             __half* src;
             __half* dst;
@@ -115,6 +133,8 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
 
 // Scalar rotate (+ store) kernel: lanes = half_dim, any stride / alignment.
 __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a) {
+    uint32_t start;
+    if (!resolve_start(a, start)) return;
     const uint64_t per_token = static_cast<uint64_t>(a.slots) * a.lanes;
     for (uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; id < a.total_items;
          id += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
@@ -122,7 +142,8 @@ __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a
         const uint32_t r = static_cast<uint32_t>(id - t * per_token);
         const uint32_t slot = r / a.lanes;
         const uint32_t i = r - slot * a.lanes;
-        const uint64_t pos = a.start_pos + t;
+        const uint64_t pos = static_cast<uint64_t>(start) + t;
+        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
         if (slot < a.num_heads + a.num_kv_heads) {
             __half* src;
             __half* dst;
@@ -155,6 +176,8 @@ __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a
 // NoPE append: K and V rows copied verbatim. lanes = kv_dim / 8 (vec8) or
 // kv_dim (scalar); slots = 2 (K, V).
 __global__ void __launch_bounds__(256) kv_copy_vec8_kernel(const RopeArgs a) {
+    uint32_t start;
+    if (!resolve_start(a, start)) return;
     const uint64_t per_token = 2ull * a.lanes;
     for (uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; id < a.total_items;
          id += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
@@ -163,12 +186,16 @@ __global__ void __launch_bounds__(256) kv_copy_vec8_kernel(const RopeArgs a) {
         const bool is_v = r >= a.lanes;
         const uint32_t e = (is_v ? r - a.lanes : r) * 8;
         const __half* src = (is_v ? a.v : a.k) + t * a.k_stride + e;
-        __half* dst = (is_v ? a.v_cache : a.k_cache) + (a.start_pos + t) * a.kv_dim + e;
+        const uint64_t pos = static_cast<uint64_t>(start) + t;
+        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
+        __half* dst = (is_v ? a.v_cache : a.k_cache) + pos * a.kv_dim + e;
         *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
     }
 }
 
 __global__ void __launch_bounds__(256) kv_copy_scalar_kernel(const RopeArgs a) {
+    uint32_t start;
+    if (!resolve_start(a, start)) return;
     const uint64_t per_token = 2ull * a.lanes;
     for (uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; id < a.total_items;
          id += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
@@ -177,7 +204,9 @@ __global__ void __launch_bounds__(256) kv_copy_scalar_kernel(const RopeArgs a) {
         const bool is_v = r >= a.lanes;
         const uint32_t e = is_v ? r - a.lanes : r;
         const __half* src = (is_v ? a.v : a.k) + t * a.k_stride + e;
-        __half* dst = (is_v ? a.v_cache : a.k_cache) + (a.start_pos + t) * a.kv_dim + e;
+        const uint64_t pos = static_cast<uint64_t>(start) + t;
+        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
+        __half* dst = (is_v ? a.v_cache : a.k_cache) + pos * a.kv_dim + e;
         *dst = *src;
     }
 }
@@ -206,12 +235,13 @@ const void* const kCopyKernels[] = {
 
 using namespace b2;
 
-extern "C" int b2_launch_rope_and_store_kv(void* d_q, void* d_k, const void* d_v, void* d_k_cache,
-                                           void* d_v_cache, const void* d_cos, const void* d_sin,
-                                           size_t seq_len, size_t num_heads, size_t num_kv_heads,
-                                           size_t head_dim, size_t q_stride, size_t k_stride,
-                                           size_t start_pos, bool apply_rotation,
-                                           b2_stream_t stream_handle) {
+namespace b2 {
+namespace {
+
+int launch_rope_impl(void* d_q, void* d_k, const void* d_v, void* d_k_cache, void* d_v_cache, const void* d_cos,
+                     const void* d_sin, size_t seq_len, size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                     size_t q_stride, size_t k_stride, size_t start_pos, const int32_t* start_pos_dev,
+                     size_t max_seq_len, bool apply_rotation, b2_stream_t stream_handle) {
     if (seq_len == 0) return B2_NOTHING_TO_DO;  // rope.hip.cpp:156
     if (head_dim == 0 || (head_dim & 1) || d_k == nullptr) return B2_ERR_INVALID_ARG;
     if (num_kv_heads == 0 && num_heads == 0) return B2_NOTHING_TO_DO;
@@ -241,6 +271,8 @@ extern "C" int b2_launch_rope_and_store_kv(void* d_q, void* d_k, const void* d_v
     a.half_dim = static_cast<uint32_t>(head_dim / 2);
     a.kv_dim = static_cast<uint32_t>(kv_dim);
     a.start_pos = static_cast<uint32_t>(start_pos);
+    a.start_pos_dev = start_pos_dev;
+    a.max_seq_len = static_cast<uint32_t>(max_seq_len > 0xffffffffull ? 0xffffffffull : max_seq_len);
 
     const bool rows16 = (k_stride % 8 == 0) && aligned16(d_k) && (!store || (aligned16(d_v) &&
                         aligned16(d_k_cache) && aligned16(d_v_cache)));
@@ -270,6 +302,31 @@ extern "C" int b2_launch_rope_and_store_kv(void* d_q, void* d_k, const void* d_v
     else
         kv_copy_scalar_kernel<<<blocks, 256, 0, stream>>>(a);
     return launch_status();
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_launch_rope_and_store_kv(void* d_q, void* d_k, const void* d_v, void* d_k_cache,
+                                           void* d_v_cache, const void* d_cos, const void* d_sin,
+                                           size_t seq_len, size_t num_heads, size_t num_kv_heads,
+                                           size_t head_dim, size_t q_stride, size_t k_stride,
+                                           size_t start_pos, bool apply_rotation,
+                                           b2_stream_t stream_handle) {
+    return launch_rope_impl(d_q, d_k, d_v, d_k_cache, d_v_cache, d_cos, d_sin, seq_len, num_heads, num_kv_heads,
+                            head_dim, q_stride, k_stride, start_pos, nullptr, 0, apply_rotation, stream_handle);
+}
+
+extern "C" int b2_launch_rope_and_store_kv_devpos(void* d_q, void* d_k, const void* d_v, void* d_k_cache,
+                                                  void* d_v_cache, const void* d_cos, const void* d_sin,
+                                                  size_t seq_len, size_t num_heads, size_t num_kv_heads,
+                                                  size_t head_dim, size_t q_stride, size_t k_stride,
+                                                  const int32_t* d_start_pos, size_t max_seq_len,
+                                                  bool apply_rotation, b2_stream_t stream_handle) {
+    if (d_start_pos == nullptr || max_seq_len == 0) return B2_ERR_INVALID_ARG;
+    return launch_rope_impl(d_q, d_k, d_v, d_k_cache, d_v_cache, d_cos, d_sin, seq_len, num_heads, num_kv_heads,
+                            head_dim, q_stride, k_stride, 0, d_start_pos, max_seq_len, apply_rotation,
+                            stream_handle);
 }
 
 extern "C" int b2_launch_rope(void* d_q, void* d_k, const void* d_cos, const void* d_sin, size_t seq_len,

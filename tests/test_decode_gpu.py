@@ -92,21 +92,107 @@ def test_decode_matches_golden_prefill_rows(cuda, interleaved):
         assert_attention_close(got, o32.reshape(-1))
 
 
-def test_decode_partials_match_oracle(cuda):
-    """The workspace holds the reference's partial semantics: o [H][chunks][d],
-    m (natural log units) and l [H][chunks]."""
-    H, KVH, d, L = 16, 4, 128, 1000
+def _sm_count():
+    import torch
+    return torch.cuda.get_device_properties(0).multi_processor_count
+
+
+@pytest.mark.parametrize("L", [1000, 5000, 65536 + 17])
+@pytest.mark.parametrize("packed", [True, False])
+def test_decode_partials_match_oracle(cuda, L, packed):
+    """The workspace holds the reference's partial semantics, one (o, m, l) per
+    split: o [H][S][d] unnormalised, m (natural-log units) and l [H][S]. The
+    TMA path (packed rows) uses S = min(#SMs, chunks) ranges of a 16-token
+    multiple; the strided path uses KV_CHUNK chunks."""
+    H, KVH, d = 16, 4, 128
+    stride = KVH * d if packed else 3072
     q = seeded_f16(H * d, 1)
-    k = seeded_f16((L, KVH * d), 2)
-    v = seeded_f16((L, KVH * d), 3)
-    _, _, (po, pm, pl) = _decode(ENTRIES["decode"], q, k, v, L, H, KVH, d, 0)
-    ro, rm, rl = oracle.decode_partials(q, k, v, L, H, KVH, d, 0, CHUNK)
-    chunks = ro.shape[1]
-    gm, gl = host(pm).reshape(H, chunks), host(pl).reshape(H, chunks)
-    go = host(po).reshape(H, chunks, d)
-    np.testing.assert_allclose(gm, rm, rtol=1e-5, atol=1e-5)
-    np.testing.assert_allclose(gl, rl, rtol=1e-3, atol=1e-4)
-    np.testing.assert_allclose(go, ro, rtol=1e-2, atol=2e-3 * np.abs(ro).max())
+    k = seeded_f16(L * stride, 2)
+    v = seeded_f16(L * stride, 3)
+    _, _, (po, pm, pl) = _decode(ENTRIES["decode"], q, k, v, L, H, KVH, d, 0 if packed else stride)
+    chunks = (L + CHUNK - 1) // CHUNK
+    if packed:
+        S = min(_sm_count(), chunks)
+        per = -(-(-(-L // S)) // 16) * 16
+    else:
+        S, per = chunks, CHUNK
+    ro, rm, rl = oracle.decode_partials(q, k, v, L, H, KVH, d, stride, per)
+    n = ro.shape[1]
+    assert n <= S
+    gm = host(pm)[:H * S].reshape(H, S)
+    gl = host(pl)[:H * S].reshape(H, S)
+    go = host(po)[:H * S * d].reshape(H, S, d)
+    np.testing.assert_allclose(gm[:, :n], rm, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(gl[:, :n], rl, rtol=2e-3, atol=1e-4)
+    np.testing.assert_allclose(go[:, :n], ro, rtol=1e-2, atol=2e-3 * np.abs(ro).max())
+    assert np.all(gm[:, n:] == -np.inf) and np.all(gl[:, n:] == 0)
+
+
+def test_devlen_equals_host_length(cuda):
+    """Graph-static decode (kv_len read from device memory) == host-length decode."""
+    import torch
+    H, KVH, d, cap = 16, 4, 128, 3000
+    k = dev(seeded_f16((cap, KVH * d), 51))
+    v = dev(seeded_f16((cap, KVH * d), 52))
+    q = dev(seeded_f16(H * d, 53))
+    ws = torch.empty(b200attn.decode_workspace_floats(H, d, cap), dtype=torch.float32, device=cuda)
+    n = H * ((cap + 255) // 256)
+    po, pm, pl = ws[:n * d], ws[n * d:n * (d + 1)], ws[n * (d + 1):]
+    pos = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for kv_len in (1, 255, 256, 257, 1234, 2999, 3000):
+        a = torch.empty(H * d, dtype=torch.float16, device=cuda)
+        b = torch.empty_like(a)
+        b200attn.launch_causal_attention_decode(q, k, v, a, po, pm, pl, 1, kv_len, kv_len - 1, H, KVH, d, 0, 0)
+        pos.fill_(kv_len - 1)
+        b200attn.launch_causal_attention_decode_devlen(q, k, v, b, po, pm, pl, pos, 1, cap, H, KVH, d)
+        _sync()
+        np.testing.assert_array_equal(bits(host(a)), bits(host(b)))
+    # past capacity is clamped to max_kv_len
+    pos.fill_(cap + 50)
+    b200attn.launch_causal_attention_decode_devlen(q, k, v, b, po, pm, pl, pos, 1, cap, H, KVH, d)
+    _sync()
+    np.testing.assert_array_equal(bits(host(a)), bits(host(b)))
+    assert b200attn.lib().b2_device_error_word() == 0
+
+
+@pytest.mark.parametrize("ranks", [2, 3, 8])
+def test_rank_partials_and_strided_merge(cuda, ranks):
+    """KV-split decode as the multi-GPU path runs it, emulated on one GPU: every
+    'rank' reduces its contiguous range to one (o, m, l) per head, the partials
+    are concatenated like an all-gather and merged with the strided merge."""
+    import torch
+    from b200attn import dist as bdist
+    H, KVH, d, L = 16, 4, 128, 9000
+    kh = seeded_f16((L, KVH * d), 61, std=0.5)
+    vh = seeded_f16((L, KVH * d), 62, std=0.5)
+    qh = seeded_f16(H * d, 63, std=0.5)
+    q = dev(qh)
+    per = H * (d + 2)
+    gathered = torch.zeros(ranks * per, dtype=torch.float32, device=cuda)
+    for r in range(ranks):
+        plan = bdist.split_kv_plan(L, ranks, r)
+        kc = dev(kh[plan.begin:plan.end])
+        vc = dev(vh[plan.begin:plan.end])
+        n = plan.end - plan.begin
+        ws = torch.empty(b200attn.decode_workspace_floats(H, d, n), dtype=torch.float32, device=cuda)
+        c = H * ((n + 255) // 256)
+        ln = torch.tensor([n], dtype=torch.int32, device=cuda)
+        part = gathered[r * per:(r + 1) * per]
+        b200attn.launch_decode_rank_partial_devlen(q, kc, vc, ws[:c * d], ws[c * d:c * (d + 1)], ws[c * (d + 1):],
+                                                   ln, 0, n, H, KVH, d, KVH * d, part[:H * d], part[H * d:H * d + H],
+                                                   part[H * d + H:])
+        _sync()
+    out = torch.empty(H * d, dtype=torch.float16, device=cuda)
+    b200attn.launch_merge_partials_strided(gathered, gathered[H * d:], gathered[H * d + H:], out, H, ranks, d, per,
+                                           d, per, 1)
+    _sync()
+    _, o32 = oracle.decode_attention(qh, kh, vh, L, H, KVH, d)
+    assert_attention_close(host(out), o32.reshape(-1))
+    # the host restatement of the cross-rank merge agrees
+    g = host(gathered).reshape(ranks, per)
+    parts = [(g[r, :H * d].reshape(H, d), g[r, H * d:H * d + H], g[r, H * d + H:]) for r in range(ranks)]
+    ref = bdist.merge_rank_partials_reference(parts)
+    assert_attention_close(ref.reshape(-1), o32.reshape(-1))
 
 
 def test_config2_append_then_decode(cuda):

@@ -242,6 +242,36 @@ int b2_launch_merge_partials_strided(const float* d_o, const float* d_m, const f
 /* d_pos[0] += delta on the stream (one thread), for device-resident positions. */
 int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream);
 
+/* ---- Decode without a caller workspace ------------------------------------
+ * No counterpart in the reference (whose decode launchers always take the
+ * three partial arrays). For callers that cannot provide scratch memory: a
+ * plugin host that passes only inputs and outputs, a serving process whose
+ * memory pool owns all of HBM, a latency-critical thread that must not call
+ * cudaMalloc. Same contract and result as b2_launch_causal_attention_decode,
+ * but the split partials live in a fixed device array inside the library, of
+ * B2_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
+ * until the process exits.
+ *  - A call is accepted when the reference-sized workspace of the call,
+ *    b2_decode_workspace_floats(num_heads, head_dim, kv_cache_len) floats,
+ *    fits in the array (num_heads 16, head_dim 128: up to 129,024 cached
+ *    tokens); larger calls return B2_ERR_WORKSPACE and launch nothing.
+ *  - The call allocates nothing: no cudaMalloc, no cudaFree, no allocating
+ *    library routine. The first call on each device looks up the array's
+ *    device address (cudaGetSymbolAddress) with that device current; make
+ *    that first call before any stream capture.
+ *  - All calls share the one array, which keeps the last call's contents.
+ *    Nothing in it needs to start at zero: each call writes every partial
+ *    it reads. Calls whose kernels can overlap on the GPU (different streams
+ *    without ordering between them) race on the array and give wrong
+ *    results; order them on one stream. */
+#define B2_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+int b2_launch_causal_attention_decode_noalloc(const void* d_q, const void* d_k_cache,
+                                              const void* d_v_cache, void* d_out,
+                                              size_t query_len, size_t kv_cache_len,
+                                              size_t num_heads, size_t num_kv_heads,
+                                              size_t head_dim, size_t kv_stride,
+                                              b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

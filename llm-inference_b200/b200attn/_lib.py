@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_advance_position": (I, [P, ctypes.c_int32, P]),
     "b2_launch_decode_rank_partial_devlen": (I, [P, P, P, P, P, P, P, ctypes.c_int32, S, S, S, S, S, P, P, P, P]),
     "b2_launch_merge_partials_strided": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
+    "b2_launch_causal_attention_decode_noalloc": (I, [P, P, P, P, S, S, S, S, S, S, P]),
 }
 
 

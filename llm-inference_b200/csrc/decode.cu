@@ -40,6 +40,7 @@
 #include <math.h>
 
 #include <atomic>
+#include <mutex>
 
 #include "b2_common.cuh"
 #include "b2_ptx.cuh"
@@ -927,4 +928,69 @@ extern "C" int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t st
     if (d_pos == nullptr) return B2_ERR_INVALID_ARG;
     advance_position_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(d_pos, delta);
     return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Flash-decode without a caller workspace.
+//
+// Some callers cannot hand this library scratch memory: a plugin host that
+// passes only its input and output buffers, a serving process whose memory
+// pool already owns all of HBM, or a latency-critical thread that must not
+// call cudaMalloc (it can synchronise the whole device). For them the split-KV
+// partials live in this fixed array instead. Every GPU that loads the library
+// holds the array (B2_NOALLOC_SCRATCH_BYTES) until the process exits.
+static __device__ __align__(256) float g_b2_noalloc_scratch[B2_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace b2 {
+namespace {
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[64] = {};  // device address of the array, per device
+
+// Resolve the array's device address for the current device (once per device).
+// The name is a host-side stand-in in host code; the kernels need the address.
+int noalloc_scratch(float** out) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        note_cuda_error(e);
+        return B2_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= 64) return B2_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t s = cudaGetSymbolAddress(&p, g_b2_noalloc_scratch);
+        if (s != cudaSuccess || p == nullptr) {
+            note_cuda_error(s);
+            return B2_ERR_CUDA;
+        }
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return B2_OK;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_launch_causal_attention_decode_noalloc(const void* d_q, const void* d_k_cache,
+                                                         const void* d_v_cache, void* d_out, size_t query_len,
+                                                         size_t kv_cache_len, size_t num_heads, size_t num_kv_heads,
+                                                         size_t head_dim, size_t kv_stride, b2_stream_t stream) {
+    if (query_len == 0 || kv_cache_len == 0 || num_kv_heads == 0 || head_dim == 0) return B2_NOTHING_TO_DO;
+    if (num_heads % num_kv_heads != 0) return B2_NOTHING_TO_DO;
+    if (!d_q || !d_k_cache || !d_v_cache || !d_out) return B2_ERR_INVALID_ARG;
+    // The partials take at most the reference-sized workspace for this call.
+    const size_t chunks = (kv_cache_len + kChunk - 1) / kChunk;
+    const size_t need = b2_decode_workspace_floats(num_heads, head_dim, kv_cache_len);
+    if (need > B2_NOALLOC_SCRATCH_BYTES / sizeof(float)) return B2_ERR_WORKSPACE;
+    float* scratch = nullptr;
+    const int st = noalloc_scratch(&scratch);
+    if (st != B2_OK) return st;
+    float* po = scratch;
+    float* pm = po + num_heads * chunks * head_dim;
+    float* pl = pm + num_heads * chunks;
+    return launch_decode(d_q, d_k_cache, d_v_cache, d_out, po, pm, pl, query_len, kv_cache_len, nullptr, 0, 0,
+                         num_heads, num_kv_heads, head_dim, kv_stride, stream, nullptr, nullptr);
 }

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "b200attn.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
@@ -36,6 +38,31 @@ inline int cuda_status(cudaError_t e) {
         return B2_ERR_CUDA;
     }
     return B2_OK;
+}
+
+// Launch with programmatic dependent launch allowed: the kernel may start
+// while the previous kernel on the stream finishes; every kernel launched this
+// way executes griddepcontrol.wait before reading memory a predecessor writes.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        note_cuda_error(e);
+        return B2_ERR_CUDA;
+    }
+    return launch_status();
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

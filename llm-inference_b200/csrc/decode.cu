@@ -6,10 +6,13 @@
 //   merge_attention_decode (:719-838)  M = max m_s, L = sum e^(m_s-M) l_s,
 //       out = sum e^(m_s-M) o_s / L
 //   launchers (:840-972), graph-node patchers (:975-1026)
-// Partials keep the reference's meaning (o unnormalised fp32, m in natural-log
-// units of q.k/sqrt(d), l = sum e^(s-m)) in a compact [H][S][d] / [H][S]
-// layout, S = number of splits <= ceil(kv_len / KV_CHUNK), so they always fit
-// the workspace the reference sizes from KV_CHUNK.
+// Partials keep the reference's meaning (o = sum e^(s-m) v unnormalised fp32,
+// l = sum e^(s-m), m in natural-log units of q.k/sqrt(d)) in a compact
+// [H][S][d] / [H][S] layout, S = number of splits <= ceil(kv_len / KV_CHUNK),
+// so they always fit the workspace the reference sizes from KV_CHUNK. One
+// difference: m is the running max of a lazily rescaled online softmax and may
+// trail the split's true max by less than 8 log2 units (o and l are relative
+// to that m, so the merge algebra is unchanged and exact).
 //
 // Split kernels (all with one query token, kv heads x group query heads):
 //
@@ -44,18 +47,15 @@
 
 #include "b2_common.cuh"
 #include "b2_ptx.cuh"
+#include "decode_tile.cuh"
 
 namespace b2 {
 namespace {
 
-constexpr int kChunk = 256;  // KV_CHUNK
-constexpr int kTile = 16;    // tokens per MMA tile
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 constexpr uint32_t kNoCap = 0xffffffffu;
 
 // TMA kernel shape
-constexpr int kTmaConsumers = 8;
+constexpr int kTmaConsumers = 12;  // 3 per KV head at 4 KV heads; 13 warps <= 4 per sub-partition
 constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
 constexpr uint32_t kTmaSmemBudget = 192 * 1024;
 
@@ -124,198 +124,14 @@ __device__ __forceinline__ Extent decode_extent(const A& a) {
     return {len, min(chunks, a.splits_cap)};
 }
 
-// Token range [begin, end) of split s when kv_len tokens are cut into
-// `splits` ranges of a 16-token multiple.
-__device__ __forceinline__ void split_range(uint32_t kv_len, uint32_t splits, uint32_t s, uint32_t& begin,
-                                            uint32_t& end) {
-    uint32_t per = (kv_len + splits - 1) / splits;
-    per = (per + kTile - 1) / kTile * kTile;
-    begin = min(s * per, kv_len);
-    end = min(begin + per, kv_len);
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ld_stream(const __half* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-// Online-softmax state of one warp: heads 2t, 2t+1 of the group (lane = 4g+t),
-// O^T fragments for 8 row tiles of head_dim.
-struct WarpState {
-    float o[8][4];
-    float m0, m1, l0, l1;
-};
-
-__device__ __forceinline__ void state_init(WarpState& st) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) st.o[i][0] = st.o[i][1] = st.o[i][2] = st.o[i][3] = 0.f;
-    st.m0 = st.m1 = -INFINITY;
-    st.l0 = st.l1 = 0.f;
-}
-
-// Q fragments (B of the score MMA) for the heads of one GQA group.
-__device__ __forceinline__ void load_q_frags(const __half* q, uint32_t kvh, uint32_t group, int g, int t,
-                                             uint32_t (&qf)[8][2]) {
-    if (static_cast<uint32_t>(g) < group) {
-        const __half* qrow = q + static_cast<uint64_t>(kvh * group + g) * 128;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint4 w = *reinterpret_cast<const uint4*>(qrow + 32 * j + 8 * t);
-            qf[2 * j][0] = w.x;
-            qf[2 * j][1] = w.y;
-            qf[2 * j + 1][0] = w.z;
-            qf[2 * j + 1][1] = w.w;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) qf[j][0] = qf[j][1] = 0u;
-    }
-}
-
-// One 16-token tile. ka/kb: K rows g and g+8 (4 x 16 B at 32j + 8t); va:
-// V rows 2t, 2t+1, 2t+8, 2t+9 (2 x 16 B at 64b + 8g); rows at or past
-// `valid` must be zero in ka/kb/va and are masked out of the softmax.
-__device__ __forceinline__ void tile_update(WarpState& st, const uint4 (&ka)[4], const uint4 (&kb)[4],
-                                            const uint4 (&va)[4][2], const uint32_t (&qf)[8][2], int g, int t,
-                                            uint32_t valid, float scale_log2) {
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-    float s2[4] = {0.f, 0.f, 0.f, 0.f};  // two accumulation chains halve the MMA latency
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        if (j & 1) {
-            mma16816(s2, ka[j].x, kb[j].x, ka[j].y, kb[j].y, qf[2 * j][0], qf[2 * j][1]);
-            mma16816(s2, ka[j].z, kb[j].z, ka[j].w, kb[j].w, qf[2 * j + 1][0], qf[2 * j + 1][1]);
-        } else {
-            mma16816(s, ka[j].x, kb[j].x, ka[j].y, kb[j].y, qf[2 * j][0], qf[2 * j][1]);
-            mma16816(s, ka[j].z, kb[j].z, ka[j].w, kb[j].w, qf[2 * j + 1][0], qf[2 * j + 1][1]);
-        }
-    }
-    const bool ok_a = static_cast<uint32_t>(g) < valid, ok_b = static_cast<uint32_t>(g + 8) < valid;
-    s[0] = ok_a ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
-    s[1] = ok_a ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
-    s[2] = ok_b ? (s[2] + s2[2]) * scale_log2 : -INFINITY;
-    s[3] = ok_b ? (s[3] + s2[3]) * scale_log2 : -INFINITY;
-
-    float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    const float mn0 = fmaxf(st.m0, mx0), mn1 = fmaxf(st.m1, mx1);
-    const float al0 = exp2f(st.m0 - mn0), al1 = exp2f(st.m1 - mn1);
-    const float p0 = exp2f(s[0] - mn0), p1 = exp2f(s[1] - mn1);
-    const float p2 = exp2f(s[2] - mn0), p3 = exp2f(s[3] - mn1);
-    st.l0 = fmaf(st.l0, al0, p0 + p2);
-    st.l1 = fmaf(st.l1, al1, p1 + p3);
-    st.m0 = mn0;
-    st.m1 = mn1;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        st.o[i][0] *= al0;
-        st.o[i][1] *= al1;
-        st.o[i][2] *= al0;
-        st.o[i][3] *= al1;
-    }
-
-    // P^T fragments: column (head) g, tokens {2t,2t+1} and {2t+8,2t+9}.
-    const uint32_t X = pack_half2(p0, p1);  // token g,   heads 2t, 2t+1
-    const uint32_t Y = pack_half2(p2, p3);  // token g+8, heads 2t, 2t+1
-    const int src_a = 8 * t + (g >> 1);
-    const int src_b = 8 * t + 4 + (g >> 1);
-    const uint32_t Xa = __shfl_sync(0xffffffffu, X, src_a);
-    const uint32_t Xb = __shfl_sync(0xffffffffu, X, src_b);
-    const uint32_t Ya = __shfl_sync(0xffffffffu, Y, src_a);
-    const uint32_t Yb = __shfl_sync(0xffffffffu, Y, src_b);
-    const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
-    const uint32_t pb0 = __byte_perm(Xa, Xb, sel);
-    const uint32_t pb1 = __byte_perm(Ya, Yb, sel);
-
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-        const int b = mt >> 2, q = mt & 3;
-        const uint32_t w0 = word(va[0][b], q), w1 = word(va[1][b], q);
-        const uint32_t w2 = word(va[2][b], q), w3 = word(va[3][b], q);
-        mma16816(st.o[mt], __byte_perm(w0, w1, 0x5410u), __byte_perm(w0, w1, 0x7632u),
-                 __byte_perm(w2, w3, 0x5410u), __byte_perm(w2, w3, 0x7632u), pb0, pb1);
-    }
-}
-
-// Reduce the per-lane row sums over the 8 token rows (lanes with equal t).
-__device__ __forceinline__ void state_finish(WarpState& st) {
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
-        st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
-    }
-}
-
-// Store one warp's state into slot `slot`: m/l [slot][8 heads], o [slot][8][128].
-__device__ __forceinline__ void state_to_smem(const WarpState& st, int slot, float* sm_m, float* sm_l, float* sm_o,
-                                              int g, int t) {
-    if (g == 0) {
-        sm_m[slot * 8 + 2 * t] = st.m0;
-        sm_m[slot * 8 + 2 * t + 1] = st.m1;
-        sm_l[slot * 8 + 2 * t] = st.l0;
-        sm_l[slot * 8 + 2 * t + 1] = st.l1;
-    }
-    float* o = sm_o + slot * 8 * 128;
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-        const int d = 64 * (mt >> 2) + 8 * g + 2 * (mt & 3);
-        o[(2 * t) * 128 + d] = st.o[mt][0];
-        o[(2 * t + 1) * 128 + d] = st.o[mt][1];
-        o[(2 * t) * 128 + d + 1] = st.o[mt][2];
-        o[(2 * t + 1) * 128 + d + 1] = st.o[mt][3];
-    }
-}
-
-// Combine `nslots` warp states of one KV head (slots first, first+stride, ...)
-// into the partial of (head kvh*group + hh, split), idx = hh*128 + d.
-__device__ __forceinline__ void combine_write(const float* sm_m, const float* sm_l, const float* sm_o, int first,
-                                              int stride, int nslots, uint32_t kvh, uint32_t group, uint32_t split,
-                                              uint32_t splits, float* po, float* pm, float* pl, uint32_t idx) {
-    const uint32_t hh = idx >> 7, d = idx & 127;
-    float M = -INFINITY;
-    for (int w = 0; w < nslots; ++w) M = fmaxf(M, sm_m[(first + w * stride) * 8 + hh]);
-    float L = 0.f, O = 0.f;
-    for (int w = 0; w < nslots; ++w) {
-        const int sl = first + w * stride;
-        const float m = sm_m[sl * 8 + hh];
-        const float sc = (m == -INFINITY) ? 0.f : exp2f(m - M);
-        L = fmaf(sc, sm_l[sl * 8 + hh], L);
-        O = fmaf(sc, sm_o[(sl * 8 + hh) * 128 + d], O);
-    }
-    const uint64_t state = static_cast<uint64_t>(kvh * group + hh) * splits + split;
-    po[state * 128 + d] = O;
-    if (d == 0) {
-        pm[state] = M == -INFINITY ? -INFINITY : M * kLn2;
-        pl[state] = L;
-    }
-}
-
 // ---------------------------------------------------------------------------
-// Persistent TMA split kernel. grid = min(#SMs, chunks), block = 9 warps.
+// Persistent TMA split kernel. grid = min(#SMs, chunks), block = 13 warps.
 __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const DecodeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
+    pdl_wait_primary();  // Q, the cache and the device length may come from the previous kernel
+    pdl_launch_dependents();
     const Extent ext = decode_extent(a);
     const uint32_t split = blockIdx.x;
-    pdl_launch_dependents();
     if (split >= ext.splits) return;
     uint32_t begin, end;
     split_range(ext.kv_len, ext.splits, split, begin, end);
@@ -328,7 +144,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * 2 * tile_bytes);
     uint64_t* empty = full + stages;
     const uint32_t ntiles = (end - begin + kTile - 1) / kTile;
-    const uint32_t npar = kTmaConsumers / KVH;       // consumer warps per KV head
+    const uint32_t npar = kTmaConsumers / KVH;       // consumer warps per KV head; divides `stages`
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -374,8 +190,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
         const int g = lane >> 2, t = lane & 3;
         uint32_t qf[8][2];
         load_q_frags(a.q, kvh, a.group, g, t, qf);
-        const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
-        for (uint32_t i = par; i < ntiles; i += npar) {
+        // warps past KVH * npar (8 KV heads: 4 of 12) have no tiles
+        for (uint32_t i = par; par < npar && i < ntiles; i += npar) {
             const uint32_t s = i % stages, round = i / stages;
             if (!mbar_wait(&full[s], round & 1)) {
                 ok = false;
@@ -384,28 +200,22 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
             const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * 256;
             const uint8_t* vt = kt + tile_bytes;
             const uint32_t valid = min(static_cast<uint32_t>(kTile), end - (begin + i * kTile));
-            uint4 ka[4], kb[4], va[4][2];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                ka[j] = static_cast<uint32_t>(g) < valid
-                            ? *reinterpret_cast<const uint4*>(kt + g * row_bytes + (32 * j + 8 * t) * 2)
-                            : zero4;
-                kb[j] = static_cast<uint32_t>(g + 8) < valid
-                            ? *reinterpret_cast<const uint4*>(kt + (g + 8) * row_bytes + (32 * j + 8 * t) * 2)
-                            : zero4;
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t row = 2 * t + (r & 1) + (r >> 1) * 8;
-#pragma unroll
-                for (int b = 0; b < 2; ++b)
-                    va[r][b] = row < valid
-                                   ? *reinterpret_cast<const uint4*>(vt + row * row_bytes + (64 * b + 8 * g) * 2)
-                                   : zero4;
+            float sc[4];
+            uint4 va[4][2];
+            if (valid == kTile) {
+                uint4 ka[4], kb[4];
+                load_k_frags<false>(kt, row_bytes, g, t, valid, ka, kb);
+                tile_scores<false>(sc, ka, kb, qf, g, valid, a.scale_log2);
+                load_v_frags<false>(vt, row_bytes, g, t, valid, va);
+            } else {
+                uint4 ka[4], kb[4];
+                load_k_frags<true>(kt, row_bytes, g, t, valid, ka, kb);
+                tile_scores<true>(sc, ka, kb, qf, g, valid, a.scale_log2);
+                load_v_frags<true>(vt, row_bytes, g, t, valid, va);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            tile_update(st, ka, kb, va, qf, g, t, valid, a.scale_log2);
+            if (lane == 0) mbar_arrive(&empty[s]);  // the stage can be refilled
+            tile_softmax_pv(st, sc, va, g, t);
         }
         state_finish(st);
     }
@@ -417,11 +227,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
     if (warp < kTmaConsumers) state_to_smem(st, warp, sm_m, sm_l, sm_o, lane >> 2, lane & 3);
     __syncthreads();
     // Slots of KV head h are h, h + KVH, ...: combine and write the partials.
-    for (uint32_t idx = threadIdx.x; idx < KVH * a.group * 128; idx += kTmaThreads) {
-        const uint32_t h = idx / (a.group * 128);
-        combine_write(sm_m, sm_l, sm_o, static_cast<int>(h), static_cast<int>(KVH), static_cast<int>(npar), h,
-                      a.group, split, ext.splits, a.po, a.pm, a.pl, idx - h * a.group * 128);
-    }
+    combine_tile_any(npar, sm_m, sm_l, sm_o, KVH, a.group, split, ext.splits, a.po, a.pm, a.pl, threadIdx.x,
+                     kTmaThreads);
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
 }
 
@@ -430,11 +237,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
 __global__ void __launch_bounds__(128) decode_split_mma_kernel(const DecodeArgs a) {
     __shared__ float sm_m[4 * 8];
     __shared__ float sm_l[4 * 8];
-    __shared__ float sm_o[4 * 8 * 128];
+    __shared__ float sm_o[4 * 8 * kOStride];
     const uint32_t kvh = blockIdx.x;
     const uint32_t chunk = blockIdx.y;
-    const Extent ext = decode_extent(a);
+    pdl_wait_primary();
     pdl_launch_dependents();
+    const Extent ext = decode_extent(a);
     if (chunk >= ext.splits) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -465,13 +273,15 @@ __global__ void __launch_bounds__(128) decode_split_mma_kernel(const DecodeArgs 
 #pragma unroll
             for (int b = 0; b < 2; ++b) va[i][b] = r < w1 ? ld_stream(vbase + r * stride + 64 * b + 8 * g) : zero4;
         }
-        tile_update(st, ka, kb, va, qf, g, t, w1 - tb, a.scale_log2);
+        float sc[4];
+        tile_scores<true>(sc, ka, kb, qf, g, w1 - tb, a.scale_log2);
+        tile_softmax_pv(st, sc, va, g, t);
     }
     state_finish(st);
     state_to_smem(st, warp, sm_m, sm_l, sm_o, g, t);
     __syncthreads();
     for (uint32_t idx = threadIdx.x; idx < a.group * 128; idx += blockDim.x)
-        combine_write(sm_m, sm_l, sm_o, 0, 1, 4, kvh, a.group, chunk, ext.splits, a.po, a.pm, a.pl, idx);
+        combine_write(sm_m, sm_l, sm_o, 0, 1, 4, kvh, a.group, chunk, ext.splits, a.po, a.pm, a.pl, idx);  // 4 warps
 }
 
 // ---------------------------------------------------------------------------
@@ -482,8 +292,9 @@ __global__ void __launch_bounds__(128) decode_split_simt_kernel(const DecodeArgs
     __shared__ float red[4];
     const uint32_t h = blockIdx.x;
     const uint32_t chunk = blockIdx.y;
-    const Extent ext = decode_extent(a);
+    pdl_wait_primary();
     pdl_launch_dependents();
+    const Extent ext = decode_extent(a);
     if (chunk >= ext.splits) return;
     const uint32_t kvh = h / a.group;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -538,12 +349,20 @@ __global__ void __launch_bounds__(128) decode_split_simt_kernel(const DecodeArgs
 }
 
 // ---------------------------------------------------------------------------
-// Merge: grid = (num_heads, ceil(head_dim / 64)), block = 256. Warps stride
-// over splits (four in flight per warp), lanes over two output dimensions.
-__global__ void __launch_bounds__(256) merge_partials_kernel(const MergeArgs a) {
-    __shared__ float red[8];
-    __shared__ float acc_s[8][64];
+// Merge: grid = (num_heads, ceil(head_dim / 64)), block = 512. Warp w takes
+// splits w, w + 16, ...; a lane owns two output dims. Each batch of kMergeBatch
+// splits per warp is loaded in one round (m, l, o all in flight) and folded
+// into a running (max, sum, o) with the same rescaling as the split kernels;
+// warp 0 then merges the 16 warp states.
+constexpr int kMergeWarps = 16;
+constexpr int kMergeBatch = 10;
+
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_partials_kernel(const MergeArgs a) {
+    __shared__ float red_m[kMergeWarps];
+    __shared__ float red_l[kMergeWarps];
+    __shared__ float2 acc_s[kMergeWarps][32];
     pdl_wait_primary();
+    pdl_launch_dependents();
     const uint32_t h = blockIdx.x;
     const uint32_t d0 = blockIdx.y * 64;
     const uint32_t d = a.head_dim;
@@ -557,16 +376,20 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeArgs a) 
         n = decode_extent(a).splits;
         o_head = static_cast<uint64_t>(n) * d, o_chunk = d, ml_head = n, ml_chunk = 1;
     }
+    const uint32_t e0 = d0 + 2 * lane, e1 = e0 + 1;
     if (n == 0) {  // graph-static launch with an empty range: defined output
-        for (uint32_t e = d0 + threadIdx.x; e < min(d0 + 64, d); e += blockDim.x) {
-            if (a.rank_o)
-                a.rank_o[static_cast<uint64_t>(h) * d + e] = 0.f;
-            else
-                a.out[static_cast<uint64_t>(h) * d + e] = __float2half_rn(0.f);
-        }
-        if (a.rank_o && blockIdx.y == 0 && threadIdx.x == 0) {
-            a.rank_m[h] = -INFINITY;
-            a.rank_l[h] = 0.f;
+        if (warp == 0) {
+            if (a.rank_o) {
+                if (e0 < d) a.rank_o[static_cast<uint64_t>(h) * d + e0] = 0.f;
+                if (e1 < d) a.rank_o[static_cast<uint64_t>(h) * d + e1] = 0.f;
+                if (blockIdx.y == 0 && lane == 0) {
+                    a.rank_m[h] = -INFINITY;
+                    a.rank_l[h] = 0.f;
+                }
+            } else {
+                if (e0 < d) a.out[static_cast<uint64_t>(h) * d + e0] = __float2half_rn(0.f);
+                if (e1 < d) a.out[static_cast<uint64_t>(h) * d + e1] = __float2half_rn(0.f);
+            }
         }
         return;
     }
@@ -574,76 +397,77 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeArgs a) 
     const float* pl = a.pl + h * ml_head;
     const float* po = a.po + h * o_head;
 
-    float mx = -INFINITY;
-    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) mx = fmaxf(mx, pm[c * ml_chunk]);
+    float m_run = -INFINITY, l_run = 0.f, ax = 0.f, ay = 0.f;
+    for (uint32_t base = warp; base < n; base += kMergeWarps * kMergeBatch) {
+        float mv[kMergeBatch], lv[kMergeBatch], ox[kMergeBatch], oy[kMergeBatch];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
+        for (int u = 0; u < kMergeBatch; ++u) {
+            const uint32_t c = base + kMergeWarps * u;
+            const bool in = c < n;
+            mv[u] = in ? pm[c * ml_chunk] : -INFINITY;
+            lv[u] = in ? pl[c * ml_chunk] : 0.f;
+            const float* row = po + c * o_chunk;
+            ox[u] = in && e0 < d ? row[e0] : 0.f;
+            oy[u] = in && e1 < d ? row[e1] : 0.f;
+        }
+        float bm = m_run;
 #pragma unroll
-    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
-    __syncthreads();
-
-    float den = 0.f;
-    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
-        const float m = pm[c * ml_chunk];
-        if (m != -INFINITY) den = fmaf(expf(m - mx), pl[c * ml_chunk], den);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-    if (lane == 0) red[warp] = den;
-    __syncthreads();
-    den = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) den += red[w];
-
-    const uint32_t e0 = d0 + 2 * lane, e1 = e0 + 1;
-    float s0 = 0.f, s1 = 0.f;
-    uint32_t c = warp;
-    for (; c + 24 < n; c += 32) {  // four independent splits per iteration
-        float sc[4], x0[4], x1[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t cc = c + 8 * u;
-            const float m = pm[cc * ml_chunk];
-            sc[u] = m == -INFINITY ? 0.f : expf(m - mx);
-            const float* row = po + cc * o_chunk;
-            x0[u] = e0 < d ? row[e0] : 0.f;
-            x1[u] = e1 < d ? row[e1] : 0.f;
+        for (int u = 0; u < kMergeBatch; ++u) bm = fmaxf(bm, mv[u]);
+        if (bm > m_run) {
+            const float sc = m_run == -INFINITY ? 0.f : expf(m_run - bm);
+            ax *= sc;
+            ay *= sc;
+            l_run *= sc;
+            m_run = bm;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            s0 = fmaf(sc[u], x0[u], s0);
-            s1 = fmaf(sc[u], x1[u], s1);
+        for (int u = 0; u < kMergeBatch; ++u) {
+            if (mv[u] != -INFINITY) {
+                const float w = expf(mv[u] - m_run);
+                ax = fmaf(w, ox[u], ax);
+                ay = fmaf(w, oy[u], ay);
+                l_run = fmaf(w, lv[u], l_run);
+            }
         }
     }
-    for (; c < n; c += 8) {
-        const float m = pm[c * ml_chunk];
-        const float sc = m == -INFINITY ? 0.f : expf(m - mx);
-        const float* row = po + c * o_chunk;
-        if (e0 < d) s0 = fmaf(sc, row[e0], s0);
-        if (e1 < d) s1 = fmaf(sc, row[e1], s1);
+    if (lane == 0) {
+        red_m[warp] = m_run;
+        red_l[warp] = l_run;
     }
-    acc_s[warp][2 * lane] = s0;
-    acc_s[warp][2 * lane + 1] = s1;
+    acc_s[warp][lane] = make_float2(ax, ay);
     __syncthreads();
-    if (threadIdx.x < 64 && d0 + threadIdx.x < d) {
-        float s = 0.f;
+    if (warp != 0) return;
+    float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) s += acc_s[w][threadIdx.x];
-        if (a.rank_o)
-            a.rank_o[static_cast<uint64_t>(h) * d + d0 + threadIdx.x] = s;
-        else
-            a.out[static_cast<uint64_t>(h) * d + d0 + threadIdx.x] = __float2half_rn(s / den);
+    for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, red_m[w]);
+    float L = 0.f, sx = 0.f, sy = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) {
+        const float m = red_m[w];
+        const float sc = m == -INFINITY ? 0.f : expf(m - M);
+        L = fmaf(sc, red_l[w], L);
+        sx = fmaf(sc, acc_s[w][lane].x, sx);
+        sy = fmaf(sc, acc_s[w][lane].y, sy);
     }
-    if (a.rank_o && blockIdx.y == 0 && threadIdx.x == 0) {
-        a.rank_m[h] = mx;
-        a.rank_l[h] = den;
+    if (a.rank_o) {
+        if (e0 < d) a.rank_o[static_cast<uint64_t>(h) * d + e0] = sx;
+        if (e1 < d) a.rank_o[static_cast<uint64_t>(h) * d + e1] = sy;
+        if (blockIdx.y == 0 && lane == 0) {
+            a.rank_m[h] = M;
+            a.rank_l[h] = L;
+        }
+    } else {
+        const float inv = 1.f / L;
+        if (e0 < d) a.out[static_cast<uint64_t>(h) * d + e0] = __float2half_rn(sx * inv);
+        if (e1 < d) a.out[static_cast<uint64_t>(h) * d + e1] = __float2half_rn(sy * inv);
     }
 }
 
-__global__ void advance_position_kernel(int32_t* pos, int32_t delta) { *pos += delta; }
+__global__ void advance_position_kernel(int32_t* pos, int32_t delta) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    *pos += delta;
+}
 
 const void* const kSplitKernels[] = {
     reinterpret_cast<const void*>(decode_split_tma_kernel),
@@ -677,23 +501,8 @@ int ensure_tma_smem() {
 }
 
 int launch_merge_kernel(const MergeArgs& m, cudaStream_t stream) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(m.num_heads, (m.head_dim + 63) / 64);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, merge_partials_kernel, m);
-    if (e != cudaSuccess) {
-        (void)cudaGetLastError();
-        note_cuda_error(e);
-        return B2_ERR_CUDA;
-    }
-    return launch_status();
+    return launch_pdl(merge_partials_kernel, dim3(m.num_heads, (m.head_dim + 63) / 64), dim3(kMergeWarps * 32), 0,
+                      stream, m);
 }
 
 MergeArgs merge_args_from(const DecodeArgs& a, __half* out, float* rank_o, float* rank_m, float* rank_l) {
@@ -761,18 +570,24 @@ int launch_decode(const void* d_q, const void* d_k, const void* d_v, void* d_out
     int st;
     if (tma_ok) {
         if ((st = ensure_tma_smem()) != B2_OK) return st;
+        // Each stage must always be consumed by the same warp of a KV head (a
+        // warp waits on a stage's next phase only after consuming the current
+        // one), so the ring depth is a multiple of the consumer warps per head.
         const uint32_t stage_bytes = 2u * kTile * static_cast<uint32_t>(num_kv_heads) * 256u;
-        a.stages = min(8u, kTmaSmemBudget / stage_bytes);
+        const uint32_t npar = kTmaConsumers / static_cast<uint32_t>(num_kv_heads);
+        a.stages = (kTmaSmemBudget / stage_bytes) / npar * npar;
+        if (a.stages == 0) return B2_ERR_UNSUPPORTED;
         a.splits_cap = static_cast<uint32_t>(device_sms());
         const uint32_t grid = static_cast<uint32_t>(chunks < a.splits_cap ? chunks : a.splits_cap);
         const size_t smem = a.stages * stage_bytes + 2 * a.stages * sizeof(uint64_t);
-        decode_split_tma_kernel<<<grid, kTmaThreads, smem, stream>>>(a);
+        st = launch_pdl(decode_split_tma_kernel, dim3(grid), dim3(kTmaThreads), smem, stream, a);
     } else if (mma_ok) {
-        decode_split_mma_kernel<<<dim3(a.num_kv_heads, static_cast<uint32_t>(chunks)), 128, 0, stream>>>(a);
+        st = launch_pdl(decode_split_mma_kernel, dim3(a.num_kv_heads, static_cast<uint32_t>(chunks)), dim3(128), 0,
+                        stream, a);
     } else {
-        decode_split_simt_kernel<<<dim3(a.num_heads, static_cast<uint32_t>(chunks)), 128, 0, stream>>>(a);
+        st = launch_pdl(decode_split_simt_kernel, dim3(a.num_heads, static_cast<uint32_t>(chunks)), dim3(128), 0,
+                        stream, a);
     }
-    st = launch_status();
     if (st != B2_OK) return st;
     if (attention_node) {
         cudaGraphNode_t n = nullptr;
@@ -926,8 +741,8 @@ extern "C" int b2_launch_decode_rank_partial_devlen(const void* d_q, const void*
 
 extern "C" int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream) {
     if (d_pos == nullptr) return B2_ERR_INVALID_ARG;
-    advance_position_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(d_pos, delta);
-    return launch_status();
+    return launch_pdl(advance_position_kernel, dim3(1), dim3(1), 0, reinterpret_cast<cudaStream_t>(stream), d_pos,
+                      delta);
 }
 
 // ---------------------------------------------------------------------------

@@ -23,6 +23,7 @@
 #include <algorithm>
 
 #include "b2_common.cuh"
+#include "b2_ptx.cuh"
 
 namespace b2 {
 namespace {
@@ -90,6 +91,8 @@ __device__ __forceinline__ void rot8(uint4& lo, uint4& hi, uint4 cv, uint4 sv) {
 
 // Vectorised rotate (+ store) kernel: lanes = half_dim / 8.
 __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
     uint32_t start;
     if (!resolve_start(a, start)) return;
     const uint64_t per_token = static_cast<uint64_t>(a.slots) * a.lanes;
@@ -133,6 +136,8 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
 
 // Scalar rotate (+ store) kernel: lanes = half_dim, any stride / alignment.
 __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
     uint32_t start;
     if (!resolve_start(a, start)) return;
     const uint64_t per_token = static_cast<uint64_t>(a.slots) * a.lanes;
@@ -176,6 +181,8 @@ __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a
 // NoPE append: K and V rows copied verbatim. lanes = kv_dim / 8 (vec8) or
 // kv_dim (scalar); slots = 2 (K, V).
 __global__ void __launch_bounds__(256) kv_copy_vec8_kernel(const RopeArgs a) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
     uint32_t start;
     if (!resolve_start(a, start)) return;
     const uint64_t per_token = 2ull * a.lanes;
@@ -194,6 +201,8 @@ __global__ void __launch_bounds__(256) kv_copy_vec8_kernel(const RopeArgs a) {
 }
 
 __global__ void __launch_bounds__(256) kv_copy_scalar_kernel(const RopeArgs a) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
     uint32_t start;
     if (!resolve_start(a, start)) return;
     const uint64_t per_token = 2ull * a.lanes;
@@ -285,10 +294,9 @@ int launch_rope_impl(void* d_q, void* d_k, const void* d_v, void* d_k_cache, voi
         a.total_items = static_cast<uint64_t>(seq_len) * a.slots * a.lanes;
         const int blocks = static_cast<int>(std::min<uint64_t>((a.total_items + 255) / 256, 16ull * sm_count()));
         if (vec)
-            rope_store_vec8_kernel<<<blocks, 256, 0, stream>>>(a);
+            return launch_pdl(rope_store_vec8_kernel, dim3(blocks), dim3(256), 0, stream, a);
         else
-            rope_store_scalar_kernel<<<blocks, 256, 0, stream>>>(a);
-        return launch_status();
+            return launch_pdl(rope_store_scalar_kernel, dim3(blocks), dim3(256), 0, stream, a);
     }
     // NoPE: copy_to_kv_cache (rope.hip.cpp:181-195). A cache is required.
     if (!store) return B2_ERR_INVALID_ARG;
@@ -298,10 +306,9 @@ int launch_rope_impl(void* d_q, void* d_k, const void* d_v, void* d_k_cache, voi
     a.total_items = static_cast<uint64_t>(seq_len) * 2 * a.lanes;
     const int blocks = static_cast<int>(std::min<uint64_t>((a.total_items + 255) / 256, 16ull * sm_count()));
     if (vec)
-        kv_copy_vec8_kernel<<<blocks, 256, 0, stream>>>(a);
+        return launch_pdl(kv_copy_vec8_kernel, dim3(blocks), dim3(256), 0, stream, a);
     else
-        kv_copy_scalar_kernel<<<blocks, 256, 0, stream>>>(a);
-    return launch_status();
+        return launch_pdl(kv_copy_scalar_kernel, dim3(blocks), dim3(256), 0, stream, a);
 }
 
 }  // namespace

@@ -115,6 +115,18 @@ int b2_launch_causal_attention_prefill(const void* d_q, const void* d_k, const v
                                        size_t q_stride, size_t kv_stride,
                                        b2_stream_t stream);
 
+/* Batched form of b2_launch_causal_attention_prefill (no reference
+ * counterpart; the reference engine is batch 1): `batch` independent
+ * sequences of seq_len tokens, sequence b's Q / K / V / out rows starting
+ * q_batch_stride / kv_batch_stride / out_batch_stride elements after
+ * sequence b-1's (e.g. per-sequence KV caches of one allocation). */
+int b2_launch_causal_attention_prefill_batched(const void* d_q, const void* d_k, const void* d_v,
+                                               void* d_out, size_t batch, size_t seq_len,
+                                               size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                               size_t q_stride, size_t kv_stride,
+                                               size_t q_batch_stride, size_t kv_batch_stride,
+                                               size_t out_batch_stride, b2_stream_t stream);
+
 /* include/kernels/kernels.hpp:104-125 launch_causal_attention_decode
  * (src/kernels/causal_attention.hip.cpp:840-921): one query token over
  * kv_cache_len cached tokens, split into KV_CHUNK-token chunks whose (o, m, l)

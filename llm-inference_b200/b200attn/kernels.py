@@ -24,7 +24,7 @@ __all__ = [
     "update_merge_attention_decode_node", "launch_merge_attention_decode_tiled",
     "decode_workspace_floats", "kernel_launch_count", "launch_rope_and_store_kv_devpos",
     "launch_causal_attention_decode_devlen", "advance_position", "launch_decode_rank_partial_devlen",
-    "launch_merge_partials_strided",
+    "launch_merge_partials_strided", "launch_causal_attention_prefill_batched",
 ]
 
 
@@ -206,3 +206,13 @@ def launch_merge_partials_strided(d_o, d_m, d_l, d_out, num_heads, num_chunks, h
     check(lib().b2_launch_merge_partials_strided(
         _ptr(d_o), _ptr(d_m), _ptr(d_l), _ptr(d_out), num_heads, num_chunks, head_dim, o_chunk_stride,
         o_head_stride, ml_chunk_stride, ml_head_stride, _stream(stream)), "launch_merge_partials_strided")
+
+
+def launch_causal_attention_prefill_batched(d_q, d_k, d_v, d_out, batch, seq_len, num_heads, num_kv_heads,
+                                            head_dim, q_stride=0, kv_stride=0, q_batch_stride=0,
+                                            kv_batch_stride=0, out_batch_stride=0, stream=None):
+    """`batch` independent causal prefills (sequence b at the given batch strides)."""
+    check(lib().b2_launch_causal_attention_prefill_batched(
+        _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_out), batch, seq_len, num_heads, num_kv_heads, head_dim,
+        q_stride, kv_stride, q_batch_stride, kv_batch_stride, out_batch_stride, _stream(stream)),
+        "launch_causal_attention_prefill_batched")

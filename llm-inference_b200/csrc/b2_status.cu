@@ -71,7 +71,7 @@ int b2_last_cuda_error(void) { return b2::g_last_cuda_error.load(); }
 
 uint64_t b2_kernel_launch_count(void) { return b2::g_launches.load(); }
 
-unsigned int b2_device_error_word(void) { return b2::device_error_decode(); }
+unsigned int b2_device_error_word(void) { return b2::device_error_decode() | b2::device_error_prefill(); }
 
 int b2_fill_rope_tables(size_t max_seq_len, size_t head_dim, float rope_theta,
                         uint16_t* host_cos, uint16_t* host_sin) {

@@ -49,3 +49,16 @@ extern "C" int b2_launch_causal_attention_prefill(const void* d_q, const void* d
     return b2::prefill_common(d_q, d_k, d_v, d_out, 1, seq_len, num_heads, num_kv_heads, head_dim, q_stride,
                               kv_stride, 0, 0, 0, reinterpret_cast<cudaStream_t>(stream));
 }
+
+extern "C" int b2_launch_causal_attention_prefill_batched(const void* d_q, const void* d_k, const void* d_v,
+                                                          void* d_out, size_t batch, size_t seq_len,
+                                                          size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                                          size_t q_stride, size_t kv_stride, size_t q_batch_stride,
+                                                          size_t kv_batch_stride, size_t out_batch_stride,
+                                                          b2_stream_t stream) {
+    if (batch > 1 && (q_batch_stride == 0 || kv_batch_stride == 0 || out_batch_stride == 0))
+        return B2_ERR_INVALID_ARG;
+    return b2::prefill_common(d_q, d_k, d_v, d_out, batch, seq_len, num_heads, num_kv_heads, head_dim, q_stride,
+                              kv_stride, q_batch_stride, kv_batch_stride, out_batch_stride,
+                              reinterpret_cast<cudaStream_t>(stream));
+}

@@ -108,3 +108,35 @@ def test_prefill_other_shapes_vs_oracle(cuda, shape):
     got = _prefill(q, k, v, S, H, KVH, d, qs, ks)
     _, o32 = oracle.causal_attention(q, k, v, S, H, KVH, d, qs, ks)
     assert_attention_close(got, o32)
+
+
+def test_prefill_batched_matches_per_sequence(cuda):
+    """Config-3 layout: B sequences with per-sequence strides (batched entry point)."""
+    import torch
+    B, S, H, KVH, d = 3, 300, 16, 4, 128
+    q = seeded_f16((B, S, H * d), 71)
+    k = seeded_f16((B, S + 5, KVH * d), 72)   # per-sequence cache with spare rows
+    v = seeded_f16((B, S + 5, KVH * d), 73)
+    out = torch.zeros((B, S, H * d), dtype=torch.float16, device=cuda)
+    b200attn.launch_causal_attention_prefill_batched(dev(q), dev(k), dev(v), out, B, S, H, KVH, d, H * d, KVH * d,
+                                                     S * H * d, (S + 5) * KVH * d, S * H * d)
+    _sync()
+    got = host(out)
+    for b in range(B):
+        _, o32 = oracle.causal_attention(q[b], k[b], v[b], S, H, KVH, d)
+        assert_attention_close(got[b], o32)
+
+
+@pytest.mark.parametrize("S", [8192])
+def test_prefill_config3_unit_sampled(cuda, S):
+    """One (sequence, KV head) unit of BASELINE config 3 at full length, sampled rows."""
+    H, KVH, d = 16, 4, 128
+    q = seeded_f16((S, H * d), 81)
+    k = seeded_f16((S, KVH * d), 82)
+    v = seeded_f16((S, KVH * d), 83)
+    got = _prefill(q, k, v, S, H, KVH, d)
+    assert np.all(np.isfinite(got.astype(np.float32)))
+    rng = np.random.default_rng(S)
+    rows = sorted(set([0, 127, 128, 4095, 4096, S - 1] + list(rng.integers(0, S, 24))))
+    _, o32 = oracle.causal_attention(q, k, v, S, H, KVH, d, rows=rows)
+    assert_attention_close(got[rows], o32)

@@ -56,6 +56,17 @@ WORKLOAD = ("config4: long-context decode, batch 1, KV 65536 tokens ~N(0,0.5) FP
             "36 layers x 1 token per step (RoPE+append+split-KV decode+merge), KV_CHUNK 256")
 
 
+# BASELINE config 3 (prefill): 4 sequences x 8192 tokens, 36 layers, NoPE every 4th layer
+PF_B, PF_S = 4, 8192
+PF_WORKLOAD = ("config3: causal GQA prefill, batch 4 x 8192 tokens, 16/4 heads, head_dim 128, N(0,1) FP16, "
+               "36 layers x (RoPE theta 5e6 / NoPE every 4th layer + KV append + causal attention)")
+
+
+def prefill_flops(batch: int, seq: int, heads: int = 16) -> int:
+    """Causal exact count for QK^T + PV: 2 * B * H * d * S * (S + 1)."""
+    return 2 * batch * heads * D * seq * (seq + 1)
+
+
 def layer_bytes(kv_len: int) -> int:
     return 2 * kv_len * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + 2 * KV_DIM * 2
 
@@ -206,6 +217,91 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- prefill (config 3)
+def run_prefill(args, rank, world, dev):
+    """36 layers of RoPE/append + causal prefill for the (sequence, KV head)
+    units this rank owns; returns a dict for the JSON line (rank 0)."""
+    import numpy as np
+    import torch
+    import b200attn
+    from b200attn import dist as bdist
+    units = bdist.prefill_units(PF_B, KVH, world, rank)
+    seqs = sorted({b for b, _ in units})
+    gen = torch.Generator(device=dev).manual_seed(SEED + 100 + rank)
+    qkv = torch.empty((PF_B, PF_S, QKV), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    cache = torch.empty((PF_B, LAYERS, 2, PF_S, KV_DIM), dtype=torch.float16, device=dev)
+    out = torch.empty((PF_B, PF_S, Q_DIM), dtype=torch.float16, device=dev)
+    cos, sin = b200attn.rope_tables_host(PF_S, D, 5.0e6)
+    d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    stream = torch.cuda.Stream(device=dev)
+    full_batch = len(units) == PF_B * KVH
+
+    def layer(l, t_attn=None):
+        rotate = (l + 1) % 4 != 0
+        for b in seqs:
+            row = qkv[b]
+            b200attn.launch_rope_and_store_kv(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[b, l, 0],
+                                              cache[b, l, 1], d_cos, d_sin, PF_S, H, KVH, D, QKV, QKV, 0, rotate,
+                                              stream=stream)
+        if t_attn is not None:
+            t_attn[0].record(stream)
+        if full_batch:
+            b200attn.launch_causal_attention_prefill_batched(
+                qkv, cache[0, l, 0], cache[0, l, 1], out, PF_B, PF_S, H, KVH, D, QKV, KV_DIM, PF_S * QKV,
+                LAYERS * 2 * PF_S * KV_DIM, PF_S * Q_DIM, stream=stream)
+        else:
+            for b, g in units:
+                g0 = g * (H // KVH)
+                b200attn.launch_causal_attention_prefill(
+                    qkv[b, :, g0 * D:], cache[b, l, 0, :, g * D:], cache[b, l, 1, :, g * D:], out[b, :, g0 * D:],
+                    PF_S, H // KVH, 1, D, QKV, KV_DIM, stream=stream)
+        if t_attn is not None:
+            t_attn[1].record(stream)
+
+    steps = max(1, min(args.steps, args.prefill_steps))
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup // 2)):
+            for l in range(LAYERS):
+                layer(l)
+    torch.cuda.synchronize()
+    n0 = b200attn.kernel_launch_count()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        for s_ in range(steps):
+            for l in range(LAYERS):
+                layer(l, attn_ev[l] if s_ == steps - 1 else None)
+        ev[1].record(stream)
+    torch.cuda.synchronize()
+    launches = b200attn.kernel_launch_count() - n0
+    ms = ev[0].elapsed_time(ev[1])
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / LAYERS
+    if world > 1:
+        ms = bdist.max_over_ranks(ms, dev)
+    total_flops = prefill_flops(PF_B, PF_S) * LAYERS * steps       # whole job, all ranks
+    unit_flops = prefill_flops(1, PF_S, H // KVH) * len(units)     # this rank, one layer
+    tf = total_flops / (ms / 1e3) / 1e12
+    achieved = unit_flops / (attn_ms / 1e3) / 1e12
+    peak = 1596.6
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    kind = "fallback"
+    if os.path.exists(pk):
+        with open(pk) as f:
+            peak, kind = float(json.load(f)["bf16_tflops"]), "measured (bf16 burst; fp16 runs at the same rate)"
+    return {"metric": "prefill TFLOP/s", "value": round(tf, 2), "unit": "TFLOP/s", "workload": PF_WORKLOAD,
+            "steps": steps, "ms_per_step": round(ms / steps, 3), "gpu_launches": launches,
+            "units_per_rank": len(units), "parallelism": f"batch x kv-head units over {world} GPU(s)",
+            "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
+                         "frac_of_nominal_2250": round(achieved / 2250.0, 4), "avg_launch_ms": round(attn_ms, 4),
+                         "algorithmic_flops_per_launch": unit_flops}}
+
+
 # --------------------------------------------------------------------------- GPU arm
 def run_b200(args, rank, world):
     import numpy as np
@@ -312,6 +408,12 @@ def run_b200(args, rank, world):
                "sample": f"{reps} layer-steps of the 64K decode (RoPE+append+attention) in {el:.1f} s, "
                          f"C oracle, {threads} OpenMP threads"}
 
+    prefill = None
+    if not args.no_prefill:
+        del cache
+        torch.cuda.empty_cache()
+        prefill = run_prefill(args, rank, world, dev)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -331,6 +433,7 @@ def run_b200(args, rank, world):
             "clocks": clocks.summary(),
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     graph.reset()
@@ -343,6 +446,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sub-measurement")
+    ap.add_argument("--prefill-steps", type=int, default=4, help="timed prefill steps (36 layers each)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

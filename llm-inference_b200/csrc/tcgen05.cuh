@@ -133,7 +133,7 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 
 // ---- tensor TMA -------------------------------------------------------------
 
-// 2-D / 3-D tiled loads into shared memory completing on `bar` (no multicast).
+// 2-D / 3-D tiled loads into this CTA's shared memory completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::

@@ -328,7 +328,7 @@ def run_b200(args, rank, world):
     qkv = qkv_host.to(dev)
     out = torch.zeros((LAYERS, Q_DIM), dtype=torch.float16, device=dev)
     out_host = torch.zeros_like(out, device="cpu").pin_memory()
-    step_state = bdist.DecodeStepState(plan, H, KVH, D, LAYERS, capacity, max_global, dev)
+    step_state = bdist.DecodeStepState(plan, H, KVH, D, LAYERS, capacity, max_global, dev, fused=not args.unfused)
 
     stream = torch.cuda.Stream(device=dev)
     group = None
@@ -381,9 +381,9 @@ def run_b200(args, rank, world):
     total_bytes = sum(step_bytes(PAST + 1 + s) for s in range(args.steps))
     value = total_bytes / (ms / 1e3) / 1e9
 
-    # ---- roofline: decode (split + merge) per layer, CUDA events on its stream
+    # ---- roofline: one layer's decode launch(es), CUDA events on its stream
     peak, peak_kind = load_peaks()
-    dec_ms = bdist.time_decode_launches(step_state, cache, qkv, out, stream, reps=3)
+    dec_ms = bdist.time_decode_launches(step_state, cache, qkv, out, stream, reps=3, d_cos=d_cos, d_sin=d_sin)
     kv_len_local = plan.local_len(PAST + 1)
     dec_bytes = 2 * kv_len_local * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2
     achieved = dec_bytes / (dec_ms / 1e3) / 1e9
@@ -425,7 +425,9 @@ def run_b200(args, rank, world):
                        "l2": "inputs larger than L2 (4.8 GB of KV per step)",
                        "step_graph": f"one CUDA graph per step, {launches_per_step} kernels"},
             "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "decode_split_mma_kernel + merge_partials_kernel",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("decode_tma_kernel<fused> (RoPE + append + split attention + merge)"
+                                    if step_state.fused else "decode_tma_kernel + merge_partials_kernel"),
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "avg_launch_us": round(dec_ms * 1e3, 3),
@@ -447,6 +449,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sub-measurement")
+    ap.add_argument("--unfused", action="store_true",
+                    help="decode step as the reference's launch sequence (RoPE/append, split, merge) per layer "
+                         "instead of the fused one-kernel-per-layer step")
     ap.add_argument("--prefill-steps", type=int, default=4, help="timed prefill steps (36 layers each)")
     args = ap.parse_args()
     if args.warmup < 3:

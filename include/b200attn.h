@@ -64,8 +64,11 @@ int b2_last_cuda_error(void);            /* cudaError_t of the last B2_ERR_CUDA 
 uint64_t b2_kernel_launch_count(void);   /* kernels this library has launched */
 /* OR of the device-side error bits on the current device: bit 0 = a bounded
  * wait inside a kernel (TMA copy / pipeline barrier) ran out of time and the
- * kernel stopped early. 0 when every kernel completed normally. */
+ * kernel stopped early; bit 1 = a fused decode step got a RoPE position
+ * outside its table. 0 when every kernel completed normally. */
 unsigned int b2_device_error_word(void);
+/* Reset those bits to 0 on the current device (host-synchronous copy). */
+int b2_clear_device_error_word(void);
 
 /* Host-side RoPE tables, include/rope_cache.hpp:49-76 (compute_inverse_frequencies,
  * fill_host_tables): cos/sin[pos][i] = fp16(cos/sin(float(pos) * inv_freq[i])),
@@ -253,6 +256,61 @@ int b2_launch_merge_partials_strided(const float* d_o, const float* d_m, const f
 
 /* d_pos[0] += delta on the stream (one thread), for device-resident positions. */
 int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream);
+
+/* ---- Fused decode step (two kernels per layer) ----------------------------
+ * No single counterpart in the reference: it replaces, for one decode token
+ * of one layer, the reference's launch_rope_and_store_kv
+ * (src/kernels/rope.hip.cpp:138-196) followed by
+ * launch_causal_attention_decode and its merge
+ * (src/kernels/causal_attention.hip.cpp:840-921), i.e. the three nodes per
+ * layer of include/model_inference.hpp:96-123, with one graph-static call:
+ * a split-attention kernel that also does the RoPE and the append, whose
+ * CTAs take 16-token tiles from a shared counter until none are left, then
+ * the merge kernel.
+ *  - kv_len = clamp(d_kv_len[0] + kv_len_bias, 0, max_kv_len), read at launch.
+ *  - Q (d_q, [num_heads][128], before RoPE) is rotated in registers at
+ *    position d_pos[0] when apply_rotation; d_q is read, never written.
+ *  - With d_k_new != NULL the new token's K (rotated when apply_rotation) and
+ *    V ([num_kv_heads][128] each) are written to cache row kv_len - 1 of
+ *    d_k_cache / d_v_cache (packed rows of num_kv_heads * 128) before that
+ *    row is attended. d_k_new == NULL appends nothing (e.g. a rank that does
+ *    not own the newest row).
+ *  - A position outside [0, rope_rows) with apply_rotation appends nothing,
+ *    leaves Q unrotated and sets bit 1 of b2_device_error_word.
+ *  - Output: d_out [num_heads][128] fp16 = the attention of the rotated Q over
+ *    rows [0, kv_len), equal to the reference's launch sequence within
+ *    floating-point reassociation; kv_len 0 writes zeros.
+ *  - head_dim 128, num_kv_heads in {1,2,4,8}, num_heads / num_kv_heads <= 8;
+ *    16-byte aligned pointers. Other shapes return B2_ERR_UNSUPPORTED.
+ *  - d_workspace holds b2_decode_step_workspace_bytes(num_heads) bytes (split
+ *    partials and the tile counter) and must be ZERO-FILLED once before its
+ *    first use; each call leaves the counter at zero again. One workspace
+ *    serves any number of calls ordered on one stream (e.g. every layer of a
+ *    captured step); calls that can overlap on the GPU need separate
+ *    workspaces. */
+size_t b2_decode_step_workspace_bytes(size_t num_heads);
+int b2_launch_decode_step_fused(const void* d_q, const void* d_k_new, const void* d_v_new,
+                                void* d_k_cache, void* d_v_cache,
+                                const void* d_cos, const void* d_sin, size_t rope_rows,
+                                bool apply_rotation, const int32_t* d_pos,
+                                const int32_t* d_kv_len, int32_t kv_len_bias, size_t max_kv_len,
+                                void* d_out, void* d_workspace, size_t workspace_bytes,
+                                size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                b2_stream_t stream);
+
+/* b2_launch_decode_step_fused over this rank's range of the cache, writing the
+ * rank partial of b2_launch_decode_rank_partial_devlen (d_rank_o unnormalised
+ * fp32 [H][128], d_rank_m natural-log max, d_rank_l weight sum) instead of an
+ * fp16 output, for a KV-split decode across GPUs. */
+int b2_launch_decode_step_fused_rank_partial(const void* d_q, const void* d_k_new, const void* d_v_new,
+                                             void* d_k_cache, void* d_v_cache,
+                                             const void* d_cos, const void* d_sin, size_t rope_rows,
+                                             bool apply_rotation, const int32_t* d_pos,
+                                             const int32_t* d_kv_len, int32_t kv_len_bias,
+                                             size_t max_kv_len, float* d_rank_o, float* d_rank_m,
+                                             float* d_rank_l, void* d_workspace, size_t workspace_bytes,
+                                             size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                             b2_stream_t stream);
 
 /* ---- Decode without a caller workspace ------------------------------------
  * No counterpart in the reference (whose decode launchers always take the

@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_last_cuda_error": (I, []),
     "b2_kernel_launch_count": (U64, []),
     "b2_device_error_word": (ctypes.c_uint, []),
+    "b2_clear_device_error_word": (I, []),
     "b2_fill_rope_tables": (I, [S, S, F, P, P]),
     "b2_launch_rope": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
     "b2_launch_rope_and_store_kv": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, S, B, P]),
@@ -48,6 +49,10 @@ SIGNATURES: dict[str, tuple] = {
     "b2_launch_decode_rank_partial_devlen": (I, [P, P, P, P, P, P, P, ctypes.c_int32, S, S, S, S, S, P, P, P, P]),
     "b2_launch_merge_partials_strided": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
     "b2_launch_causal_attention_decode_noalloc": (I, [P, P, P, P, S, S, S, S, S, S, P]),
+    "b2_decode_step_workspace_bytes": (S, [S]),
+    "b2_launch_decode_step_fused": (I, [P, P, P, P, P, P, P, S, B, P, P, ctypes.c_int32, S, P, P, S, S, S, S, P]),
+    "b2_launch_decode_step_fused_rank_partial": (
+        I, [P, P, P, P, P, P, P, S, B, P, P, ctypes.c_int32, S, P, P, P, P, S, S, S, S, P]),
 }
 
 

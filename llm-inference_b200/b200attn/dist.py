@@ -97,10 +97,15 @@ class DecodeStepState:
     """Device-resident positions and workspaces for a graph-static decode step."""
 
     def __init__(self, plan: SplitPlan, num_heads, num_kv_heads, head_dim, num_layers, capacity, max_global,
-                 device):
+                 device, fused=True):
         import torch
         from . import kernels as K
         self.plan = plan
+        # fused: one kernel per layer (RoPE + append + split attention + merge);
+        # otherwise the reference's sequence of RoPE/append, split, merge launches
+        self.fused = fused
+        self.step_ws_bytes = K.decode_step_workspace_bytes(num_heads)
+        self.step_ws = torch.zeros(self.step_ws_bytes, dtype=torch.uint8, device=device)
         self.H, self.KVH, self.D, self.L = num_heads, num_kv_heads, head_dim, num_layers
         self.capacity = capacity
         self.max_global = max_global
@@ -143,6 +148,21 @@ def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stre
         rotate = (l + 1) % 4 != 0          # include/model_inference.hpp:272 NoPE rule
         row = qkv[l]
         q, k, v = row, row[q_dim:], row[q_dim + kv_dim:]
+        if st.fused:
+            kn, vn = (k, v) if plan.is_tail else (None, None)
+            kc, vc = cache.get_k_cache(l), cache.get_v_cache(l)
+            if plan.world == 1:
+                K.launch_decode_step_fused(q, kn, vn, kc, vc, d_cos, d_sin, st.max_global, rotate, st.pos, src, bias,
+                                           st.capacity, out[l], st.step_ws, st.step_ws_bytes, H, KVH, D,
+                                           stream=stream)
+                continue
+            part = st.rank_part[l]
+            K.launch_decode_step_fused_rank_partial(q, kn, vn, kc, vc, d_cos, d_sin, st.max_global, rotate, st.pos,
+                                                    src, bias, st.capacity, part[:H * D], part[H * D:H * D + H],
+                                                    part[H * D + H:], st.step_ws, st.step_ws_bytes, H, KVH, D,
+                                                    stream=stream)
+            _exchange_and_merge(st, l, part, out, group, stream)
+            continue
         if plan.is_tail:
             # cache rows are local: global position p lives at local row p - begin
             kc = cache.get_k_cache(l)
@@ -164,14 +184,22 @@ def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stre
             K.launch_decode_rank_partial_devlen(q, cache.get_k_cache(l), cache.get_v_cache(l), st.po, st.pm, st.pl,
                                                 src, bias, st.capacity, H, KVH, D, kv_dim, part[:H * D],
                                                 part[H * D:H * D + H], part[H * D + H:], stream=stream)
-            import torch.distributed as tdist
-            with torch.cuda.stream(stream if isinstance(stream, torch.cuda.Stream) else torch.cuda.current_stream()):
-                tdist.all_gather_into_tensor(st.gathered[l], part, group=group)
-            per = H * (D + 2)
-            g = st.gathered[l]
-            K.launch_merge_partials_strided(g, g[H * D:], g[H * D + H:], out[l], H, plan.world, D, per, D, per, 1,
-                                            stream=stream)
+            _exchange_and_merge(st, l, part, out, group, stream)
     K.advance_position(st.pos, 1, stream=stream)
+
+
+def _exchange_and_merge(st: DecodeStepState, l, part, out, group, stream):
+    """All-gather every rank's (o, m, l) partial of layer l and merge them into out[l]."""
+    import torch
+    import torch.distributed as tdist
+    from . import kernels as K
+    H, D = st.H, st.D
+    with torch.cuda.stream(stream if isinstance(stream, torch.cuda.Stream) else torch.cuda.current_stream()):
+        tdist.all_gather_into_tensor(st.gathered[l], part, group=group)
+    per = H * (D + 2)
+    g = st.gathered[l]
+    K.launch_merge_partials_strided(g, g[H * D:], g[H * D + H:], out[l], H, st.plan.world, D, per, D, per, 1,
+                                    stream=stream)
 
 
 def max_over_ranks(value: float, device) -> float:
@@ -182,13 +210,16 @@ def max_over_ranks(value: float, device) -> float:
     return float(t.item())
 
 
-def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3) -> float:
-    """Average device time (ms) of one decode launch (split + merge) over the
-    local range at kv_len = past + 1, measured with CUDA events on its stream,
-    cycling through the layers so the cache is not L2-resident."""
+def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3, d_cos=None, d_sin=None) -> float:
+    """Average device time (ms) of one layer's decode launch over the local
+    range at kv_len = past + 1 -- the fused step kernel when st.fused (RoPE,
+    append of the same row each time, attention, merge), else split + merge --
+    measured with CUDA events on its stream, cycling through the layers so the
+    cache is not L2-resident."""
     import torch
     from . import kernels as K
     H, KVH, D = st.H, st.KVH, st.D
+    q_dim, kv_dim = H * D, KVH * D
     src, bias = st.kv_len_source()
     st.reset_position(st.plan.past)
     torch.cuda.synchronize()
@@ -197,10 +228,25 @@ def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3) -
     i = 0
     for _ in range(reps):
         for l in range(st.L):
+            row = qkv[l]
             starts[i].record(stream)
-            K.launch_causal_attention_decode_devlen(qkv[l], cache.get_k_cache(l), cache.get_v_cache(l), out[l],
-                                                    st.po, st.pm, st.pl, src, bias, st.capacity, H, KVH, D,
-                                                    KVH * D, stream=stream)
+            if st.fused:
+                kn, vn = (row[q_dim:], row[q_dim + kv_dim:]) if st.plan.is_tail else (None, None)
+                rotate = (l + 1) % 4 != 0
+                if st.plan.world == 1:
+                    K.launch_decode_step_fused(row, kn, vn, cache.get_k_cache(l), cache.get_v_cache(l), d_cos, d_sin,
+                                               st.max_global, rotate, st.pos, src, bias, st.capacity, out[l],
+                                               st.step_ws, st.step_ws_bytes, H, KVH, D, stream=stream)
+                else:
+                    part = st.rank_part[l]
+                    K.launch_decode_step_fused_rank_partial(
+                        row, kn, vn, cache.get_k_cache(l), cache.get_v_cache(l), d_cos, d_sin, st.max_global, rotate,
+                        st.pos, src, bias, st.capacity, part[:H * D], part[H * D:H * D + H], part[H * D + H:],
+                        st.step_ws, st.step_ws_bytes, H, KVH, D, stream=stream)
+            else:
+                K.launch_causal_attention_decode_devlen(row, cache.get_k_cache(l), cache.get_v_cache(l), out[l],
+                                                        st.po, st.pm, st.pl, src, bias, st.capacity, H, KVH, D,
+                                                        kv_dim, stream=stream)
             ends[i].record(stream)
             i += 1
     torch.cuda.synchronize()

@@ -25,6 +25,7 @@ __all__ = [
     "decode_workspace_floats", "kernel_launch_count", "launch_rope_and_store_kv_devpos",
     "launch_causal_attention_decode_devlen", "advance_position", "launch_decode_rank_partial_devlen",
     "launch_merge_partials_strided", "launch_causal_attention_prefill_batched",
+    "decode_step_workspace_bytes", "launch_decode_step_fused", "launch_decode_step_fused_rank_partial",
 ]
 
 
@@ -184,6 +185,38 @@ def launch_causal_attention_decode_devlen(d_q, d_k_cache, d_v_cache, d_out, d_pa
 
 def advance_position(d_pos, delta=1, stream=None):
     check(lib().b2_advance_position(_ptr(d_pos), int(delta), _stream(stream)), "advance_position")
+
+
+# ---- Fused decode step ----------------------------------------------------------
+
+def decode_step_workspace_bytes(num_heads):
+    """Bytes of the (zero-filled once) workspace of launch_decode_step_fused."""
+    return int(lib().b2_decode_step_workspace_bytes(num_heads))
+
+
+def launch_decode_step_fused(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows, apply_rotation,
+                             d_pos, d_kv_len, kv_len_bias, max_kv_len, d_out, d_workspace, workspace_bytes,
+                             num_heads, num_kv_heads, head_dim, stream=None):
+    """One layer's decode step in one kernel: RoPE of the new token, its K/V
+    append at row kv_len - 1, split attention and merge (rope.hip.cpp:138-196 +
+    causal_attention.hip.cpp:840-921). d_k_new None appends nothing."""
+    check(lib().b2_launch_decode_step_fused(
+        _ptr(d_q), _ptr(d_k_new), _ptr(d_v_new), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_cos), _ptr(d_sin),
+        rope_rows, bool(apply_rotation), _ptr(d_pos), _ptr(d_kv_len), int(kv_len_bias), max_kv_len, _ptr(d_out),
+        _ptr(d_workspace), workspace_bytes, num_heads, num_kv_heads, head_dim, _stream(stream)),
+        "launch_decode_step_fused")
+
+
+def launch_decode_step_fused_rank_partial(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows,
+                                          apply_rotation, d_pos, d_kv_len, kv_len_bias, max_kv_len, d_rank_o,
+                                          d_rank_m, d_rank_l, d_workspace, workspace_bytes, num_heads,
+                                          num_kv_heads, head_dim, stream=None):
+    """launch_decode_step_fused writing this rank's (o, m, l) partial instead of fp16 output."""
+    check(lib().b2_launch_decode_step_fused_rank_partial(
+        _ptr(d_q), _ptr(d_k_new), _ptr(d_v_new), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_cos), _ptr(d_sin),
+        rope_rows, bool(apply_rotation), _ptr(d_pos), _ptr(d_kv_len), int(kv_len_bias), max_kv_len,
+        _ptr(d_rank_o), _ptr(d_rank_m), _ptr(d_rank_l), _ptr(d_workspace), workspace_bytes, num_heads,
+        num_kv_heads, head_dim, _stream(stream)), "launch_decode_step_fused_rank_partial")
 
 
 # ---- KV-split decode across ranks --------------------------------------------

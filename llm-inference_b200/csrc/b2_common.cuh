@@ -21,6 +21,8 @@ void count_launch(uint64_t n = 1);
 // Device error words of the translation units with bounded waits.
 unsigned int device_error_decode();
 unsigned int device_error_prefill();
+int clear_device_error_decode();
+int clear_device_error_prefill();
 
 // Turn the launch status of the kernel just enqueued into a b2 status.
 inline int launch_status() {

@@ -15,6 +15,7 @@ namespace b2 {
 static __device__ unsigned int g_device_error = 0;
 
 constexpr unsigned int kErrWaitTimeout = 1u;
+constexpr unsigned int kErrBadPosition = 2u;  // fused decode step: RoPE position outside the table
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -82,6 +83,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (a hint: no completion, no
+// effect on correctness). src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 policy for data read exactly once (streamed KV).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;
@@ -107,6 +114,11 @@ __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontro
 // Named barrier over a subset of warps (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) { named_barrier(id, threads); }
+// Arrive without waiting (the other side syncs).
+__device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace b2

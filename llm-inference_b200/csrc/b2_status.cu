@@ -73,6 +73,11 @@ uint64_t b2_kernel_launch_count(void) { return b2::g_launches.load(); }
 
 unsigned int b2_device_error_word(void) { return b2::device_error_decode() | b2::device_error_prefill(); }
 
+int b2_clear_device_error_word(void) {
+    const int st = b2::clear_device_error_decode();
+    return st != B2_OK ? st : b2::clear_device_error_prefill();
+}
+
 int b2_fill_rope_tables(size_t max_seq_len, size_t head_dim, float rope_theta,
                         uint16_t* host_cos, uint16_t* host_sin) {
     if (head_dim == 0 || (head_dim & 1) || host_cos == nullptr || host_sin == nullptr)

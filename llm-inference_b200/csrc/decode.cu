@@ -48,6 +48,7 @@
 #include "b2_common.cuh"
 #include "b2_ptx.cuh"
 #include "decode_tile.cuh"
+#include "tcgen05.cuh"
 
 namespace b2 {
 namespace {
@@ -57,7 +58,7 @@ constexpr uint32_t kNoCap = 0xffffffffu;
 // TMA kernel shape
 constexpr int kTmaConsumers = 12;  // 3 per KV head at 4 KV heads; 13 warps <= 4 per sub-partition
 constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
-constexpr uint32_t kTmaSmemBudget = 192 * 1024;
+constexpr uint32_t kTmaSmemBudget = 200 * 1024;
 
 struct DecodeArgs {
     const __half* q;
@@ -125,26 +126,278 @@ __device__ __forceinline__ Extent decode_extent(const A& a) {
 }
 
 // ---------------------------------------------------------------------------
-// Persistent TMA split kernel. grid = min(#SMs, chunks), block = 13 warps.
-__global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const DecodeArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+// Fused decode step (graph-static): extra inputs of decode_tma_kernel<true>.
+struct StepExt {
+    const __half* q_new;     // the new token's Q, not rotated, [H][128]
+    const __half* k_new;     // its K (not rotated) [KVH][128]; nullptr = no append on this rank
+    const __half* v_new;     // its V [KVH][128]
+    __half* k_cache;         // writable views of the cache (the append target)
+    __half* v_cache;
+    const __half* cos;       // RoPE tables [table_rows][64]
+    const __half* sin;
+    const int32_t* pos_dev;  // RoPE position of the new token
+    uint32_t rotate;         // 1 = RoPE, 0 = NoPE layer
+    uint32_t table_rows;
+    uint32_t* counters;      // [0] next unclaimed tile, [1] CTAs done, [2] merges done; 0 at launch
+    __half* out;             // [H][128] fp16 result, or the rank partial below
+    float* rank_o;
+    float* rank_m;
+    float* rank_l;
+};
+
+constexpr uint32_t kStepMaxSplits = 256;      // partial slots in a fused-step workspace
+
+// Rotate 8 pairs (x[i..i+8), x[i+64..i+72)) with fp32 products and sums rounded
+// separately, as the RoPE kernel and the CPU oracle do.
+__device__ __forceinline__ void rot8_pairs(uint4& lo, uint4& hi, uint4 cv, uint4 sv) {
+    uint32_t* L = reinterpret_cast<uint32_t*>(&lo);
+    uint32_t* Hh = reinterpret_cast<uint32_t*>(&hi);
+    const uint32_t* C = reinterpret_cast<const uint32_t*>(&cv);
+    const uint32_t* S = reinterpret_cast<const uint32_t*>(&sv);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&L[w]));
+        const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&Hh[w]));
+        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&C[w]));
+        const float2 sn = __half22float2(*reinterpret_cast<const __half2*>(&S[w]));
+        const float a0 = __fsub_rn(__fmul_rn(x0.x, c.x), __fmul_rn(x1.x, sn.x));
+        const float a1 = __fsub_rn(__fmul_rn(x0.y, c.y), __fmul_rn(x1.y, sn.y));
+        const float b0 = __fadd_rn(__fmul_rn(x1.x, c.x), __fmul_rn(x0.x, sn.x));
+        const float b1 = __fadd_rn(__fmul_rn(x1.y, c.y), __fmul_rn(x0.y, sn.y));
+        L[w] = pack_half2(a0, a1);
+        Hh[w] = pack_half2(b0, b1);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent TMA split kernel. grid = min(#SMs, chunks), block = 13 warps: a
+// producer warp streams 16-token K and V tiles with tensor-map copies
+// (column block by column block, 128-byte swizzled) into a ring of stages;
+// 12 consumer warps (KV head x tile parity) run the MMA tile math; the CTA's
+// states are combined into one (o, m, l) partial per head.
+// Static (reference launchers): CTA `split` owns a contiguous token range.
+// kFused (the fused decode step): CTAs claim tiles from a global counter, so
+// all CTAs finish together whatever their DRAM share; Q is rotated in
+// registers, and the CTA that claims the tile holding row kv_len - 1 appends
+// the new token's K/V there before copying that tile.
+// ---- in-kernel merge of the fused step -------------------------------------
+constexpr uint32_t kStepBatch = 12;  // partials one warp loads at once
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void step_store(const StepExt& x, uint32_t h, uint32_t d, float o, float M, float L) {
+    if (x.rank_o) {
+        x.rank_o[h * 128 + d] = o;
+        if (d == 0) {
+            x.rank_m[h] = M;
+            x.rank_l[h] = L;
+        }
+    } else {
+        x.out[h * 128 + d] = __float2half_rn(o / L);
+    }
+}
+
+__device__ __forceinline__ void step_write_empty(uint32_t H, const StepExt& x, uint32_t tid, uint32_t nthreads) {
+    for (uint32_t i = tid; i < H * 128; i += nthreads) {
+        if (x.rank_o) {
+            x.rank_o[i] = 0.f;
+            if ((i & 127) == 0) {
+                x.rank_m[i >> 7] = -INFINITY;
+                x.rank_l[i >> 7] = 0.f;
+            }
+        } else {
+            x.out[i] = __float2half_rn(0.f);
+        }
+    }
+}
+
+// Every CTA has written its partials [H][S][128] / [H][S] (natural-log m).
+// The last R = min(S, H) CTAs to arrive each merge the heads r, r + R, ... of
+// all S partials once the remaining CTAs have arrived; every CTA they wait for
+// has already started, so the wait needs no co-residency beyond R CTAs. Warp w
+// of a merging CTA folds partials w, w + 13, ... for 4 dims per lane; the 13
+// warp states meet in shared memory `wsm` (13 x 132 floats). The last merging
+// CTA resets the counters for the next launch.
+__device__ __noinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, float* wsm) {
+    __shared__ uint32_t role_s;
+    const uint32_t H = a.num_heads;
+    const uint32_t R = min(S, H);
+    __threadfence();  // this thread's partial stores, before the arrival below
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t k = atomicAdd(&x.counters[1], 1u);
+        role_s = k + R >= S ? k + R - S : 0xffffffffu;
+    }
+    __syncthreads();
+    const uint32_t r = role_s;
+    if (r == 0xffffffffu) return;
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = global_timer_ns();
+        while (ld_acquire_gpu(&x.counters[1]) < S) {
+            if (global_timer_ns() - t0 > kWaitBudgetNs) {
+                atomicOr(&g_device_error, kErrWaitTimeout);
+                role_s = 0xffffffffu;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    if (role_s == 0xffffffffu) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int kWarps = kTmaThreads / 32;
+    for (uint32_t h = r; h < H; h += R) {
+        const float* po = a.po + static_cast<uint64_t>(h) * S * 128 + lane * 4;
+        const float* pm = a.pm + static_cast<uint64_t>(h) * S;
+        const float* pl = a.pl + static_cast<uint64_t>(h) * S;
+        float M = -INFINITY, L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t base = warp; base < S; base += kWarps * kStepBatch) {
+            float mv[kStepBatch], lv[kStepBatch];
+            float4 ov[kStepBatch];
+#pragma unroll
+            for (uint32_t u = 0; u < kStepBatch; ++u) {
+                const uint32_t c = base + u * kWarps;
+                mv[u] = c < S ? __ldcg(pm + c) : -INFINITY;
+                lv[u] = c < S ? __ldcg(pl + c) : 0.f;
+                ov[u] = c < S ? __ldcg(reinterpret_cast<const float4*>(po + static_cast<uint64_t>(c) * 128))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            float bm = M;
+#pragma unroll
+            for (uint32_t u = 0; u < kStepBatch; ++u) bm = fmaxf(bm, mv[u]);
+            if (bm == -INFINITY) continue;
+            const float sc = M == -INFINITY ? 0.f : expf(M - bm);
+            acc.x *= sc;
+            acc.y *= sc;
+            acc.z *= sc;
+            acc.w *= sc;
+            L *= sc;
+            M = bm;
+#pragma unroll
+            for (uint32_t u = 0; u < kStepBatch; ++u) {
+                const float w = mv[u] == -INFINITY ? 0.f : expf(mv[u] - M);
+                acc.x = fmaf(w, ov[u].x, acc.x);
+                acc.y = fmaf(w, ov[u].y, acc.y);
+                acc.z = fmaf(w, ov[u].z, acc.z);
+                acc.w = fmaf(w, ov[u].w, acc.w);
+                L = fmaf(w, lv[u], L);
+            }
+        }
+        constexpr uint32_t kPitch = 132;  // floats per warp state: o[128], M, L (16-byte rows)
+        float* mine = wsm + warp * kPitch;
+        *reinterpret_cast<float4*>(mine + lane * 4) = acc;
+        if (lane == 0) {
+            mine[128] = M;
+            mine[129] = L;
+        }
+        __syncthreads();
+        if (threadIdx.x < 128) {
+            const uint32_t d = threadIdx.x;
+            float Mx = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) Mx = fmaxf(Mx, wsm[w * kPitch + 128]);
+            float O = 0.f, Lx = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float m = wsm[w * kPitch + 128];
+                const float sc = m == -INFINITY ? 0.f : expf(m - Mx);
+                O = fmaf(sc, wsm[w * kPitch + d], O);
+                Lx = fmaf(sc, wsm[w * kPitch + 129], Lx);
+            }
+            step_store(x, h, d, O, Mx, Lx);
+        }
+        __syncthreads();
+    }
+    // the last merging CTA leaves the counters at zero for the next launch
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&x.counters[2], 1u) == R - 1) {
+            x.counters[0] = 0u;
+            x.counters[1] = 0u;
+            x.counters[2] = 0u;
+        }
+    }
+}
+
+constexpr uint32_t kAppendBarrier = 1;  // named barrier: appending consumer warp -> producer warp
+constexpr uint32_t kPrefetchTiles = 8;  // tiles per CTA warmed in L2 before the dependency wait
+
+// Fused kernel: tiles dealt out evenly to each split before the claimed pool.
+__device__ __forceinline__ uint32_t fused_share(uint32_t total_tiles, uint32_t splits) {
+    return (total_tiles * 4 / 5) / splits;
+}
+
+__device__ __forceinline__ bool split_index_ok(const Extent& e, uint32_t split) { return split < e.splits; }
+
+// The first tiles a split streams (up to kPrefetchTiles): its own range
+// (static) or its even share (fused).
+__device__ __forceinline__ void own_tiles(const Extent& e, uint32_t split, bool fused, uint32_t& first,
+                                          uint32_t& count) {
+    if (fused) {
+        const uint32_t per = fused_share((e.kv_len + kTile - 1) / kTile, e.splits);
+        first = split * per;
+        count = min(per, kPrefetchTiles);
+    } else {
+        uint32_t b, en;
+        split_range(e.kv_len, e.splits, split, b, en);
+        first = b / kTile;
+        // whole tiles only: a partial last tile could run past the cache
+        count = min((en - b) / kTile, kPrefetchTiles);
+    }
+}
+
+__device__ __forceinline__ uint8_t* stg_of(uint8_t* ring, uint32_t s, uint32_t tile_bytes) {
+    return ring + s * 2 * tile_bytes;
+}
+
+template <bool kFused, uint32_t KVH>
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    decode_tma_kernel(const DecodeArgs a, const StepExt x, const __grid_constant__ CUtensorMap map_k,
+                      const __grid_constant__ CUtensorMap map_v) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint32_t stage_valid[32];  // kFused: rows of the tile in each stage, 0 = no more tiles
+    constexpr uint32_t row_bytes = KVH * 256;          // one token, all KV heads
+    constexpr uint32_t tile_bytes = kTile * row_bytes; // per K (and per V): [2*KVH blocks][16 rows][128 B]
+    if (threadIdx.x >= kTmaConsumers * 32 && threadIdx.x < kTmaConsumers * 32 + 2 * kPrefetchTiles) {
+        // While the previous kernel finishes, start pulling this CTA's first
+        // tiles into L2. The length read here may be stale (it can be the
+        // previous kernel's output); a prefetch only warms L2, so any tile
+        // below max_kv_len is harmless.
+        const Extent pre = decode_extent(a);
+        if (split_index_ok(pre, blockIdx.x)) {
+            uint32_t first, count;
+            own_tiles(pre, blockIdx.x, kFused, first, count);
+            const uint32_t j = (threadIdx.x - kTmaConsumers * 32) >> 1;
+            if (j < count) {
+                const uint64_t off = static_cast<uint64_t>(first + j) * tile_bytes;
+                bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((threadIdx.x & 1) ? a.v : a.k) + off, tile_bytes);
+            }
+        }
+    }
     pdl_wait_primary();  // Q, the cache and the device length may come from the previous kernel
     pdl_launch_dependents();
     const Extent ext = decode_extent(a);
     const uint32_t split = blockIdx.x;
+    if (kFused && ext.splits == 0) {  // empty cache: defined output
+        if (split == 0) step_write_empty(a.num_heads, x, threadIdx.x, blockDim.x);
+        return;
+    }
     if (split >= ext.splits) return;
     uint32_t begin, end;
     split_range(ext.kv_len, ext.splits, split, begin, end);
 
-    const uint32_t KVH = a.num_kv_heads;
-    const uint32_t row_bytes = KVH * 256;            // one token, all KV heads
-    const uint32_t tile_bytes = kTile * row_bytes;   // per K (and per V)
     const uint32_t stages = a.stages;
-    uint8_t* ring = smem;                            // [stages][K tile | V tile]
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * 2 * tile_bytes);
+    // 128-byte swizzled TMA boxes want 1024-byte aligned destinations
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * 2 * tile_bytes);
     uint64_t* empty = full + stages;
     const uint32_t ntiles = (end - begin + kTile - 1) / kTile;
-    const uint32_t npar = kTmaConsumers / KVH;       // consumer warps per KV head; divides `stages`
+    constexpr uint32_t npar = kTmaConsumers / KVH;     // consumer warps per KV head; divides `stages`
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -156,31 +409,117 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
     }
     __syncthreads();
 
+    int32_t pos = 0;
+    bool rope_ok = true;
+    if (kFused) {
+        if (x.pos_dev != nullptr) pos = __ldg(x.pos_dev);
+        rope_ok = !x.rotate || (pos >= 0 && static_cast<uint32_t>(pos) < x.table_rows);
+        if (!rope_ok && split == 0 && threadIdx.x == 0) atomicOr(&g_device_error, kErrBadPosition);
+    }
+
     bool ok = true;
     WarpState st;
     state_init(st);
     if (warp == kTmaConsumers) {
-        // ---- producer
+        // ---- producer warp
         if (lane == 0) {
-            const uint64_t policy = l2_evict_first_policy();
-            const uint8_t* kg = reinterpret_cast<const uint8_t*>(a.k);
-            const uint8_t* vg = reinterpret_cast<const uint8_t*>(a.v);
-            uint32_t issued = 0;
-            for (uint32_t i = 0; i < ntiles; ++i) {
+            tc::prefetch_tensormap(&map_k);
+            tc::prefetch_tensormap(&map_v);
+        }
+        const uint64_t policy = l2_evict_first_policy();
+        uint32_t i = 0;
+        if constexpr (kFused) {
+            // Tile order of split s: its even share [s*per, (s+1)*per) of ~4/5
+            // of the tiles (the last split puts the last tile, which holds the
+            // new row, after its first two, once consumer warp 0 has appended
+            // the row), then tiles of the pool
+            // [S*per, total - 1), claimed kClaim at a time from the counter with
+            // the next claim in flight while the current one streams, so CTAs
+            // that run ahead take more.
+            constexpr uint32_t kClaim = 2;
+            const uint32_t total = (ext.kv_len + kTile - 1) / kTile;
+            const uint32_t per = fused_share(total, ext.splits);  // per * S <= total - 1
+            const uint32_t pool = per * ext.splits, pool_end = total - 1;
+            const bool tail_split = split + 1 == ext.splits;
+            uint32_t own = split * per, own_end = own + per;
+            uint32_t claimed = lane == 0 && pool < pool_end ? atomicAdd(&x.counters[0], kClaim) : 0u;
+            bool tail_pending = tail_split;
+            const uint32_t tail_at = min(2u, per);
+            uint32_t cur = 0, cur_left = 0;
+            for (;; ++i) {
+                uint32_t tile;
+                if (tail_pending && i == tail_at) {
+                    tile = total - 1;
+                    tail_pending = false;
+                    // consumer warp 0 appends the new row (generic stores + proxy
+                    // fence) and arrives here before this tile is copied
+                    if (x.k_new != nullptr && rope_ok) named_barrier_sync(kAppendBarrier, 64);
+                } else if (own < own_end) {
+                    tile = own++;
+                } else {
+                    if (cur_left == 0) {
+                        cur = pool + __shfl_sync(0xffffffffu, claimed, 0);
+                        cur_left = cur < pool_end ? min(kClaim, pool_end - cur) : 0u;
+                        if (lane == 0 && cur_left != 0) claimed = atomicAdd(&x.counters[0], kClaim);
+                    }
+                    tile = cur_left != 0 ? cur++ : total;
+                    if (cur_left != 0) --cur_left;
+                }
                 const uint32_t s = i % stages, round = i / stages;
-                if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1))) break;
-                const uint32_t t0 = begin + i * kTile;
-                const uint32_t rows = min(static_cast<uint32_t>(kTile), end - t0);
-                const uint32_t bytes = rows * row_bytes;
-                uint8_t* st = ring + s * 2 * tile_bytes;
-                mbar_arrive_expect_tx(&full[s], 2 * bytes);
-                bulk_g2s(st, kg + static_cast<uint64_t>(t0) * row_bytes, bytes, &full[s], policy);
-                bulk_g2s(st + tile_bytes, vg + static_cast<uint64_t>(t0) * row_bytes, bytes, &full[s], policy);
-                issued = i + 1;
+                if (tile >= total) {
+                    // no tiles left: one empty stage per consumer parity ends its loop
+                    for (uint32_t e = 0; e < npar; ++e, ++i) {
+                        const uint32_t se = i % stages, re = i / stages;
+                        if (lane == 0) {
+                            if (re > 0 && !mbar_wait(&empty[se], (re - 1) & 1)) ok = false;
+                            stage_valid[se] = 0;
+                            mbar_arrive(&full[se]);
+                        }
+                    }
+                    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                    break;
+                }
+                const uint32_t t0 = tile * kTile;
+                bool w_ok = true;
+                if (lane == 0 && round > 0) w_ok = mbar_wait(&empty[s], (round - 1) & 1);
+                if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    stage_valid[s] = min(static_cast<uint32_t>(kTile), ext.kv_len - t0);
+                    mbar_arrive_expect_tx(&full[s], 2 * tile_bytes);
+                    tc::tma_load_3d_hint(stg_of(ring, s, tile_bytes), &map_k, 0, static_cast<int32_t>(t0), 0,
+                                         &full[s], policy);
+                    tc::tma_load_3d_hint(stg_of(ring, s, tile_bytes) + tile_bytes, &map_v, 0,
+                                         static_cast<int32_t>(t0), 0, &full[s], policy);
+                }
+                __syncwarp();
             }
-            // Never leave the CTA with copies in flight into its shared memory:
-            // the last `stages` issued tiles are awaited (immediate when the
-            // consumers already drained them).
+        } else {
+            for (; i < ntiles; ++i) {
+                const uint32_t s = i % stages, round = i / stages;
+                bool w_ok = true;
+                if (lane == 0 && round > 0) w_ok = mbar_wait(&empty[s], (round - 1) & 1);
+                if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                const int32_t t0 = static_cast<int32_t>(begin + i * kTile);
+                if (lane == 0) {
+                    // whole boxes: rows past the tensor's end arrive zero-filled, rows
+                    // past this split's end are masked by the consumers
+                    mbar_arrive_expect_tx(&full[s], 2 * tile_bytes);
+                    tc::tma_load_3d_hint(stg_of(ring, s, tile_bytes), &map_k, 0, t0, 0, &full[s], policy);
+                    tc::tma_load_3d_hint(stg_of(ring, s, tile_bytes) + tile_bytes, &map_v, 0, t0, 0, &full[s],
+                                         policy);
+                }
+                __syncwarp();
+            }
+        }
+        const uint32_t issued = i;
+        // Never leave the CTA with copies in flight into its shared memory.
+        if (lane == 0) {
             const uint32_t first = issued > stages ? issued - stages : 0;
             for (uint32_t i = first; i < issued; ++i) (void)mbar_wait(&full[i % stages], (i / stages) & 1);
         }
@@ -188,30 +527,91 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
         // ---- consumers: warp = KV head (warp % KVH) x tile parity (warp / KVH)
         const uint32_t kvh = warp % KVH, par = warp / KVH;
         const int g = lane >> 2, t = lane & 3;
+        if constexpr (kFused) {
+            if (warp == 0 && split + 1 == ext.splits && x.k_new != nullptr && rope_ok) {
+                // append the new token at row kv_len - 1; the producer copies
+                // that row's tile only after the barrier below
+                const uint32_t last_row = ext.kv_len - 1;
+                const uint64_t row = static_cast<uint64_t>(last_row) * a.kv_stride;
+                for (uint32_t gi = lane; gi < KVH * 8; gi += 32) {
+                    const uint32_t h = gi >> 3, e = (gi & 7) * 8;
+                    uint4 lo = *reinterpret_cast<const uint4*>(x.k_new + h * 128 + e);
+                    uint4 hi = *reinterpret_cast<const uint4*>(x.k_new + h * 128 + 64 + e);
+                    if (x.rotate) {
+                        const uint64_t ti = static_cast<uint64_t>(pos) * 64 + e;
+                        rot8_pairs(lo, hi, *reinterpret_cast<const uint4*>(x.cos + ti),
+                                   *reinterpret_cast<const uint4*>(x.sin + ti));
+                    }
+                    *reinterpret_cast<uint4*>(x.k_cache + row + h * 128 + e) = lo;
+                    *reinterpret_cast<uint4*>(x.k_cache + row + h * 128 + 64 + e) = hi;
+                    *reinterpret_cast<uint4*>(x.v_cache + row + h * 128 + e) =
+                        *reinterpret_cast<const uint4*>(x.v_new + h * 128 + e);
+                    *reinterpret_cast<uint4*>(x.v_cache + row + h * 128 + 64 + e) =
+                        *reinterpret_cast<const uint4*>(x.v_new + h * 128 + 64 + e);
+                }
+                // the producer's tensor copies (async proxy) must see these stores
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                named_barrier_arrive(kAppendBarrier, 64);
+            }
+        }
         uint32_t qf[8][2];
-        load_q_frags(a.q, kvh, a.group, g, t, qf);
+        {
+            // Q of the new token (rotated in registers by the fused step; pairs
+            // (e, e+64) sit in words j and j+2)
+            if (static_cast<uint32_t>(g) < a.group) {
+                const __half* qrow = (kFused ? x.q_new : a.q) + static_cast<uint64_t>(kvh * a.group + g) * 128;
+                uint4 w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint4*>(qrow + 32 * j + 8 * t);
+                if (kFused && x.rotate && rope_ok) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const uint64_t ti = static_cast<uint64_t>(pos) * 64 + 32 * j + 8 * t;
+                        rot8_pairs(w[j], w[j + 2], *reinterpret_cast<const uint4*>(x.cos + ti),
+                                   *reinterpret_cast<const uint4*>(x.sin + ti));
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    qf[2 * j][0] = w[j].x;
+                    qf[2 * j][1] = w[j].y;
+                    qf[2 * j + 1][0] = w[j].z;
+                    qf[2 * j + 1][1] = w[j].w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) qf[j][0] = qf[j][1] = 0u;
+            }
+        }
         // warps past KVH * npar (8 KV heads: 4 of 12) have no tiles
-        for (uint32_t i = par; par < npar && i < ntiles; i += npar) {
+        for (uint32_t i = par; par < npar; i += npar) {
+            if (!kFused && i >= ntiles) break;
             const uint32_t s = i % stages, round = i / stages;
             if (!mbar_wait(&full[s], round & 1)) {
                 ok = false;
                 break;
             }
-            const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * 256;
+            uint32_t valid;
+            if constexpr (kFused) {
+                valid = stage_valid[s];
+                if (valid == 0) break;  // the producer ran out of tiles
+            } else {
+                valid = min(static_cast<uint32_t>(kTile), end - (begin + i * kTile));
+            }
+            const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * (2 * kTile * 128);
             const uint8_t* vt = kt + tile_bytes;
-            const uint32_t valid = min(static_cast<uint32_t>(kTile), end - (begin + i * kTile));
             float sc[4];
             uint4 va[4][2];
             if (valid == kTile) {
                 uint4 ka[4], kb[4];
-                load_k_frags<false>(kt, row_bytes, g, t, valid, ka, kb);
-                tile_scores<false>(sc, ka, kb, qf, g, valid, a.scale_log2);
-                load_v_frags<false>(vt, row_bytes, g, t, valid, va);
+                load_k_frags_sw<false>(kt, g, t, valid, ka, kb);
+                tile_scores<false>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
+                load_v_frags_sw<false>(vt, g, t, valid, va);
             } else {
                 uint4 ka[4], kb[4];
-                load_k_frags<true>(kt, row_bytes, g, t, valid, ka, kb);
-                tile_scores<true>(sc, ka, kb, qf, g, valid, a.scale_log2);
-                load_v_frags<true>(vt, row_bytes, g, t, valid, va);
+                load_k_frags_sw<true>(kt, g, t, valid, ka, kb);
+                tile_scores<true>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
+                load_v_frags_sw<true>(vt, g, t, valid, va);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);  // the stage can be refilled
@@ -230,6 +630,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_split_tma_kernel(const 
     combine_tile_any(npar, sm_m, sm_l, sm_o, KVH, a.group, split, ext.splits, a.po, a.pm, a.pl, threadIdx.x,
                      kTmaThreads);
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
+    if constexpr (kFused) step_merge(a, x, ext.splits, reinterpret_cast<float*>(ring));
 }
 
 // ---------------------------------------------------------------------------
@@ -470,10 +871,11 @@ __global__ void advance_position_kernel(int32_t* pos, int32_t delta) {
 }
 
 const void* const kSplitKernels[] = {
-    reinterpret_cast<const void*>(decode_split_tma_kernel),
-    reinterpret_cast<const void*>(decode_split_mma_kernel),
-    reinterpret_cast<const void*>(decode_split_simt_kernel),
+    reinterpret_cast<const void*>(decode_tma_kernel<false, 1>), reinterpret_cast<const void*>(decode_tma_kernel<false, 2>),
+    reinterpret_cast<const void*>(decode_tma_kernel<false, 4>), reinterpret_cast<const void*>(decode_tma_kernel<false, 8>),
+    reinterpret_cast<const void*>(decode_split_mma_kernel),    reinterpret_cast<const void*>(decode_split_simt_kernel),
 };
+constexpr int kNumTmaKernels = 4;  // the first entries of kSplitKernels take (DecodeArgs, StepExt)
 const void* const kMergeKernels[] = {reinterpret_cast<const void*>(merge_partials_kernel)};
 
 // ---------------------------------------------------------------------------
@@ -493,11 +895,83 @@ int ensure_tma_smem() {
     if (cudaGetDevice(&dev) != cudaSuccess) return B2_ERR_CUDA;
     const uint64_t bit = 1ull << (dev & 63);
     if (done_mask.load() & bit) return B2_OK;
-    const int st = cuda_status(cudaFuncSetAttribute(decode_split_tma_kernel,
-                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    static_cast<int>(kTmaSmemBudget + 1024)));
-    if (st == B2_OK) done_mask.fetch_or(bit);
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(decode_tma_kernel<false, 1>), reinterpret_cast<const void*>(decode_tma_kernel<false, 2>),
+        reinterpret_cast<const void*>(decode_tma_kernel<false, 4>), reinterpret_cast<const void*>(decode_tma_kernel<false, 8>),
+        reinterpret_cast<const void*>(decode_tma_kernel<true, 1>),  reinterpret_cast<const void*>(decode_tma_kernel<true, 2>),
+        reinterpret_cast<const void*>(decode_tma_kernel<true, 4>),  reinterpret_cast<const void*>(decode_tma_kernel<true, 8>),
+    };
+    int st = B2_OK;
+    for (const void* k : kernels) {
+        st = cuda_status(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(kTmaSmemBudget + 2048)));
+        if (st != B2_OK) return st;
+    }
+    done_mask.fetch_or(bit);
     return st;
+}
+
+// Tensor maps of one cache (K or V): rows of num_kv_heads * 256 bytes, boxes
+// of kTile rows. A few per thread are kept: the eager launchers re-use them
+// layer after layer while the length and base are unchanged.
+int cache_tensor_map(CUtensorMap* out, const void* base, uint32_t rows, uint32_t num_kv_heads) {
+    struct Entry {
+        const void* base;
+        uint32_t rows, kvh;
+        CUtensorMap map;
+    };
+    thread_local Entry cache[8] = {};
+    thread_local uint32_t next = 0;
+    for (const Entry& e : cache)
+        if (e.base == base && e.rows == rows && e.kvh == num_kv_heads) {
+            *out = e.map;
+            return B2_OK;
+        }
+    Entry& e = cache[next++ & 7];
+    if (encode_token_rows_by_column_block(&e.map, base, rows, num_kv_heads * 256u, kTile) != 0) {
+        e.base = nullptr;
+        return B2_ERR_CUDA;
+    }
+    e.base = base;
+    e.rows = rows;
+    e.kvh = num_kv_heads;
+    *out = e.map;
+    return B2_OK;
+}
+
+// Ring depth: each stage is always consumed by the same warp of a KV head (a
+// warp waits on a stage's next phase only after consuming the current one),
+// so the depth is a multiple of the consumer warps per head.
+uint32_t tma_stages(uint32_t num_kv_heads) {
+    const uint32_t stage_bytes = 2u * kTile * num_kv_heads * 256u;
+    const uint32_t npar = kTmaConsumers / num_kv_heads;
+    return (kTmaSmemBudget / stage_bytes) / npar * npar;
+}
+
+size_t tma_smem_bytes(uint32_t num_kv_heads, uint32_t stages) {
+    return static_cast<size_t>(stages) * 2u * kTile * num_kv_heads * 256u + 2 * stages * sizeof(uint64_t) +
+           1024;  // alignment slack
+}
+
+// Launch the TMA kernel over caches a.k / a.v of `map_rows` rows.
+template <bool kFused>
+int launch_tma_kernel(const DecodeArgs& a, const StepExt& x, uint32_t grid, uint32_t map_rows, cudaStream_t stream) {
+    CUtensorMap mk, mv;
+    int st = cache_tensor_map(&mk, a.k, map_rows, a.num_kv_heads);
+    if (st == B2_OK) st = cache_tensor_map(&mv, a.v, map_rows, a.num_kv_heads);
+    if (st != B2_OK) return st;
+    const size_t smem = tma_smem_bytes(a.num_kv_heads, a.stages);
+    switch (a.num_kv_heads) {
+        case 1:
+            return launch_pdl(decode_tma_kernel<kFused, 1>, dim3(grid), dim3(kTmaThreads), smem, stream, a, x, mk, mv);
+        case 2:
+            return launch_pdl(decode_tma_kernel<kFused, 2>, dim3(grid), dim3(kTmaThreads), smem, stream, a, x, mk, mv);
+        case 4:
+            return launch_pdl(decode_tma_kernel<kFused, 4>, dim3(grid), dim3(kTmaThreads), smem, stream, a, x, mk, mv);
+        case 8:
+            return launch_pdl(decode_tma_kernel<kFused, 8>, dim3(grid), dim3(kTmaThreads), smem, stream, a, x, mk, mv);
+        default: return B2_ERR_UNSUPPORTED;
+    }
 }
 
 int launch_merge_kernel(const MergeArgs& m, cudaStream_t stream) {
@@ -570,17 +1044,11 @@ int launch_decode(const void* d_q, const void* d_k, const void* d_v, void* d_out
     int st;
     if (tma_ok) {
         if ((st = ensure_tma_smem()) != B2_OK) return st;
-        // Each stage must always be consumed by the same warp of a KV head (a
-        // warp waits on a stage's next phase only after consuming the current
-        // one), so the ring depth is a multiple of the consumer warps per head.
-        const uint32_t stage_bytes = 2u * kTile * static_cast<uint32_t>(num_kv_heads) * 256u;
-        const uint32_t npar = kTmaConsumers / static_cast<uint32_t>(num_kv_heads);
-        a.stages = (kTmaSmemBudget / stage_bytes) / npar * npar;
+        a.stages = tma_stages(a.num_kv_heads);
         if (a.stages == 0) return B2_ERR_UNSUPPORTED;
         a.splits_cap = static_cast<uint32_t>(device_sms());
         const uint32_t grid = static_cast<uint32_t>(chunks < a.splits_cap ? chunks : a.splits_cap);
-        const size_t smem = a.stages * stage_bytes + 2 * a.stages * sizeof(uint64_t);
-        st = launch_pdl(decode_split_tma_kernel, dim3(grid), dim3(kTmaThreads), smem, stream, a);
+        st = launch_tma_kernel<false>(a, StepExt{}, grid, a.kv_len, stream);
     } else if (mma_ok) {
         st = launch_pdl(decode_split_mma_kernel, dim3(a.num_kv_heads, static_cast<uint32_t>(chunks)), dim3(128), 0,
                         stream, a);
@@ -604,12 +1072,105 @@ int launch_decode(const void* d_q, const void* d_k, const void* d_v, void* d_out
     return B2_OK;
 }
 
+// Workspace of the fused step: partials for up to kStepMaxSplits splits
+// ([H][S][128] o, [H][S] m, [H][S] l, floats), then 3 counters.
+struct StepWorkspace {
+    size_t po, pm, pl, counter, total_bytes;
+};
+
+StepWorkspace step_workspace_layout(size_t num_heads) {
+    StepWorkspace w{};
+    w.po = 0;
+    w.pm = w.po + num_heads * kStepMaxSplits * 128;
+    w.pl = w.pm + num_heads * kStepMaxSplits;
+    w.counter = w.pl + num_heads * kStepMaxSplits;
+    w.total_bytes = (w.counter * sizeof(float) + 3 * sizeof(uint32_t) + 255) / 256 * 256;
+    return w;
+}
+
+int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new, void* d_k_cache, void* d_v_cache,
+                       const void* d_cos, const void* d_sin, size_t rope_rows, bool apply_rotation,
+                       const int32_t* d_pos, const int32_t* d_kv_len, int32_t kv_len_bias, size_t max_kv_len,
+                       void* d_out, float* d_rank_o, float* d_rank_m, float* d_rank_l, void* d_workspace,
+                       size_t workspace_bytes, size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                       b2_stream_t stream_handle) {
+    if (max_kv_len == 0 || num_kv_heads == 0 || head_dim == 0) return B2_NOTHING_TO_DO;
+    if (num_heads % num_kv_heads != 0) return B2_NOTHING_TO_DO;
+    const bool rank = d_rank_o != nullptr || d_rank_m != nullptr || d_rank_l != nullptr;
+    if (!d_q || !d_k_cache || !d_v_cache || !d_kv_len || !d_workspace) return B2_ERR_INVALID_ARG;
+    if (rank ? (!d_rank_o || !d_rank_m || !d_rank_l || d_out) : !d_out) return B2_ERR_INVALID_ARG;
+    if (d_k_new && !d_v_new) return B2_ERR_INVALID_ARG;
+    if (apply_rotation && (!d_cos || !d_sin || !d_pos || rope_rows == 0)) return B2_ERR_INVALID_ARG;
+    const size_t group = num_heads / num_kv_heads;
+    if (head_dim != 128 || group > 8 ||
+        !(num_kv_heads == 1 || num_kv_heads == 2 || num_kv_heads == 4 || num_kv_heads == 8))
+        return B2_ERR_UNSUPPORTED;
+    const size_t chunks = (max_kv_len + kChunk - 1) / kChunk;
+    if (max_kv_len > 0x7fffffffull - kChunk || chunks > 65535 || rope_rows > 0x7fffffffull) return B2_ERR_UNSUPPORTED;
+    const void* ptrs[] = {d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, d_out, d_rank_o, d_workspace};
+    for (const void* p : ptrs)
+        if (p && !aligned16(p)) return B2_ERR_ALIGNMENT;
+    const StepWorkspace w = step_workspace_layout(num_heads);
+    if (workspace_bytes < w.total_bytes) return B2_ERR_WORKSPACE;
+    const uint32_t sms = static_cast<uint32_t>(device_sms());
+    if (sms > kStepMaxSplits) return B2_ERR_UNSUPPORTED;
+    int st = ensure_tma_smem();
+    if (st != B2_OK) return st;
+
+    float* ws = static_cast<float*>(d_workspace);
+    DecodeArgs a{};
+    a.q = static_cast<const __half*>(d_q);
+    a.k = static_cast<const __half*>(d_k_cache);
+    a.v = static_cast<const __half*>(d_v_cache);
+    a.po = ws + w.po;
+    a.pm = ws + w.pm;
+    a.pl = ws + w.pl;
+    a.kv_stride = num_kv_heads * head_dim;
+    a.kv_len = static_cast<uint32_t>(max_kv_len);
+    a.splits_cap = sms;
+    a.num_heads = static_cast<uint32_t>(num_heads);
+    a.num_kv_heads = static_cast<uint32_t>(num_kv_heads);
+    a.head_dim = static_cast<uint32_t>(head_dim);
+    a.group = static_cast<uint32_t>(group);
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.scale_log2 = a.scale * kLog2e;
+    a.kv_len_dev = d_kv_len;
+    a.kv_len_bias = kv_len_bias;
+    a.max_kv_len = static_cast<uint32_t>(max_kv_len);
+    a.stages = tma_stages(a.num_kv_heads);
+    if (a.stages == 0) return B2_ERR_UNSUPPORTED;
+
+    StepExt x{};
+    x.q_new = static_cast<const __half*>(d_q);
+    x.k_new = static_cast<const __half*>(d_k_new);
+    x.v_new = static_cast<const __half*>(d_v_new);
+    x.k_cache = static_cast<__half*>(d_k_cache);
+    x.v_cache = static_cast<__half*>(d_v_cache);
+    x.cos = static_cast<const __half*>(d_cos);
+    x.sin = static_cast<const __half*>(d_sin);
+    x.pos_dev = d_pos;
+    x.rotate = apply_rotation ? 1u : 0u;
+    x.table_rows = static_cast<uint32_t>(rope_rows);
+    x.counters = reinterpret_cast<uint32_t*>(ws + w.counter);
+    x.out = static_cast<__half*>(d_out);
+    x.rank_o = d_rank_o;
+    x.rank_m = d_rank_m;
+    x.rank_l = d_rank_l;
+    const uint32_t grid = static_cast<uint32_t>(chunks < sms ? chunks : sms);
+    return launch_tma_kernel<true>(a, x, grid, a.max_kv_len, reinterpret_cast<cudaStream_t>(stream_handle));
+}
+
 }  // namespace
 
 unsigned int device_error_decode() {
     unsigned int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0;
     return v;
+}
+
+int clear_device_error_decode() {
+    const unsigned int zero = 0;
+    return cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
 }
 
 }  // namespace b2
@@ -648,15 +1209,26 @@ extern "C" int b2_update_causal_attention_decode_node(b2_graph_exec_t graph_exec
     if (chunks > 65535 || kv_cache_len > 0x7fffffffull - kChunk) return B2_ERR_UNSUPPORTED;
     cudaGraphNode_t node = reinterpret_cast<cudaGraphNode_t>(node_handle);
     cudaKernelNodeParams params{};
-    const int st = node_kernel_params(node, kSplitKernels, 3, &params);
+    const int st = node_kernel_params(node, kSplitKernels, kNumTmaKernels + 2, &params);
     if (st != B2_OK) return st;
     DecodeArgs a = *static_cast<const DecodeArgs*>(params.kernelParams[0]);
     if (a.kv_len_dev != nullptr) return B2_ERR_GRAPH;  // graph-static nodes need no patching
     a.kv_len = static_cast<uint32_t>(kv_cache_len);
-    void* args[1] = {&a};
+    bool tma = false;
+    for (int i = 0; i < kNumTmaKernels; ++i) tma = tma || params.func == kSplitKernels[i];
+    StepExt x{};
+    CUtensorMap mk{}, mv{};
+    if (tma) {
+        // the tensor maps cover the cache rows read at the new length
+        x = *static_cast<const StepExt*>(params.kernelParams[1]);
+        int s2 = cache_tensor_map(&mk, a.k, a.kv_len, a.num_kv_heads);
+        if (s2 == B2_OK) s2 = cache_tensor_map(&mv, a.v, a.kv_len, a.num_kv_heads);
+        if (s2 != B2_OK) return s2;
+    }
+    void* args[4] = {&a, &x, &mk, &mv};
     params.kernelParams = args;
     params.extra = nullptr;
-    if (params.func == kSplitKernels[0])
+    if (tma)
         params.gridDim.x = static_cast<unsigned>(chunks < a.splits_cap ? chunks : a.splits_cap);
     else
         params.gridDim.y = static_cast<unsigned>(chunks);
@@ -737,6 +1309,34 @@ extern "C" int b2_launch_decode_rank_partial_devlen(const void* d_q, const void*
     return launch_decode(d_q, d_k_cache, d_v_cache, nullptr, d_partial_out, d_partial_max, d_partial_weight_sum, 1,
                          0, d_kv_len, kv_len_bias, max_kv_len, num_heads, num_kv_heads, head_dim, kv_stride, stream,
                          nullptr, nullptr, d_rank_o, d_rank_m, d_rank_l);
+}
+
+extern "C" size_t b2_decode_step_workspace_bytes(size_t num_heads) {
+    return b2::step_workspace_layout(num_heads).total_bytes;
+}
+
+extern "C" int b2_launch_decode_step_fused(const void* d_q, const void* d_k_new, const void* d_v_new,
+                                           void* d_k_cache, void* d_v_cache, const void* d_cos, const void* d_sin,
+                                           size_t rope_rows, bool apply_rotation, const int32_t* d_pos,
+                                           const int32_t* d_kv_len, int32_t kv_len_bias, size_t max_kv_len,
+                                           void* d_out, void* d_workspace, size_t workspace_bytes,
+                                           size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                           b2_stream_t stream) {
+    return b2::launch_decode_step(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows,
+                                  apply_rotation, d_pos, d_kv_len, kv_len_bias, max_kv_len, d_out, nullptr, nullptr,
+                                  nullptr, d_workspace, workspace_bytes, num_heads, num_kv_heads, head_dim, stream);
+}
+
+extern "C" int b2_launch_decode_step_fused_rank_partial(
+    const void* d_q, const void* d_k_new, const void* d_v_new, void* d_k_cache, void* d_v_cache, const void* d_cos,
+    const void* d_sin, size_t rope_rows, bool apply_rotation, const int32_t* d_pos, const int32_t* d_kv_len,
+    int32_t kv_len_bias, size_t max_kv_len, float* d_rank_o, float* d_rank_m, float* d_rank_l, void* d_workspace,
+    size_t workspace_bytes, size_t num_heads, size_t num_kv_heads, size_t head_dim, b2_stream_t stream) {
+    if (!d_rank_o || !d_rank_m || !d_rank_l) return B2_ERR_INVALID_ARG;
+    return b2::launch_decode_step(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows,
+                                  apply_rotation, d_pos, d_kv_len, kv_len_bias, max_kv_len, nullptr, d_rank_o,
+                                  d_rank_m, d_rank_l, d_workspace, workspace_bytes, num_heads, num_kv_heads,
+                                  head_dim, stream);
 }
 
 extern "C" int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream) {

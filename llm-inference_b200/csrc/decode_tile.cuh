@@ -95,7 +95,8 @@ constexpr float kRescaleThreshold = 8.f;
 // (zero in ka/kb) are masked to -inf.
 template <bool kPartial>
 __device__ __forceinline__ void tile_scores(float (&s)[4], const uint4 (&ka)[4], const uint4 (&kb)[4],
-                                            const uint32_t (&qf)[8][2], int g, uint32_t valid, float scale_log2) {
+                                            const uint32_t (&qf)[8][2], uint32_t g, uint32_t valid,
+                                            float scale_log2) {
     float s2[4] = {0.f, 0.f, 0.f, 0.f};  // two accumulation chains halve the MMA latency
     s[0] = s[1] = s[2] = s[3] = 0.f;
 #pragma unroll
@@ -111,8 +112,8 @@ __device__ __forceinline__ void tile_scores(float (&s)[4], const uint4 (&ka)[4],
 #pragma unroll
     for (int i = 0; i < 4; ++i) s[i] = (s[i] + s2[i]) * scale_log2;
     if (kPartial) {
-        if (static_cast<uint32_t>(g) >= valid) s[0] = s[1] = -INFINITY;
-        if (static_cast<uint32_t>(g + 8) >= valid) s[2] = s[3] = -INFINITY;
+        if (g >= valid) s[0] = s[1] = -INFINITY;  // g: the token held by MMA row g
+        if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
     }
 }
 
@@ -198,6 +199,47 @@ __device__ __forceinline__ void load_v_frags(const uint8_t* vt, uint32_t row_byt
         for (int b = 0; b < 2; ++b)
             va[r][b] = (!kPartial || row < valid)
                            ? *reinterpret_cast<const uint4*>(vt + row * row_bytes + (64 * b + 8 * g) * 2)
+                           : zero4;
+    }
+}
+
+// ---- Tiles staged column block by column block with 128-byte swizzling
+// ([block][16 rows][128 B], chunk c of row r at c ^ (r & 7); two blocks per KV
+// head). MMA row m (and P.V contraction index m) holds token tile_token(m):
+// odd rows are exchanged with the row 4 away, so the two rows a quarter-warp
+// reads land on disjoint 16-byte slots for the K fragments, and the four rows
+// of each V fragment load on disjoint slot pairs (no bank conflicts).
+__device__ __forceinline__ uint32_t tile_token(uint32_t m) { return m ^ ((m & 1u) << 2); }
+
+// K fragments of one head: kt = the head's first column block.
+template <bool kPartial>
+__device__ __forceinline__ void load_k_frags_sw(const uint8_t* kt, int g, int t, uint32_t valid, uint4 (&ka)[4],
+                                                uint4 (&kb)[4]) {
+    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t tok = tile_token(static_cast<uint32_t>(g));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t chunk = ((j & 1) * 4 + t) ^ tok;
+        const uint8_t* pa = kt + (j >> 1) * (kTile * 128) + tok * 128 + chunk * 16;
+        ka[j] = (!kPartial || tok < valid) ? *reinterpret_cast<const uint4*>(pa) : zero4;
+        kb[j] = (!kPartial || tok + 8 < valid) ? *reinterpret_cast<const uint4*>(pa + 8 * 128) : zero4;
+    }
+}
+
+// V fragments of one head: contraction rows 2t, 2t+1, 2t+8, 2t+9 (their
+// tokens via tile_token), head_dim halves 64b + 8g.
+template <bool kPartial>
+__device__ __forceinline__ void load_v_frags_sw(const uint8_t* vt, int g, int t, uint32_t valid,
+                                                uint4 (&va)[4][2]) {
+    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const uint32_t tok = tile_token(2 * t + (r & 1)) + (r >> 1) * 8;
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+            va[r][b] = (!kPartial || tok < valid)
+                           ? *reinterpret_cast<const uint4*>(vt + b * (kTile * 128) + tok * 128 +
+                                                             ((static_cast<uint32_t>(g) ^ (tok & 7u)) << 4))
                            : zero4;
     }
 }

@@ -301,6 +301,11 @@ unsigned int device_error_prefill() {
     return v;
 }
 
+int clear_device_error_prefill() {
+    const unsigned int zero = 0;
+    return cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+}
+
 int launch_prefill_sm100(const PrefillArgs& a, uint32_t batch, cudaStream_t stream) {
     if (a.head_dim != 128 || a.start_pos != 0) return B2_ERR_UNSUPPORTED;
     // tensor maps: 16-byte aligned bases and row / batch strides

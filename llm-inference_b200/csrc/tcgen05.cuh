@@ -151,6 +151,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// 3-D tiled load with an L2 cache policy (e.g. evict-first for streamed data).
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                                 uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -162,5 +172,13 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 int encode_tensor_map_3d_f16(CUtensorMap* map, const void* base, uint64_t inner_elems, uint64_t rows,
                              uint64_t batches, uint64_t row_stride_bytes, uint64_t batch_stride_bytes,
                              uint32_t box_inner, uint32_t box_rows);
+
+// Token rows of `row_bytes` (a multiple of 128) seen as a 3-D tensor
+// {64 fp16 (one 128-byte column block), rows, row_bytes / 128 column blocks}:
+// a box of `box_rows` rows lands in shared memory column block by column
+// block ([block][row][128 B], 128-byte swizzle: 16-byte chunk c of row r at
+// chunk c ^ (r & 7)). Returns 0 on success.
+int encode_token_rows_by_column_block(CUtensorMap* map, const void* base, uint64_t rows, uint32_t row_bytes,
+                                      uint32_t box_rows);
 
 }  // namespace b2

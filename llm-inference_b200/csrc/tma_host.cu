@@ -48,4 +48,19 @@ int encode_tensor_map_3d_f16(CUtensorMap* map, const void* base, uint64_t inner_
     return r == CUDA_SUCCESS ? 0 : -static_cast<int>(r);
 }
 
+int encode_token_rows_by_column_block(CUtensorMap* map, const void* base, uint64_t rows, uint32_t row_bytes,
+                                      uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return -1;
+    if (row_bytes % 128 != 0 || rows == 0) return -1;
+    const cuuint64_t dims[3] = {64, rows, row_bytes / 128};
+    const cuuint64_t strides[2] = {row_bytes, 128};
+    const cuuint32_t box[3] = {64, box_rows, row_bytes / 128};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -static_cast<int>(r);
+}
+
 }  // namespace b2

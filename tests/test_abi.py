@@ -153,3 +153,31 @@ def test_cpp_shim_header_compiles():
     res = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-x", "c++", "-", f"-I{ROOT}/include",
                           "-I/usr/local/cuda/include"], input=src, capture_output=True, text=True)
     assert res.returncode == 0, res.stderr
+
+
+def test_fused_decode_step_validation_without_cuda():
+    """b2_launch_decode_step_fused checks everything before its first CUDA call."""
+    L = b200attn.lib()
+    f = 0x1000
+    ws = L.b2_decode_step_workspace_bytes(16)
+    assert ws % 256 == 0 and ws >= 16 * (256 * 130) * 4
+    assert L.b2_decode_step_workspace_bytes(32) > ws
+
+    def call(q=f, kn=f, vn=f, kc=f, vc=f, cos=f, sin=f, rows=100, rot=True, pos=f, ln=f, bias=1, cap=99, out=f,
+             w=f, wb=ws, h=16, kvh=4, d=128):
+        return L.b2_launch_decode_step_fused(q, kn, vn, kc, vc, cos, sin, rows, rot, pos, ln, bias, cap, out, w, wb,
+                                             h, kvh, d, NULL)
+    assert call(cap=0) == 1 and call(kvh=0) == 1 and call(kvh=3) == 1          # silent skips
+    assert call(q=None) == -1 and call(ln=None) == -1 and call(w=None) == -1   # null buffers
+    assert call(out=None) == -1
+    assert call(vn=None) == -1                                                 # K without V
+    assert call(cos=None) == -1 and call(pos=None) == -1 and call(rows=0) == -1  # RoPE inputs
+    # NoPE needs none of them: this call gets as far as the workspace check
+    assert call(rot=False, cos=None, sin=None, pos=None, rows=0, wb=ws - 1) == -5
+    assert call(d=64) == -2 and call(h=48, kvh=4) == -2 and call(kvh=16, h=16) == -2
+    assert call(cap=65536 * 256 + 1) == -2
+    assert call(kc=f + 2) == -3 and call(w=f + 8) == -3
+    assert call(wb=ws - 1) == -5
+    r = L.b2_launch_decode_step_fused_rank_partial(f, None, None, f, f, f, f, 100, True, f, f, 0, 99, None, f, f, f,
+                                                   ws, 16, 4, 128, NULL)
+    assert r == -1

@@ -222,7 +222,7 @@ __device__ __forceinline__ void step_write_empty(uint32_t H, const StepExt& x, u
 // of a merging CTA folds partials w, w + 13, ... for 4 dims per lane; the 13
 // warp states meet in shared memory `wsm` (13 x 132 floats). The last merging
 // CTA resets the counters for the next launch.
-__device__ __noinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, float* wsm) {
+__device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, float* wsm) {
     __shared__ uint32_t role_s;
     const uint32_t H = a.num_heads;
     const uint32_t R = min(S, H);
@@ -329,7 +329,7 @@ constexpr uint32_t kPrefetchTiles = 8;  // tiles per CTA warmed in L2 before the
 
 // Fused kernel: tiles dealt out evenly to each split before the claimed pool.
 __device__ __forceinline__ uint32_t fused_share(uint32_t total_tiles, uint32_t splits) {
-    return (total_tiles * 4 / 5) / splits;
+    return (total_tiles * 2 / 3) / splits;
 }
 
 __device__ __forceinline__ bool split_index_ok(const Extent& e, uint32_t split) { return split < e.splits; }
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         const uint64_t policy = l2_evict_first_policy();
         uint32_t i = 0;
         if constexpr (kFused) {
-            // Tile order of split s: its even share [s*per, (s+1)*per) of ~4/5
+            // Tile order of split s: its even share [s*per, (s+1)*per) of ~2/3
             // of the tiles (the last split puts the last tile, which holds the
             // new row, after its first two, once consumer warp 0 has appended
             // the row), then tiles of the pool
@@ -627,8 +627,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (warp < kTmaConsumers) state_to_smem(st, warp, sm_m, sm_l, sm_o, lane >> 2, lane & 3);
     __syncthreads();
     // Slots of KV head h are h, h + KVH, ...: combine and write the partials.
-    combine_tile_any(npar, sm_m, sm_l, sm_o, KVH, a.group, split, ext.splits, a.po, a.pm, a.pl, threadIdx.x,
-                     kTmaThreads);
+    combine_tile2_any(npar, sm_m, sm_l, sm_o, sm_o + kTmaConsumers * 8 * kOStride, KVH, a.group, split, ext.splits,
+                      a.po, a.pm, a.pl, threadIdx.x, kTmaThreads);
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
     if constexpr (kFused) step_merge(a, x, ext.splits, reinterpret_cast<float*>(ring));
 }

@@ -189,6 +189,12 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ void step_store(const StepExt& x, uint32_t h, uint32_t d, float o, float M, float L) {
     if (x.rank_o) {
         x.rank_o[h * 128 + d] = o;
@@ -226,10 +232,10 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
     __shared__ uint32_t role_s;
     const uint32_t H = a.num_heads;
     const uint32_t R = min(S, H);
-    __threadfence();  // this thread's partial stores, before the arrival below
+    // the CTA's partial stores happen before thread 0's release increment
     __syncthreads();
     if (threadIdx.x == 0) {
-        const uint32_t k = atomicAdd(&x.counters[1], 1u);
+        const uint32_t k = atom_add_acq_rel_gpu(&x.counters[1], 1u);
         role_s = k + R >= S ? k + R - S : 0xffffffffu;
     }
     __syncthreads();

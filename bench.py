@@ -62,6 +62,14 @@ PF_WORKLOAD = ("config3: causal GQA prefill, batch 4 x 8192 tokens, 16/4 heads, 
                "36 layers x (RoPE theta 5e6 / NoPE every 4th layer + KV append + causal attention)")
 
 
+# BASELINE config 5 (ragged decode): 64 sequences, per-sequence caches of 16384 rows
+RG_B, RG_MAX = 64, 16384
+RG_WORKLOAD = ("config5: ragged decode, 64 sequences, KV lengths numpy default_rng(2024).integers(512, 16385, 64) "
+               "(length after the new token's append), per-sequence cache of 16384 rows, N(0,1) FP16, 16/4 heads, "
+               "head_dim 128, 36 layers x 1 new token per sequence per step (RoPE / NoPE + append + ragged "
+               "split-KV decode + merge)")
+
+
 def prefill_flops(batch: int, seq: int, heads: int = 16) -> int:
     """Causal exact count for QK^T + PV: 2 * B * H * d * S * (S + 1)."""
     return 2 * batch * heads * D * seq * (seq + 1)
@@ -302,6 +310,90 @@ def run_prefill(args, rank, world, dev):
                          "algorithmic_flops_per_launch": unit_flops}}
 
 
+# --------------------------------------------------------------------------- ragged decode (config 5)
+def run_ragged(args, rank, world, dev):
+    """36 layers of ragged RoPE/append + ragged decode for the sequences this
+    rank owns (greedy longest-first assignment), one captured CUDA graph per
+    step; returns a dict for the JSON line (rank 0)."""
+    import numpy as np
+    import torch
+    import b200attn
+    from b200attn import dist as bdist
+    lens_all = [int(x) for x in np.random.default_rng(SEED).integers(512, RG_MAX + 1, RG_B)]
+    mine = bdist.assign_sequences(lens_all, world)[rank]
+    B = len(mine)
+    lens = [lens_all[i] for i in mine]
+    gen = torch.Generator(device=dev).manual_seed(SEED + 200 + rank)
+    cache = torch.empty((LAYERS, 2, B, RG_MAX, KV_DIM), dtype=torch.float16, device=dev)
+    for l in range(LAYERS):
+        for kv in range(2):
+            for b in range(B):
+                cache[l, kv, b, :lens[b]].normal_(0.0, 1.0, generator=gen)
+    qkv = torch.empty((LAYERS, B, QKV), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    out = torch.empty((LAYERS, B, Q_DIM), dtype=torch.float16, device=dev)
+    cos, sin = b200attn.rope_tables_host(RG_MAX, D, 5.0e6)
+    d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device=dev)   # the new token's row
+    ws_bytes = b200attn.decode_ragged_workspace_bytes(B, H, KVH, RG_MAX)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(st):
+        for l in range(LAYERS):
+            row = qkv[l]
+            b200attn.launch_rope_and_store_kv_ragged(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[l, 0],
+                                                     cache[l, 1], RG_MAX * KV_DIM, d_cos, d_sin, B, H, KVH, D, QKV,
+                                                     QKV, pos, RG_MAX, (l + 1) % 4 != 0, stream=st)
+            b200attn.launch_causal_attention_decode_ragged(row, QKV, cache[l, 0], cache[l, 1], RG_MAX * KV_DIM, pos, 1,
+                                                           RG_MAX, out[l], 0, B, H, KVH, D, ws, ws_bytes, stream=st)
+
+    with torch.cuda.stream(stream):
+        step(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = b200attn.kernel_launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        step(torch.cuda.current_stream())
+    per_step = b200attn.kernel_launch_count() - n0
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, args.ragged_steps))
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        ms = bdist.max_over_ranks(ms, dev)
+    graph.reset()
+    # K+V rows read + Q + output + appended row, every sequence, every layer
+    seq_bytes = lambda n: 2 * n * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + 2 * KV_DIM * 2
+    total = sum(seq_bytes(n) for n in lens_all) * LAYERS * steps
+    mine_layer = sum(seq_bytes(n) for n in lens)
+    peak, peak_kind = load_peaks()
+    launch_ms = ms / steps / LAYERS
+    achieved = mine_layer / (launch_ms / 1e3) / 1e9
+    return {"metric": "ragged decode KV-read GB/s", "value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "workload": RG_WORKLOAD, "steps": steps, "ms_per_step": round(ms / steps, 4),
+            "gpu_launches": per_step * steps, "sequences_per_rank": B,
+            "parallelism": f"sequences over {world} GPU(s), greedy longest-first",
+            "roofline": {"bound": "hbm", "kernel": "decode_ragged_kernel + merge_ragged_kernel (+ ragged RoPE/append)",
+                         "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "avg_layer_us": round(launch_ms * 1e3, 3), "algorithmic_bytes_per_layer": mine_layer,
+                         "timing": "timed region (graph replays) / 36 layers per step"}}
+
+
 # --------------------------------------------------------------------------- GPU arm
 def run_b200(args, rank, world):
     import numpy as np
@@ -421,10 +513,15 @@ def run_b200(args, rank, world):
                          f"C oracle, {threads} OpenMP threads"}
 
     prefill = None
+    del cache
+    torch.cuda.empty_cache()
     if not args.no_prefill:
-        del cache
-        torch.cuda.empty_cache()
         prefill = run_prefill(args, rank, world, dev)
+        torch.cuda.empty_cache()
+    ragged = None
+    if not args.no_ragged:
+        ragged = run_ragged(args, rank, world, dev)
+        torch.cuda.empty_cache()
 
     if rank == 0:
         line = {
@@ -449,6 +546,7 @@ def run_b200(args, rank, world):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "ragged": ragged,
         }
         print(json.dumps(line), flush=True)
     graph.reset()
@@ -462,6 +560,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sub-measurement")
+    ap.add_argument("--no-ragged", action="store_true", help="skip the config-5 ragged decode sub-measurement")
+    ap.add_argument("--ragged-steps", type=int, default=8, help="timed ragged steps (36 layers each)")
     ap.add_argument("--unfused", action="store_true",
                     help="decode step as the reference's launch sequence (RoPE/append, split, merge) per layer "
                          "instead of the fused one-kernel-per-layer step")

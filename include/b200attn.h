@@ -312,6 +312,47 @@ int b2_launch_decode_step_fused_rank_partial(const void* d_q, const void* d_k_ne
                                              size_t num_heads, size_t num_kv_heads, size_t head_dim,
                                              b2_stream_t stream);
 
+/* ---- Ragged batched decode (continuous batching) ---------------------------
+ * No counterpart in the reference, whose engine decodes one sequence per
+ * call (src/kernels/causal_attention.hip.cpp:840-921); these apply the same
+ * split-KV attention and chunk merge (:493-595, :719-819) to B sequences of
+ * different lengths in one launch pair.
+ *
+ * b2_launch_rope_and_store_kv_ragged: b2_launch_rope_and_store_kv_devpos for
+ * one new token per sequence: token b (Q / K / V rows b, strides q_stride /
+ * k_stride, 0 = packed) is rotated at position d_pos[b] and its K/V written
+ * to row d_pos[b] of sequence b's cache, which starts cache_seq_stride
+ * elements after sequence b-1's (>= max_seq_len * num_kv_heads * head_dim).
+ * Tokens whose position is outside [0, max_seq_len) are skipped. */
+int b2_launch_rope_and_store_kv_ragged(void* d_q, void* d_k, const void* d_v,
+                                       void* d_k_cache, void* d_v_cache, size_t cache_seq_stride,
+                                       const void* d_cos, const void* d_sin, size_t num_seqs,
+                                       size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                       size_t q_stride, size_t k_stride, const int32_t* d_pos,
+                                       size_t max_seq_len, bool apply_rotation, b2_stream_t stream);
+
+/* One query token per sequence: out[b] ([num_heads][128] fp16 at
+ * d_out + b * out_seq_stride) = attention of Q row b (d_q + b * q_seq_stride)
+ * over rows [0, len_b) of sequence b's cache (d_k_cache / d_v_cache +
+ * b * cache_seq_stride, packed rows of num_kv_heads * 128), len_b =
+ * clamp(d_kv_len[b] + kv_len_bias, 0, max_kv_len), read at launch (graph
+ * static). Strides in elements; 0 = packed (cache: max_kv_len rows). A
+ * sequence of length 0 gets a zero output. head_dim 128, num_kv_heads in
+ * {1,2,4,8}, num_heads / num_kv_heads <= 8, num_seqs <= 1024; 16-byte
+ * aligned buffers and row strides.
+ * d_workspace: b2_decode_ragged_workspace_bytes(num_seqs, num_heads,
+ * num_kv_heads, max_kv_len) bytes, ZERO-FILLED once before first use (each
+ * call leaves its counter at zero again); one workspace per stream. */
+size_t b2_decode_ragged_workspace_bytes(size_t num_seqs, size_t num_heads, size_t num_kv_heads,
+                                        size_t max_kv_len);
+int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t q_seq_stride,
+                                             const void* d_k_cache, const void* d_v_cache,
+                                             size_t cache_seq_stride, const int32_t* d_kv_len,
+                                             int32_t kv_len_bias, size_t max_kv_len, void* d_out,
+                                             size_t out_seq_stride, size_t num_seqs, size_t num_heads,
+                                             size_t num_kv_heads, size_t head_dim, void* d_workspace,
+                                             size_t workspace_bytes, b2_stream_t stream);
+
 /* ---- Decode without a caller workspace ------------------------------------
  * No counterpart in the reference (whose decode launchers always take the
  * three partial arrays). For callers that cannot provide scratch memory: a

@@ -26,6 +26,7 @@ __all__ = [
     "launch_causal_attention_decode_devlen", "advance_position", "launch_decode_rank_partial_devlen",
     "launch_merge_partials_strided", "launch_causal_attention_prefill_batched",
     "decode_step_workspace_bytes", "launch_decode_step_fused", "launch_decode_step_fused_rank_partial",
+    "launch_rope_and_store_kv_ragged", "decode_ragged_workspace_bytes", "launch_causal_attention_decode_ragged",
 ]
 
 
@@ -217,6 +218,34 @@ def launch_decode_step_fused_rank_partial(d_q, d_k_new, d_v_new, d_k_cache, d_v_
         rope_rows, bool(apply_rotation), _ptr(d_pos), _ptr(d_kv_len), int(kv_len_bias), max_kv_len,
         _ptr(d_rank_o), _ptr(d_rank_m), _ptr(d_rank_l), _ptr(d_workspace), workspace_bytes, num_heads,
         num_kv_heads, head_dim, _stream(stream)), "launch_decode_step_fused_rank_partial")
+
+
+# ---- Ragged batched decode ----------------------------------------------------
+
+def launch_rope_and_store_kv_ragged(d_q, d_k, d_v, d_k_cache, d_v_cache, cache_seq_stride, d_cos, d_sin, num_seqs,
+                                    num_heads, num_kv_heads, head_dim, q_stride, k_stride, d_pos, max_seq_len,
+                                    apply_rotation, stream=None):
+    """One new token per sequence: token b rotated at d_pos[b] and appended to row
+    d_pos[b] of sequence b's cache (cache_seq_stride elements per sequence)."""
+    check(lib().b2_launch_rope_and_store_kv_ragged(
+        _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_k_cache), _ptr(d_v_cache), cache_seq_stride, _ptr(d_cos),
+        _ptr(d_sin), num_seqs, num_heads, num_kv_heads, head_dim, q_stride, k_stride, _ptr(d_pos), max_seq_len,
+        bool(apply_rotation), _stream(stream)), "launch_rope_and_store_kv_ragged")
+
+
+def decode_ragged_workspace_bytes(num_seqs, num_heads, num_kv_heads, max_kv_len):
+    """Bytes of the (zero-filled once) workspace of launch_causal_attention_decode_ragged."""
+    return int(lib().b2_decode_ragged_workspace_bytes(num_seqs, num_heads, num_kv_heads, max_kv_len))
+
+
+def launch_causal_attention_decode_ragged(d_q, q_seq_stride, d_k_cache, d_v_cache, cache_seq_stride, d_kv_len,
+                                          kv_len_bias, max_kv_len, d_out, out_seq_stride, num_seqs, num_heads,
+                                          num_kv_heads, head_dim, d_workspace, workspace_bytes, stream=None):
+    """Decode one token for each of num_seqs sequences of lengths d_kv_len[b] + bias."""
+    check(lib().b2_launch_causal_attention_decode_ragged(
+        _ptr(d_q), q_seq_stride, _ptr(d_k_cache), _ptr(d_v_cache), cache_seq_stride, _ptr(d_kv_len),
+        int(kv_len_bias), max_kv_len, _ptr(d_out), out_seq_stride, num_seqs, num_heads, num_kv_heads, head_dim,
+        _ptr(d_workspace), workspace_bytes, _stream(stream)), "launch_causal_attention_decode_ragged")
 
 
 # ---- KV-split decode across ranks --------------------------------------------

@@ -23,6 +23,8 @@ unsigned int device_error_decode();
 unsigned int device_error_prefill();
 int clear_device_error_decode();
 int clear_device_error_prefill();
+unsigned int device_error_ragged();
+int clear_device_error_ragged();
 
 // Turn the launch status of the kernel just enqueued into a b2 status.
 inline int launch_status() {

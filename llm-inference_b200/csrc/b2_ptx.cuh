@@ -89,6 +89,13 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// The same without an L2 policy.
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // L2 policy for data read exactly once (streamed KV).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;

@@ -71,11 +71,14 @@ int b2_last_cuda_error(void) { return b2::g_last_cuda_error.load(); }
 
 uint64_t b2_kernel_launch_count(void) { return b2::g_launches.load(); }
 
-unsigned int b2_device_error_word(void) { return b2::device_error_decode() | b2::device_error_prefill(); }
+unsigned int b2_device_error_word(void) {
+    return b2::device_error_decode() | b2::device_error_prefill() | b2::device_error_ragged();
+}
 
 int b2_clear_device_error_word(void) {
-    const int st = b2::clear_device_error_decode();
-    return st != B2_OK ? st : b2::clear_device_error_prefill();
+    int st = b2::clear_device_error_decode();
+    if (st == B2_OK) st = b2::clear_device_error_prefill();
+    return st != B2_OK ? st : b2::clear_device_error_ragged();
 }
 
 int b2_fill_rope_tables(size_t max_seq_len, size_t head_dim, float rope_theta,

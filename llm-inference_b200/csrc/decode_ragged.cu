@@ -1,0 +1,516 @@
+// Ragged batched flash-decode for sm_100a: one new query token for each of B
+// sequences whose caches hold different numbers of tokens (the continuous-
+// batching decode step: 64 sequences, 512..16384 tokens).
+//
+// The reference engine decodes one sequence at a time
+// (src/kernels/causal_attention.hip.cpp:840-921 launch_causal_attention_decode);
+// the algebra here is the same split-KV attention and chunk merge (:493-595,
+// :719-819), applied to all sequences in one persistent launch:
+//
+//   * Work unit = (sequence, a range of unit_tokens cached tokens). Units are
+//     claimed from a global counter by persistent CTAs (one per SM), so the
+//     batch's ~Σ len / unit_tokens units spread evenly however the lengths
+//     are distributed.
+//   * A producer warp streams each unit's 16-token K/V tiles (4-D tensor
+//     map: {64 fp16, row, column block, sequence}, 128-byte swizzle) into the
+//     stage ring, plus the sequence's Q row into one of two Q slots; the unit
+//     is padded with empty stages to a multiple of the consumer parities so
+//     every consumer warp sees every unit.
+//   * 12 consumer warps (KV head x tile parity) run the same MMA tile math as
+//     the single-sequence kernel and, at each unit boundary, write their own
+//     (o, m, l) state as a partial: no CTA-wide barrier per unit, so the
+//     producer keeps streaming across unit boundaries.
+//   * A merge kernel (one CTA per (sequence, head)) folds the npar partials
+//     of each of the sequence's units and writes the fp16 output.
+#include <math.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "b2_common.cuh"
+#include "b2_ptx.cuh"
+#include "decode_tile.cuh"
+#include "tcgen05.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kRgConsumers = 12;
+constexpr int kRgThreads = (kRgConsumers + 1) * 32;
+constexpr uint32_t kRgMaxSeqs = 1024;
+constexpr uint32_t kRgQSlots = 2;
+// Dynamic shared memory requested per CTA at most; with the ~8.6 KB of static
+// tables (unit prefix sums, lengths) the CTA stays under 227 KB.
+constexpr uint32_t kRgSmemLimit = 214 * 1024;
+constexpr uint32_t kNoUnit = 0xffffffffu;
+
+// Unit geometry per KV-head count: npar consumer warps per KV head; a unit is
+// a multiple of npar tiles, at least 16 tiles (256 tokens, the KV_CHUNK).
+__host__ __device__ constexpr uint32_t rg_npar(uint32_t kvh) { return kRgConsumers / kvh; }
+__host__ __device__ constexpr uint32_t rg_unit_tiles(uint32_t kvh) {
+    return rg_npar(kvh) * ((16 + rg_npar(kvh) - 1) / rg_npar(kvh));
+}
+__host__ __device__ constexpr uint32_t rg_unit_tokens(uint32_t kvh) { return rg_unit_tiles(kvh) * kTile; }
+
+struct RaggedArgs {
+    const __half* q;        // sequence b's query row at q + b * q_seq_stride, [H][128]
+    uint64_t q_seq_stride;  // elements
+    const int32_t* kv_len;  // [B]; length = clamp(kv_len[b] + bias, 0, max_kv_len)
+    int32_t kv_len_bias;
+    uint32_t max_kv_len;
+    __half* out;            // sequence b's output at out + b * out_seq_stride, [H][128]
+    uint64_t out_seq_stride;
+    float* po;              // [P][H][128] partial o (unnormalised), P = units * npar
+    float* pm;              // [P][H] natural-log max
+    float* pl;              // [P][H] weight sum
+    uint32_t* counter;      // next unclaimed unit; 0 at launch, reset by the merge
+    uint32_t num_seqs;
+    uint32_t num_heads;
+    uint32_t group;
+    uint32_t stages;
+    float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t rg_len(const RaggedArgs& a, uint32_t b) {
+    int64_t n = static_cast<int64_t>(__ldg(a.kv_len + b)) + a.kv_len_bias;
+    n = n < 0 ? 0 : (n > a.max_kv_len ? a.max_kv_len : n);
+    return static_cast<uint32_t>(n);
+}
+
+// Write one consumer warp's state as partial p of the heads of KV head kvh.
+__device__ __forceinline__ void rg_store_state(const WarpState& st, const RaggedArgs& a, uint32_t p, uint32_t kvh,
+                                               int g, int t) {
+    const uint32_t H = a.num_heads;
+#pragma unroll
+    for (int hsel = 0; hsel < 2; ++hsel) {
+        const uint32_t hh = 2 * t + hsel;
+        if (hh >= a.group) continue;
+        const uint32_t head = kvh * a.group + hh;
+        float* o = a.po + (static_cast<uint64_t>(p) * H + head) * 128;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            const int d = 64 * (mt >> 2) + 8 * g + 2 * (mt & 3);
+            *reinterpret_cast<float2*>(o + d) =
+                hsel == 0 ? make_float2(st.o[mt][0], st.o[mt][2]) : make_float2(st.o[mt][1], st.o[mt][3]);
+        }
+        if (g == 0) {
+            const float m = hsel == 0 ? st.m0 : st.m1;
+            a.pm[static_cast<uint64_t>(p) * H + head] = m == -INFINITY ? -INFINITY : m * kLn2;
+            a.pl[static_cast<uint64_t>(p) * H + head] = hsel == 0 ? st.l0 : st.l1;
+        }
+    }
+}
+
+template <uint32_t KVH>
+__global__ void __launch_bounds__(kRgThreads, 1)
+    decode_ragged_kernel(const RaggedArgs a, const __grid_constant__ CUtensorMap map_k,
+                         const __grid_constant__ CUtensorMap map_v) {
+    constexpr uint32_t npar = rg_npar(KVH);
+    constexpr uint32_t unit_tokens = rg_unit_tokens(KVH);
+    constexpr uint32_t row_bytes = KVH * 256;
+    constexpr uint32_t tile_bytes = kTile * row_bytes;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint32_t prefix[kRgMaxSeqs + 1];  // units before sequence b
+    __shared__ uint32_t lens[kRgMaxSeqs];
+    __shared__ uint32_t st_valid[32], st_unit[32], st_local[32];
+
+    pdl_wait_primary();  // lengths, Q and the caches may come from the previous kernel
+    pdl_launch_dependents();
+    const uint32_t B = a.num_seqs;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+        uint32_t carry = 0;
+        for (uint32_t base = 0; base < B; base += 32) {
+            const uint32_t b = base + lane;
+            uint32_t u = 0;
+            if (b < B) {
+                const uint32_t len = rg_len(a, b);
+                lens[b] = len;
+                u = (len + unit_tokens - 1) / unit_tokens;
+            }
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const uint32_t n = __shfl_up_sync(0xffffffffu, u, off);
+                if (lane >= off) u += n;
+            }
+            if (b < B) prefix[b + 1] = carry + u;
+            carry += __shfl_sync(0xffffffffu, u, 31);
+        }
+        if (lane == 0) prefix[0] = 0;
+    }
+
+    const uint32_t stages = a.stages;
+    const uint32_t q_bytes = a.num_heads * 256;
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* qslots = ring + stages * 2 * tile_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(qslots + kRgQSlots * q_bytes);
+    uint64_t* empty = full + stages;
+    uint64_t* qfull = empty + stages;
+    uint64_t* qempty = qfull + kRgQSlots;
+    if (threadIdx.x == 32) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], KVH);
+        }
+        for (uint32_t s = 0; s < kRgQSlots; ++s) {
+            mbar_init(&qfull[s], 1);
+            mbar_init(&qempty[s], KVH * npar);
+        }
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+    const uint32_t U = prefix[B];
+
+    bool ok = true;
+    if (warp == kRgConsumers) {
+        // ---- producer
+        if (lane == 0) {
+            tc::prefetch_tensormap(&map_k);
+            tc::prefetch_tensormap(&map_v);
+        }
+        const uint64_t policy = l2_evict_first_policy();
+        uint32_t i = 0, k = 0;
+        uint32_t claimed = lane == 0 ? atomicAdd(a.counter, 1u) : 0u;
+        for (;;) {
+            const uint32_t u = __shfl_sync(0xffffffffu, claimed, 0);
+            if (u >= U) break;
+            if (lane == 0) claimed = atomicAdd(a.counter, 1u);  // the next claim is in flight meanwhile
+            uint32_t lo = 0, hi = B;  // prefix[lo] <= u < prefix[hi]
+            while (hi - lo > 1) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (prefix[mid] <= u) lo = mid;
+                else hi = mid;
+            }
+            const uint32_t b = lo, len = lens[b];
+            const uint32_t t_begin = (u - prefix[b]) * unit_tokens;
+            const uint32_t t_end = min(len, t_begin + unit_tokens);
+            const uint32_t ntiles = (t_end - t_begin + kTile - 1) / kTile;
+            const uint32_t nstages = (ntiles + npar - 1) / npar * npar;
+            // the sequence's Q row into Q slot k % 2
+            const uint32_t qs = k % kRgQSlots;
+            bool w_ok = true;
+            if (lane == 0) {
+                if (k >= kRgQSlots) w_ok = mbar_wait(&qempty[qs], ((k / kRgQSlots) - 1) & 1);
+                if (w_ok) {
+                    mbar_arrive_expect_tx(&qfull[qs], q_bytes);
+                    bulk_g2s_plain(qslots + qs * q_bytes, a.q + static_cast<uint64_t>(b) * a.q_seq_stride, q_bytes,
+                                   &qfull[qs]);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
+                ok = false;
+                break;
+            }
+            for (uint32_t j = 0; j < nstages; ++j, ++i) {
+                const uint32_t s = i % stages, round = i / stages;
+                if (lane == 0 && round > 0) w_ok = mbar_wait(&empty[s], (round - 1) & 1);
+                if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t t0 = t_begin + j * kTile;
+                    st_unit[s] = u;
+                    st_local[s] = k;
+                    if (j < ntiles) {
+                        st_valid[s] = min(static_cast<uint32_t>(kTile), t_end - t0);
+                        mbar_arrive_expect_tx(&full[s], 2 * tile_bytes);
+                        uint8_t* stg = ring + s * 2 * tile_bytes;
+                        tc::tma_load_4d_hint(stg, &map_k, 0, static_cast<int32_t>(t0), 0, static_cast<int32_t>(b),
+                                             &full[s], policy);
+                        tc::tma_load_4d_hint(stg + tile_bytes, &map_v, 0, static_cast<int32_t>(t0), 0,
+                                             static_cast<int32_t>(b), &full[s], policy);
+                    } else {
+                        st_valid[s] = 0;  // padding: every parity sees the unit
+                        mbar_arrive(&full[s]);
+                    }
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            ++k;
+        }
+        if (ok) {
+            // one end marker per consumer parity
+            for (uint32_t e = 0; e < npar; ++e, ++i) {
+                const uint32_t s = i % stages, round = i / stages;
+                if (lane == 0) {
+                    if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) ok = false;
+                    st_unit[s] = kNoUnit;
+                    st_valid[s] = 0;
+                    mbar_arrive(&full[s]);
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        }
+        // never leave the CTA with copies in flight into its shared memory
+        if (lane == 0) {
+            const uint32_t first = i > stages ? i - stages : 0;
+            for (uint32_t j = first; j < i; ++j) (void)mbar_wait(&full[j % stages], (j / stages) & 1);
+            for (uint32_t j = k > kRgQSlots ? k - kRgQSlots : 0; j < k; ++j)
+                (void)mbar_wait(&qfull[j % kRgQSlots], (j / kRgQSlots) & 1);
+        }
+    } else if (static_cast<uint32_t>(warp) / KVH < npar) {
+        // ---- consumers: warp = KV head (warp % KVH) x tile parity (warp / KVH)
+        const uint32_t kvh = warp % KVH, par = warp / KVH;
+        const int g = lane >> 2, t = lane & 3;
+        WarpState st;
+        state_init(st);
+        uint32_t qf[8][2];
+        uint32_t cur_local = kNoUnit, cur_unit = 0;
+        for (uint32_t i = par;; i += npar) {
+            const uint32_t s = i % stages, round = i / stages;
+            if (!mbar_wait(&full[s], round & 1)) {
+                ok = false;
+                break;
+            }
+            const uint32_t u = st_unit[s], kl = st_local[s], valid = st_valid[s];
+            if (u == kNoUnit || kl != cur_local) {
+                if (cur_local != kNoUnit) {
+                    state_finish(st);
+                    rg_store_state(st, a, cur_unit * npar + par, kvh, g, t);
+                    state_init(st);
+                }
+                if (u == kNoUnit) break;
+                const uint32_t qs = kl % kRgQSlots;
+                if (!mbar_wait(&qfull[qs], (kl / kRgQSlots) & 1)) {
+                    ok = false;
+                    break;
+                }
+                if (static_cast<uint32_t>(g) < a.group) {
+                    const uint8_t* qrow = qslots + qs * q_bytes + (kvh * a.group + g) * 256;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint4 w = lds128(qrow + (32 * j + 8 * t) * 2);
+                        qf[2 * j][0] = w.x;
+                        qf[2 * j][1] = w.y;
+                        qf[2 * j + 1][0] = w.z;
+                        qf[2 * j + 1][1] = w.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) qf[j][0] = qf[j][1] = 0u;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&qempty[qs]);
+                cur_local = kl;
+                cur_unit = u;
+            }
+            if (valid != 0) {
+                const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * (2 * kTile * 128);
+                const uint8_t* vt = kt + tile_bytes;
+                float sc[4];
+                uint4 va[4][2];
+                if (valid == kTile) {
+                    uint4 ka[4], kb[4];
+                    load_k_frags_sw<false>(kt, g, t, valid, ka, kb);
+                    tile_scores<false>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
+                    load_v_frags_sw<false>(vt, g, t, valid, va);
+                } else {
+                    uint4 ka[4], kb[4];
+                    load_k_frags_sw<true>(kt, g, t, valid, ka, kb);
+                    tile_scores<true>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
+                    load_v_frags_sw<true>(vt, g, t, valid, va);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                tile_softmax_pv(st, sc, va, g, t);
+            } else {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+        }
+    }
+    if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
+}
+
+// One CTA per (sequence, head), thread = output dim: fold the sequence's
+// units x npar partials (online rescale, batches of 8 in flight) and write
+// fp16 out. Block (0, 0) resets the claim counter for the next launch.
+constexpr int kRgMergeBatch = 8;
+
+__global__ void __launch_bounds__(128) merge_ragged_kernel(const RaggedArgs a, uint32_t npar, uint32_t unit_tokens) {
+    __shared__ uint32_t part_s[4];
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    const uint32_t b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    if (b == 0 && h == 0 && d == 0) *a.counter = 0u;
+    // units of the sequences before b
+    uint32_t before = 0;
+    for (uint32_t j = d; j < b; j += 128) before += (rg_len(a, j) + unit_tokens - 1) / unit_tokens;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) before += __shfl_xor_sync(0xffffffffu, before, off);
+    if ((d & 31) == 0) part_s[d >> 5] = before;
+    __syncthreads();
+    before = part_s[0] + part_s[1] + part_s[2] + part_s[3];
+    const uint32_t units = (rg_len(a, b) + unit_tokens - 1) / unit_tokens;
+    const uint32_t p0 = before * npar, n = units * npar;
+    const uint32_t H = a.num_heads;
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (uint32_t base = 0; base < n; base += kRgMergeBatch) {
+        float mv[kRgMergeBatch], lv[kRgMergeBatch], ov[kRgMergeBatch];
+#pragma unroll
+        for (int u = 0; u < kRgMergeBatch; ++u) {
+            const uint32_t c = base + u;
+            const uint64_t p = static_cast<uint64_t>(p0 + c) * H + h;
+            mv[u] = c < n ? __ldg(a.pm + p) : -INFINITY;
+            lv[u] = c < n ? __ldg(a.pl + p) : 0.f;
+            ov[u] = c < n ? __ldg(a.po + p * 128 + d) : 0.f;
+        }
+        float bm = M;
+#pragma unroll
+        for (int u = 0; u < kRgMergeBatch; ++u) bm = fmaxf(bm, mv[u]);
+        if (bm == -INFINITY) continue;
+        const float sc = M == -INFINITY ? 0.f : expf(M - bm);
+        O *= sc;
+        L *= sc;
+        M = bm;
+#pragma unroll
+        for (int u = 0; u < kRgMergeBatch; ++u) {
+            const float w = mv[u] == -INFINITY ? 0.f : expf(mv[u] - M);
+            O = fmaf(w, ov[u], O);
+            L = fmaf(w, lv[u], L);
+        }
+    }
+    a.out[static_cast<uint64_t>(b) * a.out_seq_stride + h * 128 + d] = __float2half_rn(L > 0.f ? O / L : 0.f);
+}
+
+int device_sms_rg() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    return n;
+}
+
+struct RgWorkspace {
+    size_t po, pm, pl, counter, total_bytes;
+};
+
+RgWorkspace rg_layout(size_t num_seqs, size_t num_heads, size_t num_kv_heads, size_t max_kv_len) {
+    RgWorkspace w{};
+    const uint32_t kvh = static_cast<uint32_t>(num_kv_heads);
+    const size_t units = num_seqs * ((max_kv_len + rg_unit_tokens(kvh) - 1) / rg_unit_tokens(kvh));
+    const size_t P = units * rg_npar(kvh);
+    w.po = 0;
+    w.pm = w.po + P * num_heads * 128;
+    w.pl = w.pm + P * num_heads;
+    w.counter = w.pl + P * num_heads;
+    w.total_bytes = (w.counter * sizeof(float) + sizeof(uint32_t) + 255) / 256 * 256;
+    return w;
+}
+
+template <uint32_t KVH>
+int launch_ragged_kvh(const RaggedArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, uint32_t grid, size_t smem,
+                      cudaStream_t stream) {
+    static std::atomic<uint64_t> attr_done{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return B2_ERR_CUDA;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        const int st = cuda_status(cudaFuncSetAttribute(decode_ragged_kernel<KVH>,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        static_cast<int>(kRgSmemLimit)));
+        if (st != B2_OK) return st;
+        attr_done.fetch_or(bit);
+    }
+    return launch_pdl(decode_ragged_kernel<KVH>, dim3(grid), dim3(kRgThreads), smem, stream, a, mk, mv);
+}
+
+}  // namespace
+
+unsigned int device_error_ragged() {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0;
+    return v;
+}
+
+int clear_device_error_ragged() {
+    const unsigned int zero = 0;
+    return cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+}
+
+}  // namespace b2
+
+namespace {
+bool rg_kvh_ok(size_t kvh) { return kvh == 1 || kvh == 2 || kvh == 4 || kvh == 8; }
+}  // namespace
+
+extern "C" size_t b2_decode_ragged_workspace_bytes(size_t num_seqs, size_t num_heads, size_t num_kv_heads,
+                                                   size_t max_kv_len) {
+    if (!rg_kvh_ok(num_kv_heads)) return 0;
+    return b2::rg_layout(num_seqs, num_heads, num_kv_heads, max_kv_len).total_bytes;
+}
+
+extern "C" int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t q_seq_stride, const void* d_k_cache,
+                                                        const void* d_v_cache, size_t cache_seq_stride,
+                                                        const int32_t* d_kv_len, int32_t kv_len_bias,
+                                                        size_t max_kv_len, void* d_out, size_t out_seq_stride,
+                                                        size_t num_seqs, size_t num_heads, size_t num_kv_heads,
+                                                        size_t head_dim, void* d_workspace, size_t workspace_bytes,
+                                                        b2_stream_t stream_handle) {
+    using namespace b2;
+    if (num_seqs == 0 || max_kv_len == 0 || num_kv_heads == 0 || head_dim == 0) return B2_NOTHING_TO_DO;
+    if (num_heads % num_kv_heads != 0) return B2_NOTHING_TO_DO;
+    if (!d_q || !d_k_cache || !d_v_cache || !d_kv_len || !d_out || !d_workspace) return B2_ERR_INVALID_ARG;
+    const size_t group = num_heads / num_kv_heads;
+    if (head_dim != 128 || !rg_kvh_ok(num_kv_heads) || group > 8 || num_seqs > kRgMaxSeqs ||
+        max_kv_len > 0x7fffffffull)
+        return B2_ERR_UNSUPPORTED;
+    const size_t kv_dim = num_kv_heads * head_dim;
+    if (q_seq_stride == 0) q_seq_stride = num_heads * head_dim;
+    if (out_seq_stride == 0) out_seq_stride = num_heads * head_dim;
+    if (cache_seq_stride == 0) cache_seq_stride = max_kv_len * kv_dim;
+    if (q_seq_stride < num_heads * head_dim || out_seq_stride < num_heads * head_dim) return B2_ERR_INVALID_ARG;
+    if (num_seqs > 1 && cache_seq_stride < max_kv_len * kv_dim) return B2_ERR_INVALID_ARG;  // caches overlap
+    if (!aligned16(d_q) || !aligned16(d_k_cache) || !aligned16(d_v_cache) || !aligned16(d_workspace) ||
+        q_seq_stride % 8 != 0 || cache_seq_stride % 8 != 0)
+        return B2_ERR_ALIGNMENT;
+    const RgWorkspace w = rg_layout(num_seqs, num_heads, num_kv_heads, max_kv_len);
+    if (workspace_bytes < w.total_bytes) return B2_ERR_WORKSPACE;
+    const uint32_t kvh = static_cast<uint32_t>(num_kv_heads);
+    const uint32_t npar = rg_npar(kvh);
+    const size_t stage_bytes = 2ull * kTile * kvh * 256;
+    const size_t fixed = 1024 + kRgQSlots * num_heads * 256 + 256;
+    uint32_t stages = static_cast<uint32_t>((kRgSmemLimit - fixed) / stage_bytes) / npar * npar;
+    if (stages > 32) stages = 32 / npar * npar;
+    if (stages == 0) return B2_ERR_UNSUPPORTED;
+
+    float* ws = static_cast<float*>(d_workspace);
+    RaggedArgs a{};
+    a.q = static_cast<const __half*>(d_q);
+    a.q_seq_stride = q_seq_stride;
+    a.kv_len = d_kv_len;
+    a.kv_len_bias = kv_len_bias;
+    a.max_kv_len = static_cast<uint32_t>(max_kv_len);
+    a.out = static_cast<__half*>(d_out);
+    a.out_seq_stride = out_seq_stride;
+    a.po = ws + w.po;
+    a.pm = ws + w.pm;
+    a.pl = ws + w.pl;
+    a.counter = reinterpret_cast<uint32_t*>(ws + w.counter);
+    a.num_seqs = static_cast<uint32_t>(num_seqs);
+    a.num_heads = static_cast<uint32_t>(num_heads);
+    a.group = static_cast<uint32_t>(group);
+    a.stages = stages;
+    a.scale_log2 = kLog2e / sqrtf(static_cast<float>(head_dim));
+
+    CUtensorMap mk, mv;
+    if (encode_token_rows_by_column_block_seqs(&mk, d_k_cache, max_kv_len, kvh * 256, num_seqs,
+                                               cache_seq_stride * 2, kTile) != 0 ||
+        encode_token_rows_by_column_block_seqs(&mv, d_v_cache, max_kv_len, kvh * 256, num_seqs,
+                                               cache_seq_stride * 2, kTile) != 0)
+        return B2_ERR_CUDA;
+    const size_t smem = fixed + stages * stage_bytes + 2 * (stages + kRgQSlots) * sizeof(uint64_t);
+    const uint32_t grid = static_cast<uint32_t>(device_sms_rg());
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
+    int st;
+    switch (kvh) {
+        case 1: st = launch_ragged_kvh<1>(a, mk, mv, grid, smem, stream); break;
+        case 2: st = launch_ragged_kvh<2>(a, mk, mv, grid, smem, stream); break;
+        case 4: st = launch_ragged_kvh<4>(a, mk, mv, grid, smem, stream); break;
+        default: st = launch_ragged_kvh<8>(a, mk, mv, grid, smem, stream); break;
+    }
+    if (st != B2_OK) return st;
+    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(128), 0, stream, a, npar,
+                      rg_unit_tokens(kvh));
+}

@@ -51,9 +51,18 @@ struct RopeArgs {
     // launch and tokens at positions >= max_seq_len are skipped.
     const int32_t* start_pos_dev;
     uint32_t max_seq_len;
+    // Ragged batch: token t is sequence t's new token, at position
+    // pos_per_token[t], appended to the cache that starts cache_seq_stride
+    // elements after sequence t-1's.
+    const int32_t* pos_per_token;
+    uint64_t cache_seq_stride;
 };
 
 __device__ __forceinline__ bool resolve_start(const RopeArgs& a, uint32_t& start) {
+    if (a.pos_per_token != nullptr) {
+        start = 0;
+        return true;
+    }
     if (a.start_pos_dev == nullptr) {
         start = a.start_pos;
         return true;
@@ -61,6 +70,24 @@ __device__ __forceinline__ bool resolve_start(const RopeArgs& a, uint32_t& start
     const int32_t s = __ldg(a.start_pos_dev);
     if (s < 0) return false;
     start = static_cast<uint32_t>(s);
+    return true;
+}
+
+// Position of token t and the element offset of its cache row; false = skip
+// the token (graph-static position past the cache, or a ragged position
+// outside [0, max_seq_len)).
+__device__ __forceinline__ bool token_row(const RopeArgs& a, uint32_t start, uint64_t t, uint64_t& pos,
+                                          uint64_t& crow) {
+    if (a.pos_per_token != nullptr) {
+        const int32_t p = __ldg(a.pos_per_token + t);
+        if (p < 0 || static_cast<uint32_t>(p) >= a.max_seq_len) return false;
+        pos = static_cast<uint64_t>(p);
+        crow = t * a.cache_seq_stride + pos * a.kv_dim;
+        return true;
+    }
+    pos = static_cast<uint64_t>(start) + t;
+    if (a.start_pos_dev && pos >= a.max_seq_len) return false;
+    crow = pos * a.kv_dim;
     return true;
 }
 
@@ -102,8 +129,8 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
         const uint32_t r = static_cast<uint32_t>(id - t * per_token);
         const uint32_t slot = r / a.lanes;
         const uint32_t e = (r - slot * a.lanes) * 8;
-        const uint64_t pos = static_cast<uint64_t>(start) + t;
-        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
+        uint64_t pos, crow;
+        if (!token_row(a, start, t, pos, crow)) continue;
         if (slot < a.num_heads + a.num_kv_heads) {
             __half* src;
             __half* dst;
@@ -113,7 +140,7 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
             } else {
                 const uint32_t j = slot - a.num_heads;
                 src = a.k + t * a.k_stride + static_cast<uint64_t>(j) * a.head_dim;
-                dst = a.k_cache ? a.k_cache + pos * a.kv_dim + static_cast<uint64_t>(j) * a.head_dim : src;
+                dst = a.k_cache ? a.k_cache + crow + static_cast<uint64_t>(j) * a.head_dim : src;
             }
             uint4 lo = *reinterpret_cast<const uint4*>(src + e);
             uint4 hi = *reinterpret_cast<const uint4*>(src + a.half_dim + e);
@@ -125,7 +152,7 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
         } else {
             const uint32_t j = slot - a.num_heads - a.num_kv_heads;
             const __half* src = a.v + t * a.k_stride + static_cast<uint64_t>(j) * a.head_dim;
-            __half* dst = a.v_cache + pos * a.kv_dim + static_cast<uint64_t>(j) * a.head_dim;
+            __half* dst = a.v_cache + crow + static_cast<uint64_t>(j) * a.head_dim;
             const uint4 lo = *reinterpret_cast<const uint4*>(src + e);
             const uint4 hi = *reinterpret_cast<const uint4*>(src + a.half_dim + e);
             *reinterpret_cast<uint4*>(dst + e) = lo;
@@ -147,8 +174,8 @@ __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a
         const uint32_t r = static_cast<uint32_t>(id - t * per_token);
         const uint32_t slot = r / a.lanes;
         const uint32_t i = r - slot * a.lanes;
-        const uint64_t pos = static_cast<uint64_t>(start) + t;
-        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
+        uint64_t pos, crow;
+        if (!token_row(a, start, t, pos, crow)) continue;
         if (slot < a.num_heads + a.num_kv_heads) {
             __half* src;
             __half* dst;
@@ -158,7 +185,7 @@ __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a
             } else {
                 const uint32_t j = slot - a.num_heads;
                 src = a.k + t * a.k_stride + static_cast<uint64_t>(j) * a.head_dim;
-                dst = a.k_cache ? a.k_cache + pos * a.kv_dim + static_cast<uint64_t>(j) * a.head_dim : src;
+                dst = a.k_cache ? a.k_cache + crow + static_cast<uint64_t>(j) * a.head_dim : src;
             }
             const float x0 = __half2float(src[i]);
             const float x1 = __half2float(src[i + a.half_dim]);
@@ -171,7 +198,7 @@ __global__ void __launch_bounds__(256) rope_store_scalar_kernel(const RopeArgs a
         } else {
             const uint32_t j = slot - a.num_heads - a.num_kv_heads;
             const __half* src = a.v + t * a.k_stride + static_cast<uint64_t>(j) * a.head_dim;
-            __half* dst = a.v_cache + pos * a.kv_dim + static_cast<uint64_t>(j) * a.head_dim;
+            __half* dst = a.v_cache + crow + static_cast<uint64_t>(j) * a.head_dim;
             dst[i] = src[i];
             dst[i + a.half_dim] = src[i + a.half_dim];
         }
@@ -193,9 +220,9 @@ __global__ void __launch_bounds__(256) kv_copy_vec8_kernel(const RopeArgs a) {
         const bool is_v = r >= a.lanes;
         const uint32_t e = (is_v ? r - a.lanes : r) * 8;
         const __half* src = (is_v ? a.v : a.k) + t * a.k_stride + e;
-        const uint64_t pos = static_cast<uint64_t>(start) + t;
-        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
-        __half* dst = (is_v ? a.v_cache : a.k_cache) + pos * a.kv_dim + e;
+        uint64_t pos, crow;
+        if (!token_row(a, start, t, pos, crow)) continue;
+        __half* dst = (is_v ? a.v_cache : a.k_cache) + crow + e;
         *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
     }
 }
@@ -213,9 +240,9 @@ __global__ void __launch_bounds__(256) kv_copy_scalar_kernel(const RopeArgs a) {
         const bool is_v = r >= a.lanes;
         const uint32_t e = is_v ? r - a.lanes : r;
         const __half* src = (is_v ? a.v : a.k) + t * a.k_stride + e;
-        const uint64_t pos = static_cast<uint64_t>(start) + t;
-        if (a.start_pos_dev && pos >= a.max_seq_len) continue;
-        __half* dst = (is_v ? a.v_cache : a.k_cache) + pos * a.kv_dim + e;
+        uint64_t pos, crow;
+        if (!token_row(a, start, t, pos, crow)) continue;
+        __half* dst = (is_v ? a.v_cache : a.k_cache) + crow + e;
         *dst = *src;
     }
 }
@@ -250,7 +277,8 @@ namespace {
 int launch_rope_impl(void* d_q, void* d_k, const void* d_v, void* d_k_cache, void* d_v_cache, const void* d_cos,
                      const void* d_sin, size_t seq_len, size_t num_heads, size_t num_kv_heads, size_t head_dim,
                      size_t q_stride, size_t k_stride, size_t start_pos, const int32_t* start_pos_dev,
-                     size_t max_seq_len, bool apply_rotation, b2_stream_t stream_handle) {
+                     size_t max_seq_len, bool apply_rotation, b2_stream_t stream_handle,
+                     const int32_t* pos_per_token = nullptr, size_t cache_seq_stride = 0) {
     if (seq_len == 0) return B2_NOTHING_TO_DO;  // rope.hip.cpp:156
     if (head_dim == 0 || (head_dim & 1) || d_k == nullptr) return B2_ERR_INVALID_ARG;
     if (num_kv_heads == 0 && num_heads == 0) return B2_NOTHING_TO_DO;
@@ -282,9 +310,11 @@ int launch_rope_impl(void* d_q, void* d_k, const void* d_v, void* d_k_cache, voi
     a.start_pos = static_cast<uint32_t>(start_pos);
     a.start_pos_dev = start_pos_dev;
     a.max_seq_len = static_cast<uint32_t>(max_seq_len > 0xffffffffull ? 0xffffffffull : max_seq_len);
+    a.pos_per_token = pos_per_token;
+    a.cache_seq_stride = cache_seq_stride;
 
-    const bool rows16 = (k_stride % 8 == 0) && aligned16(d_k) && (!store || (aligned16(d_v) &&
-                        aligned16(d_k_cache) && aligned16(d_v_cache)));
+    const bool rows16 = (k_stride % 8 == 0) && (cache_seq_stride % 8 == 0) && aligned16(d_k) &&
+                        (!store || (aligned16(d_v) && aligned16(d_k_cache) && aligned16(d_v_cache)));
     if (apply_rotation) {
         if (d_cos == nullptr || d_sin == nullptr || (num_heads && d_q == nullptr)) return B2_ERR_INVALID_ARG;
         const bool vec = (a.half_dim % 8 == 0) && rows16 && (num_heads == 0 || (q_stride % 8 == 0 && aligned16(d_q))) &&
@@ -334,6 +364,20 @@ extern "C" int b2_launch_rope_and_store_kv_devpos(void* d_q, void* d_k, const vo
     return launch_rope_impl(d_q, d_k, d_v, d_k_cache, d_v_cache, d_cos, d_sin, seq_len, num_heads, num_kv_heads,
                             head_dim, q_stride, k_stride, 0, d_start_pos, max_seq_len, apply_rotation,
                             stream_handle);
+}
+
+extern "C" int b2_launch_rope_and_store_kv_ragged(void* d_q, void* d_k, const void* d_v, void* d_k_cache,
+                                                  void* d_v_cache, size_t cache_seq_stride, const void* d_cos,
+                                                  const void* d_sin, size_t num_seqs, size_t num_heads,
+                                                  size_t num_kv_heads, size_t head_dim, size_t q_stride,
+                                                  size_t k_stride, const int32_t* d_pos, size_t max_seq_len,
+                                                  bool apply_rotation, b2_stream_t stream_handle) {
+    if (d_pos == nullptr || max_seq_len == 0) return B2_ERR_INVALID_ARG;
+    if (d_k_cache != nullptr && num_seqs > 1 && cache_seq_stride < max_seq_len * num_kv_heads * head_dim)
+        return B2_ERR_INVALID_ARG;  // the sequences' caches would overlap
+    return launch_rope_impl(d_q, d_k, d_v, d_k_cache, d_v_cache, d_cos, d_sin, num_seqs, num_heads, num_kv_heads,
+                            head_dim, q_stride, k_stride, 0, nullptr, max_seq_len, apply_rotation, stream_handle,
+                            d_pos, cache_seq_stride);
 }
 
 extern "C" int b2_launch_rope(void* d_q, void* d_k, const void* d_cos, const void* d_sin, size_t seq_len,

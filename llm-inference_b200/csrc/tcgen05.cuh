@@ -161,6 +161,16 @@ __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m
         : "memory");
 }
 
+// 4-D tiled load with an L2 cache policy.
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                                 int32_t w, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -180,5 +190,10 @@ int encode_tensor_map_3d_f16(CUtensorMap* map, const void* base, uint64_t inner_
 // chunk c ^ (r & 7)). Returns 0 on success.
 int encode_token_rows_by_column_block(CUtensorMap* map, const void* base, uint64_t rows, uint32_t row_bytes,
                                       uint32_t box_rows);
+
+// The same for `seqs` caches of `rows` rows each, sequence s starting
+// s * seq_stride_bytes after `base`: a 4-D tensor {64 fp16, rows, blocks, seqs}.
+int encode_token_rows_by_column_block_seqs(CUtensorMap* map, const void* base, uint64_t rows, uint32_t row_bytes,
+                                           uint64_t seqs, uint64_t seq_stride_bytes, uint32_t box_rows);
 
 }  // namespace b2

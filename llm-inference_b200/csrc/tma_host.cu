@@ -63,4 +63,19 @@ int encode_token_rows_by_column_block(CUtensorMap* map, const void* base, uint64
     return r == CUDA_SUCCESS ? 0 : -static_cast<int>(r);
 }
 
+int encode_token_rows_by_column_block_seqs(CUtensorMap* map, const void* base, uint64_t rows, uint32_t row_bytes,
+                                           uint64_t seqs, uint64_t seq_stride_bytes, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return -1;
+    if (row_bytes % 128 != 0 || rows == 0 || seqs == 0 || seq_stride_bytes % 16 != 0) return -1;
+    const cuuint64_t dims[4] = {64, rows, row_bytes / 128, seqs};
+    const cuuint64_t strides[3] = {row_bytes, 128, seqs > 1 ? seq_stride_bytes : static_cast<uint64_t>(rows) * row_bytes};
+    const cuuint32_t box[4] = {64, box_rows, row_bytes / 128, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -static_cast<int>(r);
+}
+
 }  // namespace b2

@@ -181,3 +181,28 @@ def test_fused_decode_step_validation_without_cuda():
     r = L.b2_launch_decode_step_fused_rank_partial(f, None, None, f, f, f, f, 100, True, f, f, 0, 99, None, f, f, f,
                                                    ws, 16, 4, 128, NULL)
     assert r == -1
+
+
+def test_ragged_decode_validation_without_cuda():
+    """b2_launch_causal_attention_decode_ragged / _rope_..._ragged check before any CUDA call."""
+    L = b200attn.lib()
+    f = 0x1000
+    ws = L.b2_decode_ragged_workspace_bytes(64, 16, 4, 16384)
+    assert ws % 256 == 0 and ws > 64 * 16 * 130 * 4
+    assert L.b2_decode_ragged_workspace_bytes(64, 16, 3, 16384) == 0
+
+    def call(q=f, qs=0, k=f, v=f, cs=0, ln=f, bias=0, mx=4096, out=f, os_=0, B=8, H=16, KVH=4, d=128, w=f, wb=ws):
+        return L.b2_launch_causal_attention_decode_ragged(q, qs, k, v, cs, ln, bias, mx, out, os_, B, H, KVH, d, w,
+                                                          wb, NULL)
+    assert call(B=0) == 1 and call(mx=0) == 1 and call(KVH=3) == 1
+    assert call(q=None) == -1 and call(ln=None) == -1 and call(w=None) == -1
+    assert call(d=64) == -2 and call(B=2000) == -2 and call(H=48) == -2
+    assert call(cs=100) == -1 and call(qs=8) == -1            # overlapping caches / rows
+    assert call(k=f + 2) == -3 and call(qs=2052) == -3
+    assert call(wb=16) == -5
+    assert L.b2_launch_rope_and_store_kv_ragged(f, f, f, f, f, 0, f, f, 4, 16, 4, 128, 0, 0, None, 64, True,
+                                                NULL) == -1
+    assert L.b2_launch_rope_and_store_kv_ragged(f, f, f, f, f, 100, f, f, 4, 16, 4, 128, 0, 0, f, 64, True,
+                                                NULL) == -1
+    assert L.b2_launch_rope_and_store_kv_ragged(f, f, f, f, f, 0, f, f, 0, 16, 4, 128, 0, 0, f, 64, True,
+                                                NULL) == 1

@@ -420,7 +420,8 @@ def run_b200(args, rank, world):
     qkv = qkv_host.to(dev)
     out = torch.zeros((LAYERS, Q_DIM), dtype=torch.float16, device=dev)
     out_host = torch.zeros_like(out, device="cpu").pin_memory()
-    step_state = bdist.DecodeStepState(plan, H, KVH, D, LAYERS, capacity, max_global, dev, fused=not args.unfused)
+    step_state = bdist.DecodeStepState(plan, H, KVH, D, LAYERS, capacity, max_global, dev, fused=not args.unfused,
+                                       exchange=args.exchange)
 
     stream = torch.cuda.Stream(device=dev)
     group = None
@@ -479,7 +480,7 @@ def run_b200(args, rank, world):
     kv_len_local = plan.local_len(PAST + 1)
     # K/V rows read, Q read, output written (+ the new K/V row read and appended)
     dec_bytes = 2 * kv_len_local * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + (4 * KV_DIM * 2 if step_state.fused else 0)
-    if step_state.fused and world == 1:
+    if step_state.fused and (world == 1 or step_state.exchange == "peer"):
         # Inside the captured step consecutive layers overlap (programmatic
         # dependent launch, L2 warm-up of the next layer's first tiles), so the
         # per-launch time is the timed region over its fused launches; the
@@ -530,7 +531,9 @@ def run_b200(args, rank, world):
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
             "data": "synthetic: KV ~N(0,0.5) (torch CUDA generator, seed 2024+rank), Q/K/V rows ~N(0,1) seeded",
             "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": PAST, "layers": LAYERS,
-                       "parallelism": f"kv-split{world}" if world > 1 else "single-gpu",
+                       "parallelism": (f"kv-split{world}, " + ("cross-rank merge in the fused kernel over CUDA-IPC "
+                                       "peer memory" if step_state.exchange == "peer" else "NCCL all-gather of rank "
+                                       "partials + merge kernel")) if world > 1 else "single-gpu",
                        "l2": "inputs larger than L2 (4.8 GB of KV per step)",
                        "step_graph": f"one CUDA graph per step, {launches_per_step} kernels"},
             "gpu_launches": launches_per_step * args.steps,
@@ -550,6 +553,7 @@ def run_b200(args, rank, world):
         }
         print(json.dumps(line), flush=True)
     graph.reset()
+    step_state.close()
 
 
 def main():
@@ -561,6 +565,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sub-measurement")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-5 ragged decode sub-measurement")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
+                         "all-gather of the rank partials and a merge kernel")
     ap.add_argument("--ragged-steps", type=int, default=8, help="timed ragged steps (36 layers each)")
     ap.add_argument("--unfused", action="store_true",
                     help="decode step as the reference's launch sequence (RoPE/append, split, merge) per layer "

@@ -312,6 +312,40 @@ int b2_launch_decode_step_fused_rank_partial(const void* d_q, const void* d_k_ne
                                              size_t num_heads, size_t num_kv_heads, size_t head_dim,
                                              b2_stream_t stream);
 
+/* ---- Fused decode step across GPUs (exchange inside the kernel) -----------
+ * b2_launch_decode_step_fused over this rank's KV range (as the _rank_partial
+ * form) whose merging CTAs publish each head's rank partial straight into
+ * every rank's exchange buffer (peer stores over NVLink, release flags),
+ * wait (bounded, 2 s) for every rank's partial of that head and write the
+ * merged fp16 output: d_out holds the full attention on every rank. The
+ * cross-rank merge is the reference's chunk merge with ranks as chunks
+ * (src/kernels/causal_attention.hip.cpp:719-819).
+ *  - exchange_buffers: HOST array of `world` (2..8) device pointers, every
+ *    rank's exchange buffer mapped into this process ([rank] = its own, from
+ *    b2_ipc_alloc; the others from b2_ipc_open of their handles), each
+ *    b2_decode_exchange_bytes(world, num_heads) bytes, zero at allocation.
+ *  - Every rank must make the same sequence of calls (one exchange per call),
+ *    each rank on its own GPU; a rank that stops makes the others time out
+ *    (device error bit 0) instead of hanging. */
+size_t b2_decode_exchange_bytes(size_t world, size_t num_heads);
+int b2_launch_decode_step_fused_exchange(const void* d_q, const void* d_k_new, const void* d_v_new,
+                                         void* d_k_cache, void* d_v_cache,
+                                         const void* d_cos, const void* d_sin, size_t rope_rows,
+                                         bool apply_rotation, const int32_t* d_pos,
+                                         const int32_t* d_kv_len, int32_t kv_len_bias,
+                                         size_t max_kv_len, void* d_out, void* d_workspace,
+                                         size_t workspace_bytes, size_t world, size_t rank,
+                                         void* const* exchange_buffers, size_t num_heads,
+                                         size_t num_kv_heads, size_t head_dim, b2_stream_t stream);
+
+/* CUDA IPC helpers for exchange buffers: allocate `bytes` zero-filled device
+ * memory and export its 64-byte handle; map a peer's handle into this
+ * process; unmap; free. */
+int b2_ipc_alloc(size_t bytes, void** d_ptr, void* handle_out);
+int b2_ipc_open(const void* handle, void** d_ptr);
+int b2_ipc_close(void* d_ptr);
+int b2_ipc_free(void* d_ptr);
+
 /* ---- Ragged batched decode (continuous batching) ---------------------------
  * No counterpart in the reference, whose engine decodes one sequence per
  * call (src/kernels/causal_attention.hip.cpp:840-921); these apply the same

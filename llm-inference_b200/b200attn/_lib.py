@@ -50,6 +50,13 @@ SIGNATURES: dict[str, tuple] = {
     "b2_launch_merge_partials_strided": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
     "b2_launch_causal_attention_decode_noalloc": (I, [P, P, P, P, S, S, S, S, S, S, P]),
     "b2_decode_step_workspace_bytes": (S, [S]),
+    "b2_decode_exchange_bytes": (S, [S, S]),
+    "b2_launch_decode_step_fused_exchange": (
+        I, [P, P, P, P, P, P, P, S, B, P, P, ctypes.c_int32, S, P, P, S, S, S, P, S, S, S, P]),
+    "b2_ipc_alloc": (I, [S, PP, P]),
+    "b2_ipc_open": (I, [P, PP]),
+    "b2_ipc_close": (I, [P]),
+    "b2_ipc_free": (I, [P]),
     "b2_launch_rope_and_store_kv_ragged": (I, [P, P, P, P, P, S, P, P, S, S, S, S, S, S, P, S, B, P]),
     "b2_decode_ragged_workspace_bytes": (S, [S, S, S, S]),
     "b2_launch_causal_attention_decode_ragged": (

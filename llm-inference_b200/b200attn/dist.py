@@ -97,7 +97,7 @@ class DecodeStepState:
     """Device-resident positions and workspaces for a graph-static decode step."""
 
     def __init__(self, plan: SplitPlan, num_heads, num_kv_heads, head_dim, num_layers, capacity, max_global,
-                 device, fused=True):
+                 device, fused=True, exchange="peer"):
         import torch
         from . import kernels as K
         self.plan = plan
@@ -106,6 +106,18 @@ class DecodeStepState:
         self.fused = fused
         self.step_ws_bytes = K.decode_step_workspace_bytes(num_heads)
         self.step_ws = torch.zeros(self.step_ws_bytes, dtype=torch.uint8, device=device)
+        # world > 1: "peer" = cross-rank merge inside the fused kernel over
+        # CUDA-IPC exchange buffers; "nccl" = rank partials all-gathered by NCCL
+        self.exchange = exchange if (fused and plan.world > 1) else None
+        self.xbuf = None
+        if self.exchange == "peer":
+            import torch.distributed as tdist
+
+            def gather(obj):
+                out = [None] * plan.world
+                tdist.all_gather_object(out, obj)
+                return out
+            self.xbuf = K.ExchangeBuffers(plan.world, plan.rank, num_heads, gather)
         self.H, self.KVH, self.D, self.L = num_heads, num_kv_heads, head_dim, num_layers
         self.capacity = capacity
         self.max_global = max_global
@@ -123,6 +135,11 @@ class DecodeStepState:
         per = num_heads * (head_dim + 2)
         self.rank_part = torch.zeros((num_layers, per), dtype=torch.float32, device=device)
         self.gathered = torch.zeros((num_layers, w * per), dtype=torch.float32, device=device)
+
+    def close(self):
+        if self.xbuf is not None:
+            self.xbuf.close()
+            self.xbuf = None
 
     def reset_position(self, pos: int):
         self.pos.fill_(pos)
@@ -155,6 +172,11 @@ def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stre
                 K.launch_decode_step_fused(q, kn, vn, kc, vc, d_cos, d_sin, st.max_global, rotate, st.pos, src, bias,
                                            st.capacity, out[l], st.step_ws, st.step_ws_bytes, H, KVH, D,
                                            stream=stream)
+                continue
+            if st.exchange == "peer":
+                K.launch_decode_step_fused_exchange(q, kn, vn, kc, vc, d_cos, d_sin, st.max_global, rotate, st.pos,
+                                                    src, bias, st.capacity, out[l], st.step_ws, st.step_ws_bytes,
+                                                    plan.world, plan.rank, st.xbuf.ptrs, H, KVH, D, stream=stream)
                 continue
             part = st.rank_part[l]
             K.launch_decode_step_fused_rank_partial(q, kn, vn, kc, vc, d_cos, d_sin, st.max_global, rotate, st.pos,
@@ -237,6 +259,11 @@ def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3, d
                     K.launch_decode_step_fused(row, kn, vn, cache.get_k_cache(l), cache.get_v_cache(l), d_cos, d_sin,
                                                st.max_global, rotate, st.pos, src, bias, st.capacity, out[l],
                                                st.step_ws, st.step_ws_bytes, H, KVH, D, stream=stream)
+                elif st.exchange == "peer":
+                    K.launch_decode_step_fused_exchange(
+                        row, kn, vn, cache.get_k_cache(l), cache.get_v_cache(l), d_cos, d_sin, st.max_global, rotate,
+                        st.pos, src, bias, st.capacity, out[l], st.step_ws, st.step_ws_bytes, st.plan.world,
+                        st.plan.rank, st.xbuf.ptrs, H, KVH, D, stream=stream)
                 else:
                     part = st.rank_part[l]
                     K.launch_decode_step_fused_rank_partial(

@@ -27,6 +27,7 @@ __all__ = [
     "launch_merge_partials_strided", "launch_causal_attention_prefill_batched",
     "decode_step_workspace_bytes", "launch_decode_step_fused", "launch_decode_step_fused_rank_partial",
     "launch_rope_and_store_kv_ragged", "decode_ragged_workspace_bytes", "launch_causal_attention_decode_ragged",
+    "decode_exchange_bytes", "launch_decode_step_fused_exchange", "ExchangeBuffers",
 ]
 
 
@@ -218,6 +219,61 @@ def launch_decode_step_fused_rank_partial(d_q, d_k_new, d_v_new, d_k_cache, d_v_
         rope_rows, bool(apply_rotation), _ptr(d_pos), _ptr(d_kv_len), int(kv_len_bias), max_kv_len,
         _ptr(d_rank_o), _ptr(d_rank_m), _ptr(d_rank_l), _ptr(d_workspace), workspace_bytes, num_heads,
         num_kv_heads, head_dim, _stream(stream)), "launch_decode_step_fused_rank_partial")
+
+
+# ---- Fused decode step across GPUs ---------------------------------------------
+
+def decode_exchange_bytes(world, num_heads):
+    return int(lib().b2_decode_exchange_bytes(world, num_heads))
+
+
+def launch_decode_step_fused_exchange(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows,
+                                      apply_rotation, d_pos, d_kv_len, kv_len_bias, max_kv_len, d_out, d_workspace,
+                                      workspace_bytes, world, rank, exchange_buffers, num_heads, num_kv_heads,
+                                      head_dim, stream=None):
+    """launch_decode_step_fused over this rank's KV range with the cross-rank
+    merge done inside the kernel over peer memory; d_out is the full result."""
+    import ctypes
+    arr = (ctypes.c_void_p * len(exchange_buffers))(*[int(p) for p in exchange_buffers])
+    check(lib().b2_launch_decode_step_fused_exchange(
+        _ptr(d_q), _ptr(d_k_new), _ptr(d_v_new), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_cos), _ptr(d_sin),
+        rope_rows, bool(apply_rotation), _ptr(d_pos), _ptr(d_kv_len), int(kv_len_bias), max_kv_len, _ptr(d_out),
+        _ptr(d_workspace), workspace_bytes, world, rank, arr, num_heads, num_kv_heads, head_dim, _stream(stream)),
+        "launch_decode_step_fused_exchange")
+
+
+class ExchangeBuffers:
+    """This rank's exchange buffer (CUDA IPC) plus every peer's, mapped here.
+    `all_gather` gathers a list of python objects from every rank (e.g.
+    torch.distributed.all_gather_object wrapped by the caller)."""
+
+    def __init__(self, world, rank, num_heads, all_gather):
+        import ctypes
+        self.world, self.rank = world, rank
+        self.bytes = decode_exchange_bytes(world, num_heads)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        check(lib().b2_ipc_alloc(self.bytes, ctypes.byref(own), handle), "ipc_alloc")
+        self.own = own.value
+        handles = all_gather(bytes(handle))
+        self.ptrs, self._opened = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                self.ptrs.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            hb = (ctypes.c_char * 64).from_buffer_copy(h)
+            check(lib().b2_ipc_open(hb, ctypes.byref(p)), "ipc_open")
+            self.ptrs.append(p.value)
+            self._opened.append(p.value)
+
+    def close(self):
+        for p in self._opened:
+            lib().b2_ipc_close(p)
+        self._opened = []
+        if self.own:
+            lib().b2_ipc_free(self.own)
+            self.own = None
 
 
 # ---- Ragged batched decode ----------------------------------------------------

@@ -41,6 +41,7 @@
 // Merge: one CTA per (head, 64 output dims), launched with programmatic
 // dependent launch so its launch overlaps the split kernel's tail.
 #include <math.h>
+#include <string.h>
 
 #include <atomic>
 #include <mutex>
@@ -127,6 +128,8 @@ __device__ __forceinline__ Extent decode_extent(const A& a) {
 
 // ---------------------------------------------------------------------------
 // Fused decode step (graph-static): extra inputs of decode_tma_kernel<true>.
+constexpr uint32_t kMaxWorld = 8;       // ranks of one NVLink domain
+constexpr uint32_t kExchangePitch = 132;  // exchange words per (slot, rank, head): o[128], m, l
 struct StepExt {
     const __half* q_new;     // the new token's Q, not rotated, [H][128]
     const __half* k_new;     // its K (not rotated) [KVH][128]; nullptr = no append on this rank
@@ -143,6 +146,13 @@ struct StepExt {
     float* rank_o;
     float* rank_m;
     float* rank_l;
+    // Cross-GPU exchange (world > 1): every rank's exchange buffer, mapped
+    // into this process (peers[rank] is this rank's own); layout in
+    // exchange_layout(). epoch: this rank's count of exchanges so far.
+    uint32_t world;
+    uint32_t rank;
+    uint32_t* epoch;
+    float* peers[kMaxWorld];
 };
 
 constexpr uint32_t kStepMaxSplits = 256;      // partial slots in a fused-step workspace
@@ -207,6 +217,89 @@ __device__ __forceinline__ void step_store(const StepExt& x, uint32_t h, uint32_
     }
 }
 
+// Exchange buffer of one rank: [2 slots][world][H][kExchangePitch] 8-byte
+// words {value, exchange number}, then this rank's exchange counter. Rank r's
+// partial of head h for exchange e sits in slot e & 1, row (r, h): o[0..127],
+// m, l. Each value travels with its exchange number in one 8-byte store, so a
+// reader polls the words themselves and needs no fence or flag (the writer
+// cannot reuse a slot before every rank has read it: exchange e + 2 starts
+// only after all ranks finished exchange e + 1, which follows their reads of e).
+__host__ __device__ __forceinline__ uint64_t exchange_words(uint32_t world, uint32_t H) {
+    return 2ull * world * H * kExchangePitch;
+}
+
+__device__ __forceinline__ void st_pair_sys(uint2* p, float v, uint32_t e) {
+    asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(e)
+                 : "memory");
+}
+__device__ __forceinline__ uint2 ld_pair_sys(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded poll of one exchange word until it carries exchange number e.
+__device__ __forceinline__ bool poll_pair(const uint2* p, uint32_t e, uint64_t t0, float& v) {
+    uint2 w = ld_pair_sys(p);
+    while (w.y != e) {
+        if (global_timer_ns() - t0 > kWaitBudgetNs) return false;
+        __nanosleep(20);
+        w = ld_pair_sys(p);
+    }
+    v = __uint_as_float(w.x);
+    return true;
+}
+
+// Publish this rank's partial (O over the 128 dims held by threads 0..127,
+// M, L) of head h to every rank, wait (bounded) for every rank's partial of
+// head h for exchange e, and write the merged fp16 output. Threads 0..127
+// of the CTA take part; returns false on a timeout.
+__device__ __noinline__ bool step_exchange_head(const StepExt& x, uint32_t H, uint32_t h, uint32_t e, float O,
+                                                float M, float L) {
+    const uint32_t slot = e & 1, world = x.world, d = threadIdx.x;
+    if (d >= 128) return true;
+    for (uint32_t r = 0; r < world; ++r) {
+        uint2* dst = reinterpret_cast<uint2*>(x.peers[r]) +
+                     ((static_cast<uint64_t>(slot) * world + x.rank) * H + h) * kExchangePitch;
+        st_pair_sys(dst + d, O, e);
+        if (d == 0) {
+            st_pair_sys(dst + 128, M, e);
+            st_pair_sys(dst + 129, L, e);
+        }
+    }
+    const uint2* own = reinterpret_cast<const uint2*>(x.peers[x.rank]);
+    const uint64_t t0 = global_timer_ns();
+    float mv[kMaxWorld], lv[kMaxWorld], ov[kMaxWorld];
+    bool ok = true;
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxWorld; ++r) {
+        if (r < world && ok) {
+            const uint2* src = own + ((static_cast<uint64_t>(slot) * world + r) * H + h) * kExchangePitch;
+            ok = poll_pair(src + d, e, t0, ov[r]) && poll_pair(src + 128, e, t0, mv[r]) &&
+                 poll_pair(src + 129, e, t0, lv[r]);
+        }
+    }
+    if (!ok) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        return false;
+    }
+    float Mx = -INFINITY;
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxWorld; ++r)
+        if (r < world) Mx = fmaxf(Mx, mv[r]);
+    float Ox = 0.f, Lx = 0.f;
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxWorld; ++r) {
+        if (r < world) {
+            const float sc = mv[r] == -INFINITY ? 0.f : expf(mv[r] - Mx);
+            Ox = fmaf(sc, ov[r], Ox);
+            Lx = fmaf(sc, lv[r], Lx);
+        }
+    }
+    x.out[h * 128 + d] = __float2half_rn(Lx > 0.f ? Ox / Lx : 0.f);
+    return true;
+}
+
 __device__ __forceinline__ void step_write_empty(uint32_t H, const StepExt& x, uint32_t tid, uint32_t nthreads) {
     for (uint32_t i = tid; i < H * 128; i += nthreads) {
         if (x.rank_o) {
@@ -256,6 +349,8 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
     if (role_s == 0xffffffffu) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kWarps = kTmaThreads / 32;
+    const uint32_t epoch_next = x.world > 1 ? *x.epoch + 1 : 0u;
+    float O_keep = 0.f, M_keep = -INFINITY, L_keep = 0.f;
     for (uint32_t h = r; h < H; h += R) {
         const float* po = a.po + static_cast<uint64_t>(h) * S * 128 + lane * 4;
         const float* pm = a.pm + static_cast<uint64_t>(h) * S;
@@ -315,9 +410,13 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
                 O = fmaf(sc, wsm[w * kPitch + d], O);
                 Lx = fmaf(sc, wsm[w * kPitch + 129], Lx);
             }
-            step_store(x, h, d, O, Mx, Lx);
+            if (x.world <= 1) step_store(x, h, d, O, Mx, Lx);
+            O_keep = O;
+            M_keep = Mx;
+            L_keep = Lx;
         }
         __syncthreads();
+        if (x.world > 1) (void)step_exchange_head(x, H, h, epoch_next, O_keep, M_keep, L_keep);
     }
     // the last merging CTA leaves the counters at zero for the next launch
     if (threadIdx.x == 0) {
@@ -326,6 +425,7 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
             x.counters[0] = 0u;
             x.counters[1] = 0u;
             x.counters[2] = 0u;
+            if (x.world > 1) *x.epoch = epoch_next;
         }
     }
 }
@@ -390,7 +490,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const Extent ext = decode_extent(a);
     const uint32_t split = blockIdx.x;
     if (kFused && ext.splits == 0) {  // empty cache: defined output
-        if (split == 0) step_write_empty(a.num_heads, x, threadIdx.x, blockDim.x);
+        if (split == 0) {
+            if (x.world > 1) {
+                // nothing to attend here, but the other ranks wait for this rank's partials
+                const uint32_t e = *x.epoch + 1;
+                for (uint32_t h = 0; h < a.num_heads; ++h)
+                    (void)step_exchange_head(x, a.num_heads, h, e, 0.f, -INFINITY, 0.f);
+                if (threadIdx.x == 0) *x.epoch = e;
+            } else {
+                step_write_empty(a.num_heads, x, threadIdx.x, blockDim.x);
+            }
+        }
         return;
     }
     if (split >= ext.splits) return;
@@ -1099,8 +1209,14 @@ int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new
                        const int32_t* d_pos, const int32_t* d_kv_len, int32_t kv_len_bias, size_t max_kv_len,
                        void* d_out, float* d_rank_o, float* d_rank_m, float* d_rank_l, void* d_workspace,
                        size_t workspace_bytes, size_t num_heads, size_t num_kv_heads, size_t head_dim,
-                       b2_stream_t stream_handle) {
+                       b2_stream_t stream_handle, size_t world = 1, size_t rank_index = 0,
+                       void* const* exchange_buffers = nullptr) {
     if (max_kv_len == 0 || num_kv_heads == 0 || head_dim == 0) return B2_NOTHING_TO_DO;
+    if (world > 1) {
+        if (world > kMaxWorld || rank_index >= world || exchange_buffers == nullptr) return B2_ERR_INVALID_ARG;
+        for (size_t r = 0; r < world; ++r)
+            if (exchange_buffers[r] == nullptr || !aligned16(exchange_buffers[r])) return B2_ERR_INVALID_ARG;
+    }
     if (num_heads % num_kv_heads != 0) return B2_NOTHING_TO_DO;
     const bool rank = d_rank_o != nullptr || d_rank_m != nullptr || d_rank_l != nullptr;
     if (!d_q || !d_k_cache || !d_v_cache || !d_kv_len || !d_workspace) return B2_ERR_INVALID_ARG;
@@ -1162,6 +1278,13 @@ int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new
     x.rank_o = d_rank_o;
     x.rank_m = d_rank_m;
     x.rank_l = d_rank_l;
+    x.world = static_cast<uint32_t>(world > 1 ? world : 1);
+    x.rank = static_cast<uint32_t>(rank_index);
+    if (world > 1) {
+        for (size_t r = 0; r < world; ++r) x.peers[r] = static_cast<float*>(exchange_buffers[r]);
+        x.epoch = reinterpret_cast<uint32_t*>(reinterpret_cast<uint2*>(x.peers[rank_index]) +
+                                              exchange_words(x.world, a.num_heads));
+    }
     const uint32_t grid = static_cast<uint32_t>(chunks < sms ? chunks : sms);
     return launch_tma_kernel<true>(a, x, grid, a.max_kv_len, reinterpret_cast<cudaStream_t>(stream_handle));
 }
@@ -1343,6 +1466,61 @@ extern "C" int b2_launch_decode_step_fused_rank_partial(
                                   apply_rotation, d_pos, d_kv_len, kv_len_bias, max_kv_len, nullptr, d_rank_o,
                                   d_rank_m, d_rank_l, d_workspace, workspace_bytes, num_heads, num_kv_heads,
                                   head_dim, stream);
+}
+
+extern "C" size_t b2_decode_exchange_bytes(size_t world, size_t num_heads) {
+    if (world == 0 || world > b2::kMaxWorld) return 0;
+    // exchange words + the exchange counter, rounded to 256 B
+    const size_t words = b2::exchange_words(static_cast<uint32_t>(world), static_cast<uint32_t>(num_heads));
+    return (words * sizeof(uint2) + sizeof(uint32_t) + 255) / 256 * 256;
+}
+
+extern "C" int b2_launch_decode_step_fused_exchange(
+    const void* d_q, const void* d_k_new, const void* d_v_new, void* d_k_cache, void* d_v_cache, const void* d_cos,
+    const void* d_sin, size_t rope_rows, bool apply_rotation, const int32_t* d_pos, const int32_t* d_kv_len,
+    int32_t kv_len_bias, size_t max_kv_len, void* d_out, void* d_workspace, size_t workspace_bytes,
+    size_t world, size_t rank, void* const* exchange_buffers, size_t num_heads, size_t num_kv_heads,
+    size_t head_dim, b2_stream_t stream) {
+    if (world < 2) return B2_ERR_INVALID_ARG;
+    return b2::launch_decode_step(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows,
+                                  apply_rotation, d_pos, d_kv_len, kv_len_bias, max_kv_len, d_out, nullptr, nullptr,
+                                  nullptr, d_workspace, workspace_bytes, num_heads, num_kv_heads, head_dim, stream,
+                                  world, rank, exchange_buffers);
+}
+
+extern "C" int b2_ipc_alloc(size_t bytes, void** d_ptr, void* handle_out) {
+    if (d_ptr == nullptr || handle_out == nullptr || bytes == 0) return B2_ERR_INVALID_ARG;
+    *d_ptr = nullptr;
+    void* p = nullptr;
+    int st = b2::cuda_status(cudaMalloc(&p, bytes));
+    if (st != B2_OK) return st;
+    st = b2::cuda_status(cudaMemset(p, 0, bytes));
+    cudaIpcMemHandle_t h;
+    if (st == B2_OK) st = b2::cuda_status(cudaIpcGetMemHandle(&h, p));
+    if (st != B2_OK) {
+        cudaFree(p);
+        return st;
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    *d_ptr = p;
+    return B2_OK;
+}
+
+extern "C" int b2_ipc_open(const void* handle, void** d_ptr) {
+    if (d_ptr == nullptr || handle == nullptr) return B2_ERR_INVALID_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return b2::cuda_status(cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+extern "C" int b2_ipc_close(void* d_ptr) {
+    if (d_ptr == nullptr) return B2_ERR_INVALID_ARG;
+    return b2::cuda_status(cudaIpcCloseMemHandle(d_ptr));
+}
+
+extern "C" int b2_ipc_free(void* d_ptr) {
+    if (d_ptr == nullptr) return B2_ERR_INVALID_ARG;
+    return b2::cuda_status(cudaFree(d_ptr));
 }
 
 extern "C" int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream) {

@@ -282,13 +282,13 @@ int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream);
  *    floating-point reassociation; kv_len 0 writes zeros.
  *  - head_dim 128, num_kv_heads in {1,2,4,8}, num_heads / num_kv_heads <= 8;
  *    16-byte aligned pointers. Other shapes return B2_ERR_UNSUPPORTED.
- *  - d_workspace holds b2_decode_step_workspace_bytes(num_heads) bytes (split
- *    partials and the tile counter) and must be ZERO-FILLED once before its
+ *  - d_workspace holds b2_decode_step_workspace_bytes(num_heads, num_kv_heads)
+ *    bytes (split partials and counters) and must be ZERO-FILLED once before its
  *    first use; each call leaves the counter at zero again. One workspace
  *    serves any number of calls ordered on one stream (e.g. every layer of a
  *    captured step); calls that can overlap on the GPU need separate
  *    workspaces. */
-size_t b2_decode_step_workspace_bytes(size_t num_heads);
+size_t b2_decode_step_workspace_bytes(size_t num_heads, size_t num_kv_heads);
 int b2_launch_decode_step_fused(const void* d_q, const void* d_k_new, const void* d_v_new,
                                 void* d_k_cache, void* d_v_cache,
                                 const void* d_cos, const void* d_sin, size_t rope_rows,

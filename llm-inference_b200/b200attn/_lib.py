@@ -49,7 +49,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_launch_decode_rank_partial_devlen": (I, [P, P, P, P, P, P, P, ctypes.c_int32, S, S, S, S, S, P, P, P, P]),
     "b2_launch_merge_partials_strided": (I, [P, P, P, P, S, S, S, S, S, S, S, P]),
     "b2_launch_causal_attention_decode_noalloc": (I, [P, P, P, P, S, S, S, S, S, S, P]),
-    "b2_decode_step_workspace_bytes": (S, [S]),
+    "b2_decode_step_workspace_bytes": (S, [S, S]),
     "b2_decode_exchange_bytes": (S, [S, S]),
     "b2_launch_decode_step_fused_exchange": (
         I, [P, P, P, P, P, P, P, S, B, P, P, ctypes.c_int32, S, P, P, S, S, S, P, S, S, S, P]),

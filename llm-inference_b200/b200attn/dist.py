@@ -104,7 +104,7 @@ class DecodeStepState:
         # fused: one kernel per layer (RoPE + append + split attention + merge);
         # otherwise the reference's sequence of RoPE/append, split, merge launches
         self.fused = fused
-        self.step_ws_bytes = K.decode_step_workspace_bytes(num_heads)
+        self.step_ws_bytes = K.decode_step_workspace_bytes(num_heads, num_kv_heads)
         self.step_ws = torch.zeros(self.step_ws_bytes, dtype=torch.uint8, device=device)
         # world > 1: "peer" = cross-rank merge inside the fused kernel over
         # CUDA-IPC exchange buffers; "nccl" = rank partials all-gathered by NCCL

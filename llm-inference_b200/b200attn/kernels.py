@@ -191,9 +191,9 @@ def advance_position(d_pos, delta=1, stream=None):
 
 # ---- Fused decode step ----------------------------------------------------------
 
-def decode_step_workspace_bytes(num_heads):
+def decode_step_workspace_bytes(num_heads, num_kv_heads=4):
     """Bytes of the (zero-filled once) workspace of launch_decode_step_fused."""
-    return int(lib().b2_decode_step_workspace_bytes(num_heads))
+    return int(lib().b2_decode_step_workspace_bytes(num_heads, num_kv_heads))
 
 
 def launch_decode_step_fused(d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, rope_rows, apply_rotation,

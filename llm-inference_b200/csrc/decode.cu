@@ -1194,7 +1194,7 @@ struct StepWorkspace {
     size_t po, pm, pl, counter, total_bytes;
 };
 
-StepWorkspace step_workspace_layout(size_t num_heads) {
+StepWorkspace step_workspace_layout(size_t num_heads, size_t /*num_kv_heads*/) {
     StepWorkspace w{};
     w.po = 0;
     w.pm = w.po + num_heads * kStepMaxSplits * 128;
@@ -1232,7 +1232,7 @@ int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new
     const void* ptrs[] = {d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, d_out, d_rank_o, d_workspace};
     for (const void* p : ptrs)
         if (p && !aligned16(p)) return B2_ERR_ALIGNMENT;
-    const StepWorkspace w = step_workspace_layout(num_heads);
+    const StepWorkspace w = step_workspace_layout(num_heads, num_kv_heads);
     if (workspace_bytes < w.total_bytes) return B2_ERR_WORKSPACE;
     const uint32_t sms = static_cast<uint32_t>(device_sms());
     if (sms > kStepMaxSplits) return B2_ERR_UNSUPPORTED;
@@ -1440,8 +1440,9 @@ extern "C" int b2_launch_decode_rank_partial_devlen(const void* d_q, const void*
                          nullptr, nullptr, d_rank_o, d_rank_m, d_rank_l);
 }
 
-extern "C" size_t b2_decode_step_workspace_bytes(size_t num_heads) {
-    return b2::step_workspace_layout(num_heads).total_bytes;
+extern "C" size_t b2_decode_step_workspace_bytes(size_t num_heads, size_t num_kv_heads) {
+    if (num_kv_heads == 0) return 0;
+    return b2::step_workspace_layout(num_heads, num_kv_heads).total_bytes;
 }
 
 extern "C" int b2_launch_decode_step_fused(const void* d_q, const void* d_k_new, const void* d_v_new,

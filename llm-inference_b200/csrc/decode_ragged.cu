@@ -77,30 +77,6 @@ __device__ __forceinline__ uint32_t rg_len(const RaggedArgs& a, uint32_t b) {
     return static_cast<uint32_t>(n);
 }
 
-// Write one consumer warp's state as partial p of the heads of KV head kvh.
-__device__ __forceinline__ void rg_store_state(const WarpState& st, const RaggedArgs& a, uint32_t p, uint32_t kvh,
-                                               int g, int t) {
-    const uint32_t H = a.num_heads;
-#pragma unroll
-    for (int hsel = 0; hsel < 2; ++hsel) {
-        const uint32_t hh = 2 * t + hsel;
-        if (hh >= a.group) continue;
-        const uint32_t head = kvh * a.group + hh;
-        float* o = a.po + (static_cast<uint64_t>(p) * H + head) * 128;
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-            const int d = 64 * (mt >> 2) + 8 * g + 2 * (mt & 3);
-            *reinterpret_cast<float2*>(o + d) =
-                hsel == 0 ? make_float2(st.o[mt][0], st.o[mt][2]) : make_float2(st.o[mt][1], st.o[mt][3]);
-        }
-        if (g == 0) {
-            const float m = hsel == 0 ? st.m0 : st.m1;
-            a.pm[static_cast<uint64_t>(p) * H + head] = m == -INFINITY ? -INFINITY : m * kLn2;
-            a.pl[static_cast<uint64_t>(p) * H + head] = hsel == 0 ? st.l0 : st.l1;
-        }
-    }
-}
-
 template <uint32_t KVH>
 __global__ void __launch_bounds__(kRgThreads, 1)
     decode_ragged_kernel(const RaggedArgs a, const __grid_constant__ CUtensorMap map_k,
@@ -268,7 +244,8 @@ __global__ void __launch_bounds__(kRgThreads, 1)
             if (u == kNoUnit || kl != cur_local) {
                 if (cur_local != kNoUnit) {
                     state_finish(st);
-                    rg_store_state(st, a, cur_unit * npar + par, kvh, g, t);
+                    store_warp_partial(st, a.po, a.pm, a.pl, 128, static_cast<uint64_t>(a.num_heads) * 128, 1,
+                                       a.num_heads, cur_unit * npar + par, kvh * a.group, a.group, g, t);
                     state_init(st);
                 }
                 if (u == kNoUnit) break;

@@ -203,6 +203,33 @@ __device__ __forceinline__ void load_v_frags(const uint8_t* vt, uint32_t row_byt
     }
 }
 
+// Write one warp's state (after state_finish) as partial p of its KV head's
+// query heads head0 .. head0 + group - 1: o of (head, p) at
+// po + head * o_hs + p * o_ps (128 floats), m (natural log) and l at
+// pm / pl + head * ml_hs + p * ml_ps.
+__device__ __forceinline__ void store_warp_partial(const WarpState& st, float* po, float* pm, float* pl,
+                                                   uint64_t o_hs, uint64_t o_ps, uint64_t ml_hs, uint64_t ml_ps,
+                                                   uint32_t p, uint32_t head0, uint32_t group, int g, int t) {
+#pragma unroll
+    for (int hsel = 0; hsel < 2; ++hsel) {
+        const uint32_t hh = 2 * t + hsel;
+        if (hh >= group) continue;
+        const uint32_t head = head0 + hh;
+        float* o = po + head * o_hs + p * o_ps;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            const int d = 64 * (mt >> 2) + 8 * g + 2 * (mt & 3);
+            *reinterpret_cast<float2*>(o + d) =
+                hsel == 0 ? make_float2(st.o[mt][0], st.o[mt][2]) : make_float2(st.o[mt][1], st.o[mt][3]);
+        }
+        if (g == 0) {
+            const float m = hsel == 0 ? st.m0 : st.m1;
+            pm[head * ml_hs + p * ml_ps] = m == -INFINITY ? -INFINITY : m * kLn2;
+            pl[head * ml_hs + p * ml_ps] = hsel == 0 ? st.l0 : st.l1;
+        }
+    }
+}
+
 // ---- Tiles staged column block by column block with 128-byte swizzling
 // ([block][16 rows][128 B], chunk c of row r at c ^ (r & 7); two blocks per KV
 // head). MMA row m (and P.V contraction index m) holds token tile_token(m):

@@ -159,9 +159,9 @@ def test_fused_decode_step_validation_without_cuda():
     """b2_launch_decode_step_fused checks everything before its first CUDA call."""
     L = b200attn.lib()
     f = 0x1000
-    ws = L.b2_decode_step_workspace_bytes(16)
-    assert ws % 256 == 0 and ws >= 16 * (256 * 130) * 4
-    assert L.b2_decode_step_workspace_bytes(32) > ws
+    ws = L.b2_decode_step_workspace_bytes(16, 4)
+    assert ws % 256 == 0 and ws >= 16 * (256 * 130) * 4   # one partial per split and head
+    assert L.b2_decode_step_workspace_bytes(32, 8) > 0 and L.b2_decode_step_workspace_bytes(16, 0) == 0
 
     def call(q=f, kn=f, vn=f, kc=f, vc=f, cos=f, sin=f, rows=100, rot=True, pos=f, ln=f, bias=1, cap=99, out=f,
              w=f, wb=ws, h=16, kvh=4, d=128):

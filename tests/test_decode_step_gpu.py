@@ -21,9 +21,9 @@ def _sync():
     torch.cuda.synchronize()
 
 
-def _workspace(heads=H):
+def _workspace(heads=H, kvh=KVH):
     import torch
-    n = b200attn.decode_step_workspace_bytes(heads)
+    n = b200attn.decode_step_workspace_bytes(heads, kvh)
     return torch.zeros(n, dtype=torch.uint8, device="cuda"), n
 
 
@@ -236,7 +236,7 @@ def test_fused_step_other_gqa_shapes(cuda, kvh, heads):
     qkv_d = dev(qkv)
     pos = torch.tensor([kv_len - 1], dtype=torch.int32, device=cuda)
     out = torch.empty(heads * D, dtype=torch.float16, device=cuda)
-    ws = _workspace(heads)
+    ws = _workspace(heads, kvh)
     _fused(qkv_d, kc, vc, dev(cos), dev(sin), cap, True, pos, pos, 1, cap, out, ws, heads, kvh)
     _sync()
     np.testing.assert_array_equal(bits(host(kc)), bits(exp_k))

@@ -279,13 +279,13 @@ def run_prefill(args, rank, world, dev):
         import torch.distributed as tdist
         tdist.barrier()
     torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
+    with ClockSampler(dev.index) as clocks, torch.cuda.stream(stream):
         ev[0].record(stream)
         for s_ in range(steps):
             for l in range(LAYERS):
                 layer(l, attn_ev[l] if s_ == steps - 1 else None)
         ev[1].record(stream)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
     launches = b200attn.kernel_launch_count() - n0
     ms = ev[0].elapsed_time(ev[1])
     attn_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / LAYERS
@@ -295,17 +295,24 @@ def run_prefill(args, rank, world, dev):
     unit_flops = prefill_flops(1, PF_S, H // KVH) * len(units)     # this rank, one layer
     tf = total_flops / (ms / 1e3) / 1e12
     achieved = unit_flops / (attn_ms / 1e3) / 1e12
-    peak = 1596.6
+    # the attention launches are timed inside a long (power-capped) step: the
+    # sustained tensor peak is the denominator, the burst one is reported beside
+    peak, burst = 1400.0, 1590.0
     pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    kind = "fallback"
+    kind = "fallback (sustained)"
     if os.path.exists(pk):
         with open(pk) as f:
-            peak, kind = float(json.load(f)["bf16_tflops"]), "measured (bf16 burst; fp16 runs at the same rate)"
+            pj = json.load(f)
+        peak = float(pj.get("bf16_tflops_sustained", pj["bf16_tflops"]))
+        burst = float(pj["bf16_tflops"])
+        kind = "measured (bf16 sustained, back-to-back GEMMs under the power cap; fp16 runs at the same rate)"
     return {"metric": "prefill TFLOP/s", "value": round(tf, 2), "unit": "TFLOP/s", "workload": PF_WORKLOAD,
+            "clocks": clocks.summary(),
             "steps": steps, "ms_per_step": round(ms / steps, 3), "gpu_launches": launches,
             "units_per_rank": len(units), "parallelism": f"batch x kv-head units over {world} GPU(s)",
             "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
+                         "frac_of_burst": round(achieved / burst, 4),
                          "frac_of_nominal_2250": round(achieved / 2250.0, 4), "avg_launch_ms": round(attn_ms, 4),
                          "algorithmic_flops_per_launch": unit_flops}}
 

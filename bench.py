@@ -310,7 +310,7 @@ def run_prefill(args, rank, world, dev):
             "clocks": clocks.summary(),
             "steps": steps, "ms_per_step": round(ms / steps, 3), "gpu_launches": launches,
             "units_per_rank": len(units), "parallelism": f"batch x kv-head units over {world} GPU(s)",
-            "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel", "achieved": round(achieved, 1),
+            "roofline": {"bound": "tensor", "kernel": "prefill_pair_kernel", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
                          "frac_of_burst": round(achieved / burst, 4),
                          "frac_of_nominal_2250": round(achieved / 2250.0, 4), "avg_launch_ms": round(attn_ms, 4),

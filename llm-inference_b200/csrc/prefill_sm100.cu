@@ -339,6 +339,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // for relative error (max 2.2e-4, under fp16's half ulp), and n added to the
 // exponent bits. x is clamped at -125 so the result stays a normal float
 // (2^-125 rounds to 0 in fp16, and -inf gives the same).
+constexpr bool kPolyPacked = true;  // exp2_poly2 on f32x2 pairs
+
 __device__ __forceinline__ float exp2_poly(float x) {
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
     x = fmaxf(x, -125.f);
@@ -350,8 +352,24 @@ __device__ __forceinline__ float exp2_poly(float x) {
     return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-    y0 = exp2_poly(x0);
-    y1 = exp2_poly(x1);
+    if (kPolyPacked) {
+        constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+        x0 = fmaxf(x0, -125.f);
+        x1 = fmaxf(x1, -125.f);
+        float t0, t1, n0, n1, f0, f1, p0, p1;
+        fadd2(t0, t1, x0, x1, kMagic, kMagic);
+        fadd2(n0, n1, t0, t1, -kMagic, -kMagic);
+        fadd2(f0, f1, x0, x1, -n0, -n1);
+        ffma2(p0, p1, f0, f1, 0.05286743491888046f, 0.05286743491888046f, 0.2421518862247467f,
+              0.2421518862247467f);
+        ffma2(p0, p1, p0, p1, f0, f1, 0.6935867667198181f, 0.6935867667198181f);
+        ffma2(p0, p1, p0, p1, f0, f1, 0.9999627470970154f, 0.9999627470970154f);
+        y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+        y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+    } else {
+        y0 = exp2_poly(x0);
+        y1 = exp2_poly(x1);
+    }
 }
 
 // One pair of exponentials in four goes through exp2_poly2 (the special

@@ -509,7 +509,12 @@ def run_b200(args, rank, world):
     e2e = None
     if world == 1:
         e2e = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup, args.steps,
-                               stream, step_state)
+                               stream, step_state, mode="reference" if args.unfused else "fused")
+        if not args.unfused:
+            ref_calls = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup,
+                                         args.steps, stream, step_state, mode="reference")
+            e2e["reference_launchers"] = {"value": ref_calls["value"], "ms_per_step": ref_calls["ms_per_step"],
+                                          "path": ref_calls["path"]}
 
     # ---- CPU baseline (rank 0, N=1): bounded sample
     cpu = None

@@ -281,28 +281,44 @@ def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3, d
     return sum(times) / len(times)
 
 
-def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, steps, stream, st) -> dict:
-    """The decode metric through the reference-facing C-ABI launchers
-    (launch_rope_and_store_kv + launch_causal_attention_decode_vectorized per
-    layer, host positions), with the step's Q/K/V rows copied in from pinned
-    host memory and the outputs copied back every step."""
+def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, steps, stream, st,
+               mode="fused") -> dict:
+    """The decode metric end to end through the C ABI with host buffers: every
+    step copies its Q/K/V rows (and position) in from pinned host memory, runs
+    36 layers, and copies the attention outputs back.
+    mode "fused": one b2_launch_decode_step_fused call per layer (the position
+    travels with the step's inputs); mode "reference": the reference engine's
+    calls, launch_rope_and_store_kv + launch_causal_attention_decode_vectorized
+    per layer with a host start_pos."""
     import torch
     from . import kernels as K
     H, KVH, D, L = st.H, st.KVH, st.D, st.L
     q_dim, kv_dim = H * D, KVH * D
     total = q_dim + 2 * kv_dim
+    pos_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    pos_dev = torch.zeros(1, dtype=torch.int32, device=qkv.device)
 
     def step(s):
         pos = past + s
         qkv.copy_(qkv_host, non_blocking=True)
-        for l in range(L):
-            row = qkv[l]
-            K.launch_rope_and_store_kv(row, row[q_dim:], row[q_dim + kv_dim:], cache.get_k_cache(l),
-                                       cache.get_v_cache(l), d_cos, d_sin, 1, H, KVH, D, total, total, pos,
-                                       (l + 1) % 4 != 0, stream=stream)
-            K.launch_causal_attention_decode_vectorized(row, cache.get_k_cache(l), cache.get_v_cache(l), out[l],
-                                                        st.po, st.pm, st.pl, 1, pos + 1, pos, H, KVH, D, total,
-                                                        kv_dim, stream=stream)
+        if mode == "fused":
+            pos_host[0] = pos
+            pos_dev.copy_(pos_host, non_blocking=True)
+            for l in range(L):
+                row = qkv[l]
+                K.launch_decode_step_fused(row, row[q_dim:], row[q_dim + kv_dim:], cache.get_k_cache(l),
+                                           cache.get_v_cache(l), d_cos, d_sin, st.max_global, (l + 1) % 4 != 0,
+                                           pos_dev, pos_dev, 1, st.capacity, out[l], st.step_ws, st.step_ws_bytes,
+                                           H, KVH, D, stream=stream)
+        else:
+            for l in range(L):
+                row = qkv[l]
+                K.launch_rope_and_store_kv(row, row[q_dim:], row[q_dim + kv_dim:], cache.get_k_cache(l),
+                                           cache.get_v_cache(l), d_cos, d_sin, 1, H, KVH, D, total, total, pos,
+                                           (l + 1) % 4 != 0, stream=stream)
+                K.launch_causal_attention_decode_vectorized(row, cache.get_k_cache(l), cache.get_v_cache(l), out[l],
+                                                            st.po, st.pm, st.pl, 1, pos + 1, pos, H, KVH, D, total,
+                                                            kv_dim, stream=stream)
         out_host.copy_(out, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -317,7 +333,11 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     nbytes = sum(L * (2 * (past + 1 + s) * kv_dim * 2 + q_dim * 2 * 2 + 2 * kv_dim * 2) for s in range(steps))
+    h2d = int(qkv_host.numel() * 2) + (4 if mode == "fused" else 0)
+    path = ("C-ABI b2_launch_decode_step_fused per layer (eager launches, device position copied in with the "
+            "step's rows), pinned H2D/D2H each step" if mode == "fused" else
+            "C-ABI launch_rope_and_store_kv + launch_causal_attention_decode_vectorized per layer (the reference "
+            "engine's calls), host start_pos, pinned H2D/D2H each step")
     return {"value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": int(qkv_host.numel() * 2), "d2h_bytes_per_step": int(out_host.numel() * 2),
-            "ms_per_step": round(ms / steps, 4), "path": "C-ABI launch_rope_and_store_kv + "
-            "launch_causal_attention_decode_vectorized per layer, host start_pos, pinned H2D/D2H each step"}
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(out_host.numel() * 2),
+            "ms_per_step": round(ms / steps, 4), "path": path}

@@ -233,7 +233,8 @@ def run_prefill(args, rank, world, dev):
     import torch
     import b200attn
     from b200attn import dist as bdist
-    units = bdist.prefill_units(PF_B, KVH, world, rank)
+    shard = bdist.prefill_shard(PF_B, KVH, world, rank)
+    units = shard.units() if shard is not None else bdist.prefill_units(PF_B, KVH, world, rank)
     seqs = sorted({b for b, _ in units})
     gen = torch.Generator(device=dev).manual_seed(SEED + 100 + rank)
     qkv = torch.empty((PF_B, PF_S, QKV), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
@@ -242,7 +243,7 @@ def run_prefill(args, rank, world, dev):
     cos, sin = b200attn.rope_tables_host(PF_S, D, 5.0e6)
     d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
     stream = torch.cuda.Stream(device=dev)
-    full_batch = len(units) == PF_B * KVH
+    G = H // KVH
 
     def layer(l, t_attn=None):
         rotate = (l + 1) % 4 != 0
@@ -253,13 +254,17 @@ def run_prefill(args, rank, world, dev):
                                               stream=stream)
         if t_attn is not None:
             t_attn[0].record(stream)
-        if full_batch:
+        if shard is not None:
+            # one batched launch over this rank's block of sequences x KV heads
+            s0, nb = shard.seq_begin, shard.seq_end - shard.seq_begin
+            g0, ng = shard.kvh_begin, shard.kvh_end - shard.kvh_begin
             b200attn.launch_causal_attention_prefill_batched(
-                qkv, cache[0, l, 0], cache[0, l, 1], out, PF_B, PF_S, H, KVH, D, QKV, KV_DIM, PF_S * QKV,
-                LAYERS * 2 * PF_S * KV_DIM, PF_S * Q_DIM, stream=stream)
+                qkv[s0, :, g0 * G * D:], cache[s0, l, 0, :, g0 * D:], cache[s0, l, 1, :, g0 * D:],
+                out[s0, :, g0 * G * D:], nb, PF_S, ng * G, ng, D, QKV, KV_DIM, PF_S * QKV,
+                LAYERS * 2 * PF_S * KV_DIM, PF_S * Q_DIM, stream=stream, out_stride=Q_DIM)
         else:
             for b, g in units:
-                g0 = g * (H // KVH)
+                g0 = g * G
                 b200attn.launch_causal_attention_prefill(
                     qkv[b, :, g0 * D:], cache[b, l, 0, :, g * D:], cache[b, l, 1, :, g * D:], out[b, :, g0 * D:],
                     PF_S, H // KVH, 1, D, QKV, KV_DIM, stream=stream)
@@ -309,7 +314,9 @@ def run_prefill(args, rank, world, dev):
     return {"metric": "prefill TFLOP/s", "value": round(tf, 2), "unit": "TFLOP/s", "workload": PF_WORKLOAD,
             "clocks": clocks.summary(),
             "steps": steps, "ms_per_step": round(ms / steps, 3), "gpu_launches": launches,
-            "units_per_rank": len(units), "parallelism": f"batch x kv-head units over {world} GPU(s)",
+            "units_per_rank": len(units), "parallelism": f"batch x kv-head units over {world} GPU(s)" + (
+                f", one batched launch per layer for sequences [{shard.seq_begin}, {shard.seq_end}) x kv heads "
+                f"[{shard.kvh_begin}, {shard.kvh_end})" if shard is not None else ""),
             "roofline": {"bound": "tensor", "kernel": "prefill_pair_kernel", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
                          "frac_of_burst": round(achieved / burst, 4),

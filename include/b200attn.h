@@ -122,11 +122,13 @@ int b2_launch_causal_attention_prefill(const void* d_q, const void* d_k, const v
  * counterpart; the reference engine is batch 1): `batch` independent
  * sequences of seq_len tokens, sequence b's Q / K / V / out rows starting
  * q_batch_stride / kv_batch_stride / out_batch_stride elements after
- * sequence b-1's (e.g. per-sequence KV caches of one allocation). */
+ * sequence b-1's (e.g. per-sequence KV caches of one allocation). out_stride
+ * is the output row stride (0 = packed num_heads * head_dim), so a block of
+ * heads can be written into a wider output. */
 int b2_launch_causal_attention_prefill_batched(const void* d_q, const void* d_k, const void* d_v,
                                                void* d_out, size_t batch, size_t seq_len,
                                                size_t num_heads, size_t num_kv_heads, size_t head_dim,
-                                               size_t q_stride, size_t kv_stride,
+                                               size_t q_stride, size_t kv_stride, size_t out_stride,
                                                size_t q_batch_stride, size_t kv_batch_stride,
                                                size_t out_batch_stride, b2_stream_t stream);
 

@@ -37,7 +37,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_launch_rope_and_store_kv": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, S, B, P]),
     "b2_update_rope_and_store_kv_node": (I, [P, P, S, B]),
     "b2_launch_causal_attention_prefill": (I, [P, P, P, P, S, S, S, S, S, S, P]),
-    "b2_launch_causal_attention_prefill_batched": (I, [P, P, P, P, S, S, S, S, S, S, S, S, S, S, P]),
+    "b2_launch_causal_attention_prefill_batched": (I, [P, P, P, P, S, S, S, S, S, S, S, S, S, S, S, P]),
     "b2_launch_causal_attention_decode": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, S, S, P, PP, PP]),
     "b2_launch_causal_attention_decode_vectorized": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, S, S, P, PP, PP]),
     "b2_update_causal_attention_decode_node": (I, [P, P, S]),

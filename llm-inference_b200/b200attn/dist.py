@@ -57,6 +57,35 @@ def split_kv_plan(past: int, world: int, rank: int) -> SplitPlan:
     return SplitPlan(past, world, rank, begin, end)
 
 
+@dataclasses.dataclass(frozen=True)
+class PrefillShard:
+    """Rank's block of a batched prefill: sequences [seq_begin, seq_end) x KV
+    heads [kvh_begin, kvh_end), launched as one batched call."""
+    seq_begin: int
+    seq_end: int
+    kvh_begin: int
+    kvh_end: int
+
+    def units(self) -> list[tuple[int, int]]:
+        return [(b, g) for b in range(self.seq_begin, self.seq_end) for g in range(self.kvh_begin, self.kvh_end)]
+
+
+def prefill_shard(batch: int, num_kv_heads: int, world: int, rank: int) -> PrefillShard | None:
+    """Contiguous (sequence, KV head) block per rank when the batch divides
+    evenly: whole sequences while world <= batch, else each sequence's KV heads
+    split over world / batch ranks. None when no even block exists (use
+    prefill_units)."""
+    if world <= batch and batch % world == 0:
+        per = batch // world
+        return PrefillShard(rank * per, (rank + 1) * per, 0, num_kv_heads)
+    if world > batch and world % batch == 0 and num_kv_heads % (world // batch) == 0:
+        parts = world // batch
+        per = num_kv_heads // parts
+        b, p = divmod(rank, parts)
+        return PrefillShard(b, b + 1, p * per, (p + 1) * per)
+    return None
+
+
 def prefill_units(batch: int, num_kv_heads: int, world: int, rank: int) -> list[tuple[int, int]]:
     """(sequence, kv_head) units of a batched causal prefill owned by `rank`.
     Every unit has the same causal work, so a round-robin split balances."""

@@ -328,9 +328,10 @@ def launch_merge_partials_strided(d_o, d_m, d_l, d_out, num_heads, num_chunks, h
 
 def launch_causal_attention_prefill_batched(d_q, d_k, d_v, d_out, batch, seq_len, num_heads, num_kv_heads,
                                             head_dim, q_stride=0, kv_stride=0, q_batch_stride=0,
-                                            kv_batch_stride=0, out_batch_stride=0, stream=None):
-    """`batch` independent causal prefills (sequence b at the given batch strides)."""
+                                            kv_batch_stride=0, out_batch_stride=0, stream=None, out_stride=0):
+    """`batch` independent causal prefills (sequence b at the given batch strides);
+    out_stride: output row stride (0 = packed)."""
     check(lib().b2_launch_causal_attention_prefill_batched(
         _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_out), batch, seq_len, num_heads, num_kv_heads, head_dim,
-        q_stride, kv_stride, q_batch_stride, kv_batch_stride, out_batch_stride, _stream(stream)),
+        q_stride, kv_stride, out_stride, q_batch_stride, kv_batch_stride, out_batch_stride, _stream(stream)),
         "launch_causal_attention_prefill_batched")

@@ -83,6 +83,7 @@ struct DecodeArgs {
     int32_t kv_len_bias;
     uint32_t max_kv_len;
     uint32_t stages;      // TMA kernel: ring depth
+    uint32_t split_tokens;  // tokens per split before capping at the SM count (0 = KV_CHUNK)
 };
 
 struct MergeArgs {
@@ -107,6 +108,7 @@ struct MergeArgs {
     float* rank_o;
     float* rank_m;
     float* rank_l;
+    uint32_t split_tokens;  // as DecodeArgs::split_tokens
 };
 
 struct Extent {
@@ -122,7 +124,8 @@ __device__ __forceinline__ Extent decode_extent(const A& a) {
         n = n < 0 ? 0 : (n > a.max_kv_len ? a.max_kv_len : n);
         len = static_cast<uint32_t>(n);
     }
-    const uint32_t chunks = (len + kChunk - 1) / kChunk;
+    const uint32_t per = a.split_tokens ? a.split_tokens : static_cast<uint32_t>(kChunk);
+    const uint32_t chunks = (len + per - 1) / per;
     return {len, min(chunks, a.splits_cap)};
 }
 
@@ -1111,6 +1114,7 @@ MergeArgs merge_args_from(const DecodeArgs& a, __half* out, float* rank_o, float
     m.rank_o = rank_o;
     m.rank_m = rank_m;
     m.rank_l = rank_l;
+    m.split_tokens = a.split_tokens;
     return m;
 }
 
@@ -1227,8 +1231,11 @@ int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new
     if (head_dim != 128 || group > 8 ||
         !(num_kv_heads == 1 || num_kv_heads == 2 || num_kv_heads == 4 || num_kv_heads == 8))
         return B2_ERR_UNSUPPORTED;
-    const size_t chunks = (max_kv_len + kChunk - 1) / kChunk;
-    if (max_kv_len > 0x7fffffffull - kChunk || chunks > 65535 || rope_rows > 0x7fffffffull) return B2_ERR_UNSUPPORTED;
+    // splits of 64 tokens, capped at the SM count: short per-rank ranges
+    // (several GPUs) still spread over every SM
+    constexpr uint32_t kStepSplitTokens = 64;
+    const size_t chunks = (max_kv_len + kStepSplitTokens - 1) / kStepSplitTokens;
+    if (max_kv_len > 0x7fffffffull - kChunk || rope_rows > 0x7fffffffull) return B2_ERR_UNSUPPORTED;
     const void* ptrs[] = {d_q, d_k_new, d_v_new, d_k_cache, d_v_cache, d_cos, d_sin, d_out, d_rank_o, d_workspace};
     for (const void* p : ptrs)
         if (p && !aligned16(p)) return B2_ERR_ALIGNMENT;
@@ -1259,6 +1266,7 @@ int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new
     a.kv_len_dev = d_kv_len;
     a.kv_len_bias = kv_len_bias;
     a.max_kv_len = static_cast<uint32_t>(max_kv_len);
+    a.split_tokens = kStepSplitTokens;
     a.stages = tma_stages(a.num_kv_heads);
     if (a.stages == 0) return B2_ERR_UNSUPPORTED;
 

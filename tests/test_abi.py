@@ -175,7 +175,7 @@ def test_fused_decode_step_validation_without_cuda():
     # NoPE needs none of them: this call gets as far as the workspace check
     assert call(rot=False, cos=None, sin=None, pos=None, rows=0, wb=ws - 1) == -5
     assert call(d=64) == -2 and call(h=48, kvh=4) == -2 and call(kvh=16, h=16) == -2
-    assert call(cap=65536 * 256 + 1) == -2
+    assert call(cap=1 << 31) == -2
     assert call(kc=f + 2) == -3 and call(w=f + 8) == -3
     assert call(wb=ws - 1) == -5
     r = L.b2_launch_decode_step_fused_rank_partial(f, None, None, f, f, f, f, 100, True, f, f, 0, 99, None, f, f, f,

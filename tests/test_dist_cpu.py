@@ -37,6 +37,18 @@ def test_assign_sequences_balanced_and_complete():
         assert max(loads) - min(loads) <= int(lens.max())
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_prefill_shard_blocks_partition(world):
+    """Config 3 (4 sequences x 4 KV heads): every (sequence, KV head) unit
+    belongs to exactly one rank's contiguous block, equal work per rank."""
+    shards = [bdist.prefill_shard(4, 4, world, r) for r in range(world)]
+    assert all(sh is not None for sh in shards)
+    units = [u for sh in shards for u in sh.units()]
+    assert sorted(units) == [(b, g) for b in range(4) for g in range(4)]
+    assert len({len(sh.units()) for sh in shards}) == 1
+    assert bdist.prefill_shard(4, 4, 3, 0) is None
+
+
 def test_prefill_units_partition():
     for world in (1, 2, 4, 8):
         units = [bdist.prefill_units(4, 4, world, r) for r in range(world)]

@@ -140,3 +140,27 @@ def test_prefill_config3_unit_sampled(cuda, S):
     rows = sorted(set([0, 127, 128, 4095, 4096, S - 1] + list(rng.integers(0, S, 24))))
     _, o32 = oracle.causal_attention(q, k, v, S, H, KVH, d, rows=rows)
     assert_attention_close(got[rows], o32)
+
+
+def test_prefill_batched_head_block_into_wider_output(cuda):
+    """One rank's block of KV heads (the multi-GPU prefill split): heads of KV
+    heads [2, 4) written into the full-width output rows (out_stride), other
+    heads' columns untouched."""
+    import torch
+    B, S, H, KVH, d = 2, 300, 16, 4, 128
+    G = H // KVH
+    q = seeded_f16((B, S, H * d), 91)
+    k = seeded_f16((B, S, KVH * d), 92)
+    v = seeded_f16((B, S, KVH * d), 93)
+    out = torch.full((B, S, H * d), -5.0, dtype=torch.float16, device=cuda)
+    dq, dk, dv = dev(q), dev(k), dev(v)
+    g0, ng = 2, 2
+    b200attn.launch_causal_attention_prefill_batched(dq[:, :, g0 * G * d:], dk[:, :, g0 * d:], dv[:, :, g0 * d:],
+                                                     out[:, :, g0 * G * d:], B, S, ng * G, ng, d, H * d, KVH * d,
+                                                     S * H * d, S * KVH * d, S * H * d, out_stride=H * d)
+    _sync()
+    got = host(out)
+    assert np.all(got[:, :, :g0 * G * d] == np.float16(-5.0))
+    for b in range(B):
+        _, o32 = oracle.causal_attention(q[b], k[b], v[b], S, H, KVH, d)
+        assert_attention_close(got[b, :, g0 * G * d:], o32[:, g0 * G * d:])

@@ -241,18 +241,6 @@ __device__ __forceinline__ uint2 ld_pair_sys(const uint2* p) {
     return v;
 }
 
-// Bounded poll of one exchange word until it carries exchange number e.
-__device__ __forceinline__ bool poll_pair(const uint2* p, uint32_t e, uint64_t t0, float& v) {
-    uint2 w = ld_pair_sys(p);
-    while (w.y != e) {
-        if (global_timer_ns() - t0 > kWaitBudgetNs) return false;
-        __nanosleep(20);
-        w = ld_pair_sys(p);
-    }
-    v = __uint_as_float(w.x);
-    return true;
-}
-
 // Publish this rank's partial (O over the 128 dims held by threads 0..127,
 // M, L) of head h to every rank, wait (bounded) for every rank's partial of
 // head h for exchange e, and write the merged fp16 output. Threads 0..127
@@ -270,21 +258,45 @@ __device__ __noinline__ bool step_exchange_head(const StepExt& x, uint32_t H, ui
             st_pair_sys(dst + 129, L, e);
         }
     }
+    // every rank's words of this head, all loads in flight at once; only the
+    // words that do not carry exchange e yet are read again
     const uint2* own = reinterpret_cast<const uint2*>(x.peers[x.rank]);
     const uint64_t t0 = global_timer_ns();
     float mv[kMaxWorld], lv[kMaxWorld], ov[kMaxWorld];
-    bool ok = true;
+    uint2 wo[kMaxWorld], wm[kMaxWorld], wl[kMaxWorld];
 #pragma unroll
-    for (uint32_t r = 0; r < kMaxWorld; ++r) {
-        if (r < world && ok) {
-            const uint2* src = own + ((static_cast<uint64_t>(slot) * world + r) * H + h) * kExchangePitch;
-            ok = poll_pair(src + d, e, t0, ov[r]) && poll_pair(src + 128, e, t0, mv[r]) &&
-                 poll_pair(src + 129, e, t0, lv[r]);
+    for (uint32_t r = 0; r < kMaxWorld; ++r) wo[r] = wm[r] = wl[r] = make_uint2(0u, e + 1u);  // not yet read
+    bool ok = true;
+    for (;;) {
+        bool ready = true;
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxWorld; ++r) {
+            if (r < world) {
+                const uint2* src = own + ((static_cast<uint64_t>(slot) * world + r) * H + h) * kExchangePitch;
+                if (wo[r].y != e) wo[r] = ld_pair_sys(src + d);
+                if (wm[r].y != e) wm[r] = ld_pair_sys(src + 128);
+                if (wl[r].y != e) wl[r] = ld_pair_sys(src + 129);
+            }
         }
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxWorld; ++r)
+            if (r < world) ready = ready && wo[r].y == e && wm[r].y == e && wl[r].y == e;
+        if (ready) break;
+        if (global_timer_ns() - t0 > kWaitBudgetNs) {
+            ok = false;
+            break;
+        }
+        __nanosleep(20);
     }
     if (!ok) {
         atomicOr(&g_device_error, kErrWaitTimeout);
         return false;
+    }
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxWorld; ++r) {
+        ov[r] = __uint_as_float(wo[r].x);
+        mv[r] = __uint_as_float(wm[r].x);
+        lv[r] = __uint_as_float(wl[r].x);
     }
     float Mx = -INFINITY;
 #pragma unroll

@@ -120,7 +120,8 @@ template <class A>
 __device__ __forceinline__ Extent decode_extent(const A& a) {
     uint32_t len = a.kv_len;
     if (a.kv_len_dev != nullptr) {
-        int64_t n = static_cast<int64_t>(__ldg(a.kv_len_dev)) + a.kv_len_bias;
+        // L2 load: the value may have been written by the kernel this one overlapped
+        int64_t n = static_cast<int64_t>(__ldcg(a.kv_len_dev)) + a.kv_len_bias;
         n = n < 0 ? 0 : (n > a.max_kv_len ? a.max_kv_len : n);
         len = static_cast<uint32_t>(n);
     }
@@ -200,6 +201,10 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
@@ -332,11 +337,16 @@ __device__ __forceinline__ void step_write_empty(uint32_t H, const StepExt& x, u
 // Every CTA has written its partials [H][S][128] / [H][S] (natural-log m).
 // The last R = min(S, H) CTAs to arrive each merge the heads r, r + R, ... of
 // all S partials once the remaining CTAs have arrived; every CTA they wait for
-// has already started, so the wait needs no co-residency beyond R CTAs. Warp w
-// of a merging CTA folds partials w, w + 13, ... for 4 dims per lane; the 13
-// warp states meet in shared memory `wsm` (13 x 132 floats). The last merging
-// CTA resets the counters for the next launch.
-__device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, float* wsm) {
+// has already started, so the wait needs no co-residency beyond R CTAs. The
+// last CTA to arrive resets the tile and arrival counters for the next launch
+// (no CTA reads them again) and then advances the generation word
+// counters[2] with a release store; the other merging CTAs wait for the
+// generation to move past gen0, the value every CTA read after its dependency
+// wait. Warp w of a merging CTA folds partials w, w + 13, ... for 4 dims per
+// lane; the 13 warp states meet in shared memory `wsm` (13 x 132 floats).
+// epoch_next: the exchange number of this launch (world > 1).
+__device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, float* wsm,
+                                           uint32_t gen0, uint32_t epoch_next) {
     __shared__ uint32_t role_s;
     const uint32_t H = a.num_heads;
     const uint32_t R = min(S, H);
@@ -344,27 +354,30 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
     __syncthreads();
     if (threadIdx.x == 0) {
         const uint32_t k = atom_add_acq_rel_gpu(&x.counters[1], 1u);
-        role_s = k + R >= S ? k + R - S : 0xffffffffu;
+        uint32_t role = k + R >= S ? k + R - S : 0xffffffffu;
+        if (k == S - 1) {
+            x.counters[0] = 0u;
+            x.counters[1] = 0u;
+            if (x.world > 1) *x.epoch = epoch_next;
+            st_release_gpu(&x.counters[2], gen0 + 1u);
+        } else if (role != 0xffffffffu) {
+            const uint64_t t0 = global_timer_ns();
+            while (ld_acquire_gpu(&x.counters[2]) == gen0) {
+                if (global_timer_ns() - t0 > kWaitBudgetNs) {
+                    atomicOr(&g_device_error, kErrWaitTimeout);
+                    role = 0xffffffffu;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        role_s = role;
     }
     __syncthreads();
     const uint32_t r = role_s;
     if (r == 0xffffffffu) return;
-    if (threadIdx.x == 0) {
-        const uint64_t t0 = global_timer_ns();
-        while (ld_acquire_gpu(&x.counters[1]) < S) {
-            if (global_timer_ns() - t0 > kWaitBudgetNs) {
-                atomicOr(&g_device_error, kErrWaitTimeout);
-                role_s = 0xffffffffu;
-                break;
-            }
-            __nanosleep(64);
-        }
-    }
-    __syncthreads();
-    if (role_s == 0xffffffffu) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kWarps = kTmaThreads / 32;
-    const uint32_t epoch_next = x.world > 1 ? *x.epoch + 1 : 0u;
     float O_keep = 0.f, M_keep = -INFINITY, L_keep = 0.f;
     for (uint32_t h = r; h < H; h += R) {
         const float* po = a.po + static_cast<uint64_t>(h) * S * 128 + lane * 4;
@@ -433,16 +446,6 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
         __syncthreads();
         if (x.world > 1) (void)step_exchange_head(x, H, h, epoch_next, O_keep, M_keep, L_keep);
     }
-    // the last merging CTA leaves the counters at zero for the next launch
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(&x.counters[2], 1u) == R - 1) {
-            x.counters[0] = 0u;
-            x.counters[1] = 0u;
-            x.counters[2] = 0u;
-            if (x.world > 1) *x.epoch = epoch_next;
-        }
-    }
 }
 
 constexpr uint32_t kAppendBarrier = 1;  // named barrier: appending consumer warp -> producer warp
@@ -476,6 +479,72 @@ __device__ __forceinline__ uint8_t* stg_of(uint8_t* ring, uint32_t s, uint32_t t
     return ring + s * 2 * tile_bytes;
 }
 
+// Combine of one split's consumer warp states into its partial. The warps of
+// KV head h are h, h + KVH, ... (one per tile parity); warps of parity >= 1
+// leave their state in shared memory `sm` and the parity-0 warp of each KV
+// head folds them into its own registers -- every lane reads the fragment
+// positions it holds itself -- and writes the partial from registers:
+// po [head][splits][128], pm (natural-log max) and pl [head][splits].
+// Every thread of the CTA calls it (one barrier when npar > 1).
+template <uint32_t KVH>
+__device__ __forceinline__ void combine_split(WarpState& st, uint32_t warp, uint32_t lane, float* sm, uint32_t group,
+                                              uint32_t split, uint32_t splits, float* po, float* pm, float* pl) {
+    constexpr uint32_t npar = kTmaConsumers / KVH;
+    float* sm_m = sm;                        // [slot][8]
+    float* sm_l = sm_m + kTmaConsumers * 8;  // [slot][8]
+    float* sm_o = sm_l + kTmaConsumers * 8;  // [slot][8][kOStride]
+    const int g = static_cast<int>(lane >> 2), t = static_cast<int>(lane & 3);
+    if constexpr (npar > 1) {
+        if (warp >= KVH && warp < KVH * npar) state_to_smem(st, static_cast<int>(warp), sm_m, sm_l, sm_o, g, t);
+        __syncthreads();
+    }
+    if (warp >= KVH) return;
+    float M0 = st.m0, M1 = st.m1;
+#pragma unroll
+    for (uint32_t j = 1; j < npar; ++j) {
+        const uint32_t slot = warp + KVH * j;
+        M0 = fmaxf(M0, sm_m[slot * 8 + 2 * t]);
+        M1 = fmaxf(M1, sm_m[slot * 8 + 2 * t + 1]);
+    }
+    if constexpr (npar > 1) {
+        const float a0 = st.m0 == -INFINITY ? 0.f : ex2(st.m0 - M0);
+        const float a1 = st.m1 == -INFINITY ? 0.f : ex2(st.m1 - M1);
+        float L0 = st.l0 * a0, L1 = st.l1 * a1;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            st.o[mt][0] *= a0;
+            st.o[mt][2] *= a0;
+            st.o[mt][1] *= a1;
+            st.o[mt][3] *= a1;
+        }
+#pragma unroll
+        for (uint32_t j = 1; j < npar; ++j) {
+            const uint32_t slot = warp + KVH * j;
+            const float m0 = sm_m[slot * 8 + 2 * t], m1 = sm_m[slot * 8 + 2 * t + 1];
+            const float s0 = m0 == -INFINITY ? 0.f : ex2(m0 - M0);
+            const float s1 = m1 == -INFINITY ? 0.f : ex2(m1 - M1);
+            L0 = fmaf(s0, sm_l[slot * 8 + 2 * t], L0);
+            L1 = fmaf(s1, sm_l[slot * 8 + 2 * t + 1], L1);
+            const float* o0 = sm_o + (slot * 8 + 2 * t) * kOStride;
+            const float* o1 = o0 + kOStride;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                const int d = 64 * (mt >> 2) + 8 * g + 2 * (mt & 3);
+                st.o[mt][0] = fmaf(s0, o0[d], st.o[mt][0]);
+                st.o[mt][1] = fmaf(s1, o1[d], st.o[mt][1]);
+                st.o[mt][2] = fmaf(s0, o0[d + 1], st.o[mt][2]);
+                st.o[mt][3] = fmaf(s1, o1[d + 1], st.o[mt][3]);
+            }
+        }
+        st.m0 = M0;
+        st.m1 = M1;
+        st.l0 = L0;
+        st.l1 = L1;
+    }
+    store_warp_partial(st, po, pm, pl, static_cast<uint64_t>(splits) * 128, 128, splits, 1, split, warp * group,
+                       group, g, t);
+}
+
 template <bool kFused, uint32_t KVH>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     decode_tma_kernel(const DecodeArgs a, const StepExt x, const __grid_constant__ CUtensorMap map_k,
@@ -484,34 +553,64 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     __shared__ uint32_t stage_valid[32];  // kFused: rows of the tile in each stage, 0 = no more tiles
     constexpr uint32_t row_bytes = KVH * 256;          // one token, all KV heads
     constexpr uint32_t tile_bytes = kTile * row_bytes; // per K (and per V): [2*KVH blocks][16 rows][128 B]
-    if (threadIdx.x >= kTmaConsumers * 32 && threadIdx.x < kTmaConsumers * 32 + 2 * kPrefetchTiles) {
-        // While the previous kernel finishes, start pulling this CTA's first
-        // tiles into L2. The length read here may be stale (it can be the
-        // previous kernel's output); a prefetch only warms L2, so any tile
-        // below max_kv_len is harmless.
-        const Extent pre = decode_extent(a);
-        if (split_index_ok(pre, blockIdx.x)) {
-            uint32_t first, count;
-            own_tiles(pre, blockIdx.x, kFused, first, count);
-            const uint32_t j = (threadIdx.x - kTmaConsumers * 32) >> 1;
-            if (j < count) {
-                const uint64_t off = static_cast<uint64_t>(first + j) * tile_bytes;
-                bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((threadIdx.x & 1) ? a.v : a.k) + off, tile_bytes);
+    const uint32_t stages = a.stages;
+    // 128-byte swizzled TMA boxes want 1024-byte aligned destinations
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * 2 * tile_bytes);
+    uint64_t* empty = full + stages;
+    constexpr uint32_t npar = kTmaConsumers / KVH;     // consumer warps per KV head; divides `stages`
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // While the previous kernel finishes (nothing here depends on its output):
+    // barriers, tensor-map prefetch, and this CTA's first tiles pulled into
+    // L2. The length read for the prefetch may be stale (it can be the
+    // previous kernel's output); a prefetch only warms L2, so any tile below
+    // max_kv_len is harmless.
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], KVH);
+        }
+        fence_mbarrier_init();
+    }
+    if (warp == kTmaConsumers) {
+        if (lane == 0) {
+            tc::prefetch_tensormap(&map_k);
+            tc::prefetch_tensormap(&map_v);
+        }
+        if (lane < 2 * kPrefetchTiles) {
+            const Extent pre = decode_extent(a);
+            if (split_index_ok(pre, blockIdx.x)) {
+                uint32_t first, count;
+                own_tiles(pre, blockIdx.x, kFused, first, count);
+                const uint32_t j = static_cast<uint32_t>(lane) >> 1;
+                if (j < count) {
+                    const uint64_t off = static_cast<uint64_t>(first + j) * tile_bytes;
+                    bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((lane & 1) ? a.v : a.k) + off, tile_bytes);
+                }
             }
         }
     }
+    __syncthreads();
     pdl_wait_primary();  // Q, the cache and the device length may come from the previous kernel
     pdl_launch_dependents();
+    // every load that only depends on the previous kernel goes out at once
+    int32_t pos = 0;
+    uint32_t gen0 = 0, epoch_next = 0;
+    if (kFused) {
+        if (x.pos_dev != nullptr) pos = __ldcg(x.pos_dev);
+        if (threadIdx.x == 0) gen0 = __ldcg(&x.counters[2]);
+        if (x.world > 1) epoch_next = __ldcg(x.epoch) + 1u;
+    }
     const Extent ext = decode_extent(a);
     const uint32_t split = blockIdx.x;
     if (kFused && ext.splits == 0) {  // empty cache: defined output
         if (split == 0) {
             if (x.world > 1) {
                 // nothing to attend here, but the other ranks wait for this rank's partials
-                const uint32_t e = *x.epoch + 1;
                 for (uint32_t h = 0; h < a.num_heads; ++h)
-                    (void)step_exchange_head(x, a.num_heads, h, e, 0.f, -INFINITY, 0.f);
-                if (threadIdx.x == 0) *x.epoch = e;
+                    (void)step_exchange_head(x, a.num_heads, h, epoch_next, 0.f, -INFINITY, 0.f);
+                if (threadIdx.x == 0) *x.epoch = epoch_next;
             } else {
                 step_write_empty(a.num_heads, x, threadIdx.x, blockDim.x);
             }
@@ -521,29 +620,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (split >= ext.splits) return;
     uint32_t begin, end;
     split_range(ext.kv_len, ext.splits, split, begin, end);
-
-    const uint32_t stages = a.stages;
-    // 128-byte swizzled TMA boxes want 1024-byte aligned destinations
-    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * 2 * tile_bytes);
-    uint64_t* empty = full + stages;
     const uint32_t ntiles = (end - begin + kTile - 1) / kTile;
-    constexpr uint32_t npar = kTmaConsumers / KVH;     // consumer warps per KV head; divides `stages`
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], KVH);
-        }
-        fence_mbarrier_init();
-    }
-    __syncthreads();
-
-    int32_t pos = 0;
     bool rope_ok = true;
     if (kFused) {
-        if (x.pos_dev != nullptr) pos = __ldg(x.pos_dev);
         rope_ok = !x.rotate || (pos >= 0 && static_cast<uint32_t>(pos) < x.table_rows);
         if (!rope_ok && split == 0 && threadIdx.x == 0) atomicOr(&g_device_error, kErrBadPosition);
     }
@@ -553,10 +633,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     state_init(st);
     if (warp == kTmaConsumers) {
         // ---- producer warp
-        if (lane == 0) {
-            tc::prefetch_tensormap(&map_k);
-            tc::prefetch_tensormap(&map_v);
-        }
         const uint64_t policy = l2_evict_first_policy();
         uint32_t i = 0;
         if constexpr (kFused) {
@@ -752,16 +828,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     // All ring reads and copies are done: reuse the ring for the combine.
     __syncthreads();
-    float* sm_m = reinterpret_cast<float*>(ring);
-    float* sm_l = sm_m + kTmaConsumers * 8;
-    float* sm_o = sm_l + kTmaConsumers * 8;
-    if (warp < kTmaConsumers) state_to_smem(st, warp, sm_m, sm_l, sm_o, lane >> 2, lane & 3);
-    __syncthreads();
-    // Slots of KV head h are h, h + KVH, ...: combine and write the partials.
-    combine_tile2_any(npar, sm_m, sm_l, sm_o, sm_o + kTmaConsumers * 8 * kOStride, KVH, a.group, split, ext.splits,
-                      a.po, a.pm, a.pl, threadIdx.x, kTmaThreads);
+    combine_split<KVH>(st, static_cast<uint32_t>(warp), static_cast<uint32_t>(lane), reinterpret_cast<float*>(ring),
+                       a.group, split, ext.splits, a.po, a.pm, a.pl);
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
-    if constexpr (kFused) step_merge(a, x, ext.splits, reinterpret_cast<float*>(ring));
+    if constexpr (kFused) step_merge(a, x, ext.splits, reinterpret_cast<float*>(ring), gen0, epoch_next);
 }
 
 // ---------------------------------------------------------------------------

@@ -285,9 +285,9 @@ int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream);
  *  - head_dim 128, num_kv_heads in {1,2,4,8}, num_heads / num_kv_heads <= 8;
  *    16-byte aligned pointers. Other shapes return B2_ERR_UNSUPPORTED.
  *  - d_workspace holds b2_decode_step_workspace_bytes(num_heads, num_kv_heads)
- *    bytes (split partials, two counters and a generation word) and must be
- *    ZERO-FILLED once before its first use; each call leaves its counters at
- *    zero again and advances the generation word. One workspace
+ *    bytes (split partials and three counter words) and must be ZERO-FILLED
+ *    once before its first use; each call leaves the words consistent for the
+ *    next (after a device error bit 0, zero it again). One workspace
  *    serves any number of calls ordered on one stream (e.g. every layer of a
  *    captured step); calls that can overlap on the GPU need separate
  *    workspaces. */

@@ -195,22 +195,11 @@ __device__ __forceinline__ void rot8_pairs(uint4& lo, uint4& hi, uint4 cv, uint4
 // registers, and the CTA that claims the tile holding row kv_len - 1 appends
 // the new token's K/V there before copying that tile.
 // ---- in-kernel merge of the fused step -------------------------------------
-constexpr uint32_t kStepBatch = 12;  // partials one warp loads at once
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
 }
 
 __device__ __forceinline__ void step_store(const StepExt& x, uint32_t h, uint32_t d, float o, float M, float L) {
@@ -334,117 +323,110 @@ __device__ __forceinline__ void step_write_empty(uint32_t H, const StepExt& x, u
     }
 }
 
-// Every CTA has written its partials [H][S][128] / [H][S] (natural-log m).
-// The last R = min(S, H) CTAs to arrive each merge the heads r, r + R, ... of
-// all S partials once the remaining CTAs have arrived; every CTA they wait for
-// has already started, so the wait needs no co-residency beyond R CTAs. The
-// last CTA to arrive resets the tile and arrival counters for the next launch
-// (no CTA reads them again) and then advances the generation word
-// counters[2] with a release store; the other merging CTAs wait for the
-// generation to move past gen0, the value every CTA read after its dependency
-// wait. Warp w of a merging CTA folds partials w, w + 13, ... for 4 dims per
-// lane; the 13 warp states meet in shared memory `wsm` (13 x 132 floats).
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Every CTA has written its partials [H][S][128] / [H][S] (natural-log m)
+// and adds one to the arrival counter counters[1] with a release reduction;
+// the counter only grows, and counters[2] holds its value at the start of
+// the launch (`base`, read after the dependency wait). Splits r < R =
+// min(S, H) merge heads r, r + R, ...: once the counter reaches base + S
+// (acquire) the CTA copies the head's S partial rows into shared memory with
+// one bulk copy while its threads reduce the S maxima and weight sums, then
+// 384 threads sum the weighted rows (three interleaved partial sets per dim).
+// Merging split 0 resets the tile counter and records base + S for the next
+// launch (no other CTA reads either word again in this launch). The merging
+// CTAs wait for CTAs that may start after them, which every launch can
+// schedule: there is one CTA per SM and at most as many CTAs as SMs.
 // epoch_next: the exchange number of this launch (world > 1).
-__device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, float* wsm,
-                                           uint32_t gen0, uint32_t epoch_next) {
-    __shared__ uint32_t role_s;
+__device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, uint32_t split,
+                                           uint8_t* smem, uint64_t* bar, uint32_t base, uint32_t epoch_next) {
+    __shared__ uint32_t ok_s;
+    __shared__ float red_s[2][kTmaThreads / 32];
     const uint32_t H = a.num_heads;
     const uint32_t R = min(S, H);
-    // the CTA's partial stores happen before thread 0's release increment
+    // the CTA's partial stores happen before thread 0's release
     __syncthreads();
+    const bool merger = split < R;
     if (threadIdx.x == 0) {
-        const uint32_t k = atom_add_acq_rel_gpu(&x.counters[1], 1u);
-        uint32_t role = k + R >= S ? k + R - S : 0xffffffffu;
-        if (k == S - 1) {
-            x.counters[0] = 0u;
-            x.counters[1] = 0u;
-            if (x.world > 1) *x.epoch = epoch_next;
-            st_release_gpu(&x.counters[2], gen0 + 1u);
-        } else if (role != 0xffffffffu) {
+        red_add_release_gpu(&x.counters[1], 1u);
+        if (merger) {
+            uint32_t ok = 1u;
             const uint64_t t0 = global_timer_ns();
-            while (ld_acquire_gpu(&x.counters[2]) == gen0) {
+            while (ld_acquire_gpu(&x.counters[1]) - base < S) {
                 if (global_timer_ns() - t0 > kWaitBudgetNs) {
                     atomicOr(&g_device_error, kErrWaitTimeout);
-                    role = 0xffffffffu;
+                    ok = 0u;
                     break;
                 }
                 __nanosleep(32);
             }
+            if (ok && split == 0) {
+                x.counters[0] = 0u;
+                x.counters[2] = base + S;
+                if (x.world > 1) *x.epoch = epoch_next;
+            }
+            // the partials were written through the generic proxy; the bulk
+            // copies below read them through the async proxy
+            fence_proxy_async_global();
+            ok_s = ok;
         }
-        role_s = role;
     }
+    if (!merger) return;
     __syncthreads();
-    const uint32_t r = role_s;
-    if (r == 0xffffffffu) return;
+    if (ok_s == 0u) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kWarps = kTmaThreads / 32;
-    float O_keep = 0.f, M_keep = -INFINITY, L_keep = 0.f;
-    for (uint32_t h = r; h < H; h += R) {
-        const float* po = a.po + static_cast<uint64_t>(h) * S * 128 + lane * 4;
-        const float* pm = a.pm + static_cast<uint64_t>(h) * S;
-        const float* pl = a.pl + static_cast<uint64_t>(h) * S;
-        float M = -INFINITY, L = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t base = warp; base < S; base += kWarps * kStepBatch) {
-            float mv[kStepBatch], lv[kStepBatch];
-            float4 ov[kStepBatch];
-#pragma unroll
-            for (uint32_t u = 0; u < kStepBatch; ++u) {
-                const uint32_t c = base + u * kWarps;
-                mv[u] = c < S ? __ldcg(pm + c) : -INFINITY;
-                lv[u] = c < S ? __ldcg(pl + c) : 0.f;
-                ov[u] = c < S ? __ldcg(reinterpret_cast<const float4*>(po + static_cast<uint64_t>(c) * 128))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            float bm = M;
-#pragma unroll
-            for (uint32_t u = 0; u < kStepBatch; ++u) bm = fmaxf(bm, mv[u]);
-            if (bm == -INFINITY) continue;
-            const float sc = M == -INFINITY ? 0.f : expf(M - bm);
-            acc.x *= sc;
-            acc.y *= sc;
-            acc.z *= sc;
-            acc.w *= sc;
-            L *= sc;
-            M = bm;
-#pragma unroll
-            for (uint32_t u = 0; u < kStepBatch; ++u) {
-                const float w = mv[u] == -INFINITY ? 0.f : expf(mv[u] - M);
-                acc.x = fmaf(w, ov[u].x, acc.x);
-                acc.y = fmaf(w, ov[u].y, acc.y);
-                acc.z = fmaf(w, ov[u].z, acc.z);
-                acc.w = fmaf(w, ov[u].w, acc.w);
-                L = fmaf(w, lv[u], L);
-            }
+    float* rows = reinterpret_cast<float*>(smem);  // [S][128]
+    float* wts = rows + static_cast<size_t>(S) * 128;  // [S]
+    float* sums = wts + kStepMaxSplits;               // [3][128]
+    uint32_t phase = 0;
+    for (uint32_t h = split; h < H; h += R, phase ^= 1u) {
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(bar, S * 512u);
+            bulk_g2s_plain(rows, a.po + static_cast<uint64_t>(h) * S * 128, S * 512u, bar);
         }
-        constexpr uint32_t kPitch = 132;  // floats per warp state: o[128], M, L (16-byte rows)
-        float* mine = wsm + warp * kPitch;
-        *reinterpret_cast<float4*>(mine + lane * 4) = acc;
-        if (lane == 0) {
-            mine[128] = M;
-            mine[129] = L;
+        const uint32_t c = threadIdx.x;
+        const float m = c < S ? __ldcg(a.pm + static_cast<uint64_t>(h) * S + c) : -INFINITY;
+        const float l = c < S ? __ldcg(a.pl + static_cast<uint64_t>(h) * S + c) : 0.f;
+        float v = m;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) red_s[0][warp] = v;
+        __syncthreads();
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, red_s[0][w]);
+        const float wt = m == -INFINITY ? 0.f : expf(m - M);
+        if (c < S) wts[c] = wt;
+        v = wt * l;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) red_s[1][warp] = v;
+        (void)mbar_wait(bar, phase);
+        __syncthreads();
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) L += red_s[1][w];
+        if (threadIdx.x < 384) {
+            const uint32_t q = threadIdx.x >> 7, d = threadIdx.x & 127;
+            float acc = 0.f;
+            for (uint32_t cc = q; cc < S; cc += 3) acc = fmaf(wts[cc], rows[cc * 128 + d], acc);
+            sums[q * 128 + d] = acc;
         }
         __syncthreads();
         if (threadIdx.x < 128) {
             const uint32_t d = threadIdx.x;
-            float Mx = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) Mx = fmaxf(Mx, wsm[w * kPitch + 128]);
-            float O = 0.f, Lx = 0.f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const float m = wsm[w * kPitch + 128];
-                const float sc = m == -INFINITY ? 0.f : expf(m - Mx);
-                O = fmaf(sc, wsm[w * kPitch + d], O);
-                Lx = fmaf(sc, wsm[w * kPitch + 129], Lx);
-            }
-            if (x.world <= 1) step_store(x, h, d, O, Mx, Lx);
-            O_keep = O;
-            M_keep = Mx;
-            L_keep = Lx;
+            const float O = sums[d] + sums[128 + d] + sums[256 + d];
+            if (x.world <= 1) step_store(x, h, d, O, M, L);
+            else (void)step_exchange_head(x, H, h, epoch_next, O, M, L);
         }
-        __syncthreads();
-        if (x.world > 1) (void)step_exchange_head(x, H, h, epoch_next, O_keep, M_keep, L_keep);
+        __syncthreads();  // rows, weights and sums are reused by the next head
     }
 }
 
@@ -551,6 +533,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                       const __grid_constant__ CUtensorMap map_v) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t stage_valid[32];  // kFused: rows of the tile in each stage, 0 = no more tiles
+    __shared__ uint64_t merge_bar;        // kFused: bulk copies of the merge
     constexpr uint32_t row_bytes = KVH * 256;          // one token, all KV heads
     constexpr uint32_t tile_bytes = kTile * row_bytes; // per K (and per V): [2*KVH blocks][16 rows][128 B]
     const uint32_t stages = a.stages;
@@ -571,6 +554,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], KVH);
         }
+        if (kFused) mbar_init(&merge_bar, 1);
         fence_mbarrier_init();
     }
     if (warp == kTmaConsumers) {
@@ -596,10 +580,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     pdl_launch_dependents();
     // every load that only depends on the previous kernel goes out at once
     int32_t pos = 0;
-    uint32_t gen0 = 0, epoch_next = 0;
+    uint32_t base = 0, epoch_next = 0;
     if (kFused) {
         if (x.pos_dev != nullptr) pos = __ldcg(x.pos_dev);
-        if (threadIdx.x == 0) gen0 = __ldcg(&x.counters[2]);
+        if (threadIdx.x == 0) base = __ldcg(&x.counters[2]);
         if (x.world > 1) epoch_next = __ldcg(x.epoch) + 1u;
     }
     const Extent ext = decode_extent(a);
@@ -831,7 +815,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     combine_split<KVH>(st, static_cast<uint32_t>(warp), static_cast<uint32_t>(lane), reinterpret_cast<float*>(ring),
                        a.group, split, ext.splits, a.po, a.pm, a.pl);
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
-    if constexpr (kFused) step_merge(a, x, ext.splits, reinterpret_cast<float*>(ring), gen0, epoch_next);
+    if constexpr (kFused) {
+        // the merging CTAs read these partials with bulk (async-proxy) copies
+        if (warp < static_cast<int>(KVH)) fence_proxy_async_global();
+        step_merge(a, x, ext.splits, split, ring, &merge_bar, base, epoch_next);
+    }
 }
 
 // ---------------------------------------------------------------------------

@@ -338,7 +338,8 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // min(S, H) merge heads r, r + R, ...: once the counter reaches base + S
 // (acquire) the CTA copies the head's S partial rows into shared memory with
 // one bulk copy while its threads reduce the S maxima and weight sums, then
-// 384 threads sum the weighted rows (three interleaved partial sets per dim).
+// 12 warps sum the weighted rows (rows w, w + 12, ... in warp w, four dims
+// per lane) and 128 threads add the 12 sums.
 // Merging split 0 resets the tile counter and records base + S for the next
 // launch (no other CTA reads either word again in this launch). The merging
 // CTAs wait for CTAs that may start after them, which every launch can
@@ -364,7 +365,6 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
                     ok = 0u;
                     break;
                 }
-                __nanosleep(32);
             }
             if (ok && split == 0) {
                 x.counters[0] = 0u;
@@ -384,7 +384,7 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
     constexpr int kWarps = kTmaThreads / 32;
     float* rows = reinterpret_cast<float*>(smem);  // [S][128]
     float* wts = rows + static_cast<size_t>(S) * 128;  // [S]
-    float* sums = wts + kStepMaxSplits;               // [3][128]
+    float* sums = wts + kStepMaxSplits;               // [12][128]
     uint32_t phase = 0;
     for (uint32_t h = split; h < H; h += R, phase ^= 1u) {
         if (threadIdx.x == 0) {
@@ -413,16 +413,26 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
         float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) L += red_s[1][w];
-        if (threadIdx.x < 384) {
-            const uint32_t q = threadIdx.x >> 7, d = threadIdx.x & 127;
-            float acc = 0.f;
-            for (uint32_t cc = q; cc < S; cc += 3) acc = fmaf(wts[cc], rows[cc * 128 + d], acc);
-            sums[q * 128 + d] = acc;
+        if (warp < 12) {
+            // warp w sums rows w, w + 12, ... for dims 4*lane .. 4*lane + 3
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+            for (uint32_t cc = warp; cc < S; cc += 12) {
+                const float wc = wts[cc];
+                const float4 r4 = reinterpret_cast<const float4*>(rows + cc * 128)[lane];
+                acc.x = fmaf(wc, r4.x, acc.x);
+                acc.y = fmaf(wc, r4.y, acc.y);
+                acc.z = fmaf(wc, r4.z, acc.z);
+                acc.w = fmaf(wc, r4.w, acc.w);
+            }
+            reinterpret_cast<float4*>(sums + warp * 128)[lane] = acc;
         }
         __syncthreads();
         if (threadIdx.x < 128) {
             const uint32_t d = threadIdx.x;
-            const float O = sums[d] + sums[128 + d] + sums[256 + d];
+            float O = 0.f;
+#pragma unroll
+            for (int w = 0; w < 12; ++w) O += sums[w * 128 + d];
             if (x.world <= 1) step_store(x, h, d, O, M, L);
             else (void)step_exchange_head(x, H, h, epoch_next, O, M, L);
         }
@@ -431,7 +441,8 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
 }
 
 constexpr uint32_t kAppendBarrier = 1;  // named barrier: appending consumer warp -> producer warp
-constexpr uint32_t kPrefetchTiles = 8;  // tiles per CTA warmed in L2 before the dependency wait
+constexpr uint32_t kPrefetchTiles = 4;  // tiles per CTA warmed in L2 before the dependency wait
+constexpr uint32_t kPostPrefetchTiles = 4;  // and the next ones, right after it
 
 // Fused kernel: tiles dealt out evenly to each split before the claimed pool.
 __device__ __forceinline__ uint32_t fused_share(uint32_t total_tiles, uint32_t splits) {
@@ -633,7 +644,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             const uint32_t pool = per * ext.splits, pool_end = total - 1;
             const bool tail_split = split + 1 == ext.splits;
             uint32_t own = split * per, own_end = own + per;
-            uint32_t claimed = lane == 0 && pool < pool_end ? atomicAdd(&x.counters[0], kClaim) : 0u;
+            // With an own share the first claim goes out after the first copy
+            // (its round trip is hidden behind the share); without one, now.
+            uint32_t claimed = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], kClaim) : 0u;
+            bool first_claim = per != 0 && pool < pool_end;
+            // The tiles after the ones warmed before the wait: HBM starts on
+            // them while the first copies come from L2.
+            {
+                const uint32_t tj = own + kPrefetchTiles + (static_cast<uint32_t>(lane) >> 1);
+                if (lane < 2 * kPostPrefetchTiles && tj < own_end)
+                    bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((lane & 1) ? a.v : a.k) +
+                                         static_cast<uint64_t>(tj) * tile_bytes,
+                                     tile_bytes);
+            }
             bool tail_pending = tail_split;
             const uint32_t tail_at = min(2u, per);
             uint32_t cur = 0, cur_left = 0;
@@ -684,6 +707,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                                          &full[s], policy);
                     tc::tma_load_3d_hint(stg_of(ring, s, tile_bytes) + tile_bytes, &map_v, 0,
                                          static_cast<int32_t>(t0), 0, &full[s], policy);
+                }
+                if (first_claim) {
+                    first_claim = false;
+                    if (lane == 0) claimed = atomicAdd(&x.counters[0], kClaim);
                 }
                 __syncwarp();
             }

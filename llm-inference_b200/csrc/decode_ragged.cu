@@ -10,7 +10,10 @@
 //   * Work unit = (sequence, a range of unit_tokens cached tokens). Units are
 //     claimed from a global counter by persistent CTAs (one per SM), so the
 //     batch's ~Σ len / unit_tokens units spread evenly however the lengths
-//     are distributed.
+//     are distributed. unit_tokens is chosen per launch from the batch's
+//     device lengths: about 4.5 units per CTA, between 256 and 768 tokens
+//     (a multiple of the consumer parities' tiles) -- short batches get small
+//     units for balance, long ones large units for fewer partials.
 //   * A producer warp streams each unit's 16-token K/V tiles (4-D tensor
 //     map: {64 fp16, row, column block, sequence}, 128-byte swizzle) into the
 //     stage ring, plus the sequence's Q row into one of two Q slots; the unit
@@ -45,12 +48,22 @@ constexpr uint32_t kRgSmemLimit = 214 * 1024;
 constexpr uint32_t kNoUnit = 0xffffffffu;
 
 // Unit geometry per KV-head count: npar consumer warps per KV head; a unit is
-// a multiple of npar tiles, at least 16 tiles (256 tokens, the KV_CHUNK).
+// a multiple of npar tiles, from at least 16 tiles (256 tokens, the KV_CHUNK)
+// up to at least 48 tiles: the largest that still gives every CTA about 4.5
+// units (balance), since each unit costs npar partials per head (traffic).
+constexpr uint32_t kRgHalfUnitsPerCta = 9;
 __host__ __device__ constexpr uint32_t rg_npar(uint32_t kvh) { return kRgConsumers / kvh; }
-__host__ __device__ constexpr uint32_t rg_unit_tiles(uint32_t kvh) {
-    return rg_npar(kvh) * ((16 + rg_npar(kvh) - 1) / rg_npar(kvh));
+__host__ __device__ constexpr uint32_t rg_round_tiles(uint32_t kvh, uint32_t tiles) {
+    return rg_npar(kvh) * ((tiles + rg_npar(kvh) - 1) / rg_npar(kvh));
 }
-__host__ __device__ constexpr uint32_t rg_unit_tokens(uint32_t kvh) { return rg_unit_tiles(kvh) * kTile; }
+__host__ __device__ constexpr uint32_t rg_min_unit_tokens(uint32_t kvh) { return rg_round_tiles(kvh, 16) * kTile; }
+__host__ __device__ constexpr uint32_t rg_max_unit_tokens(uint32_t kvh) { return rg_round_tiles(kvh, 48) * kTile; }
+// The unit size for a batch of `total_tiles` 16-token tiles over `ctas` CTAs.
+__host__ __device__ inline uint32_t rg_unit_tokens(uint32_t kvh, uint32_t total_tiles, uint32_t ctas) {
+    const uint32_t want = static_cast<uint32_t>(2ull * total_tiles / (static_cast<uint64_t>(ctas) * kRgHalfUnitsPerCta));
+    const uint32_t t = rg_round_tiles(kvh, want) * kTile;
+    return t < rg_min_unit_tokens(kvh) ? rg_min_unit_tokens(kvh) : (t > rg_max_unit_tokens(kvh) ? rg_max_unit_tokens(kvh) : t);
+}
 
 struct RaggedArgs {
     const __half* q;        // sequence b's query row at q + b * q_seq_stride, [H][128]
@@ -64,6 +77,7 @@ struct RaggedArgs {
     float* pm;              // [P][H] natural-log max
     float* pl;              // [P][H] weight sum
     uint32_t* counter;      // next unclaimed unit; 0 at launch, reset by the merge
+    uint32_t* unit_word;    // this launch's unit size in tokens, for the merge
     uint32_t num_seqs;
     uint32_t num_heads;
     uint32_t group;
@@ -82,28 +96,39 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     decode_ragged_kernel(const RaggedArgs a, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v) {
     constexpr uint32_t npar = rg_npar(KVH);
-    constexpr uint32_t unit_tokens = rg_unit_tokens(KVH);
     constexpr uint32_t row_bytes = KVH * 256;
     constexpr uint32_t tile_bytes = kTile * row_bytes;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t prefix[kRgMaxSeqs + 1];  // units before sequence b
     __shared__ uint32_t lens[kRgMaxSeqs];
     __shared__ uint32_t st_valid[32], st_unit[32], st_local[32];
+    __shared__ uint32_t unit_s;
 
     pdl_wait_primary();  // lengths, Q and the caches may come from the previous kernel
     pdl_launch_dependents();
     const uint32_t B = a.num_seqs;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp == 0) {
+        // the batch's tiles give the unit size, then the units' prefix sums
+        uint32_t tiles = 0;
+        for (uint32_t b = lane; b < B; b += 32) {
+            const uint32_t len = rg_len(a, b);
+            lens[b] = len;
+            tiles += (len + kTile - 1) / kTile;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) tiles += __shfl_xor_sync(0xffffffffu, tiles, off);
+        const uint32_t unit_tokens = rg_unit_tokens(KVH, tiles, gridDim.x);
+        if (lane == 0) {
+            unit_s = unit_tokens;
+            if (blockIdx.x == 0) *a.unit_word = unit_tokens;
+        }
+        __syncwarp();
         uint32_t carry = 0;
         for (uint32_t base = 0; base < B; base += 32) {
             const uint32_t b = base + lane;
             uint32_t u = 0;
-            if (b < B) {
-                const uint32_t len = rg_len(a, b);
-                lens[b] = len;
-                u = (len + unit_tokens - 1) / unit_tokens;
-            }
+            if (b < B) u = (lens[b] + unit_tokens - 1) / unit_tokens;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
                 const uint32_t n = __shfl_up_sync(0xffffffffu, u, off);
@@ -136,6 +161,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     }
     __syncthreads();
     const uint32_t U = prefix[B];
+    const uint32_t unit_tokens = unit_s;
 
     bool ok = true;
     if (warp == kRgConsumers) {
@@ -306,10 +332,11 @@ __global__ void __launch_bounds__(kRgThreads, 1)
 // fp16 out. Block (0, 0) resets the claim counter for the next launch.
 constexpr int kRgMergeBatch = 8;
 
-__global__ void __launch_bounds__(128) merge_ragged_kernel(const RaggedArgs a, uint32_t npar, uint32_t unit_tokens) {
+__global__ void __launch_bounds__(128) merge_ragged_kernel(const RaggedArgs a, uint32_t npar) {
     __shared__ uint32_t part_s[4];
     pdl_wait_primary();
     pdl_launch_dependents();
+    const uint32_t unit_tokens = __ldcg(a.unit_word);  // written by the decode kernel
     const uint32_t b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     if (b == 0 && h == 0 && d == 0) *a.counter = 0u;
     // units of the sequences before b
@@ -360,19 +387,19 @@ int device_sms_rg() {
 }
 
 struct RgWorkspace {
-    size_t po, pm, pl, counter, total_bytes;
+    size_t po, pm, pl, counter, total_bytes;  // counter: the claim counter, then the unit-size word
 };
 
 RgWorkspace rg_layout(size_t num_seqs, size_t num_heads, size_t num_kv_heads, size_t max_kv_len) {
     RgWorkspace w{};
     const uint32_t kvh = static_cast<uint32_t>(num_kv_heads);
-    const size_t units = num_seqs * ((max_kv_len + rg_unit_tokens(kvh) - 1) / rg_unit_tokens(kvh));
+    const size_t units = num_seqs * ((max_kv_len + rg_min_unit_tokens(kvh) - 1) / rg_min_unit_tokens(kvh));
     const size_t P = units * rg_npar(kvh);
     w.po = 0;
     w.pm = w.po + P * num_heads * 128;
     w.pl = w.pm + P * num_heads;
     w.counter = w.pl + P * num_heads;
-    w.total_bytes = (w.counter * sizeof(float) + sizeof(uint32_t) + 255) / 256 * 256;
+    w.total_bytes = (w.counter * sizeof(float) + 2 * sizeof(uint32_t) + 255) / 256 * 256;
     return w;
 }
 
@@ -465,6 +492,7 @@ extern "C" int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t 
     a.pm = ws + w.pm;
     a.pl = ws + w.pl;
     a.counter = reinterpret_cast<uint32_t*>(ws + w.counter);
+    a.unit_word = a.counter + 1;
     a.num_seqs = static_cast<uint32_t>(num_seqs);
     a.num_heads = static_cast<uint32_t>(num_heads);
     a.group = static_cast<uint32_t>(group);
@@ -488,6 +516,5 @@ extern "C" int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t 
         default: st = launch_ragged_kvh<8>(a, mk, mv, grid, smem, stream); break;
     }
     if (st != B2_OK) return st;
-    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(128), 0, stream, a, npar,
-                      rg_unit_tokens(kvh));
+    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(128), 0, stream, a, npar);
 }

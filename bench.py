@@ -397,13 +397,20 @@ def run_ragged(args, rank, world, dev):
     peak, peak_kind = load_peaks()
     launch_ms = ms / steps / LAYERS
     achieved = mine_layer / (launch_ms / 1e3) / 1e9
+    # ncu DRAM bytes of one config-5-shape launch, scaled by this layer's algorithmic bytes
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "ragged_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            t = json.load(f)
+        traffic = int(round(mine_layer * t["bytes_per_launch"] / t["algorithmic_bytes"]))
     return {"metric": "ragged decode KV-read GB/s", "value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "workload": RG_WORKLOAD, "steps": steps, "ms_per_step": round(ms / steps, 4),
             "gpu_launches": per_step * steps, "sequences_per_rank": B,
             "parallelism": f"sequences over {world} GPU(s), greedy longest-first",
             "roofline": {"bound": "hbm", "kernel": "decode_ragged_kernel + merge_ragged_kernel (+ ragged RoPE/append)",
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                          "avg_layer_us": round(launch_ms * 1e3, 3), "algorithmic_bytes_per_layer": mine_layer,
                          "timing": "timed region (graph replays) / 36 layers per step"}}
 

@@ -23,8 +23,9 @@
 //     the single-sequence kernel and, at each unit boundary, write their own
 //     (o, m, l) state as a partial: no CTA-wide barrier per unit, so the
 //     producer keeps streaming across unit boundaries.
-//   * A merge kernel (one CTA per (sequence, head)) folds the npar partials
-//     of each of the sequence's units and writes the fp16 output.
+//   * A merge kernel (one CTA per (sequence, head), four groups of 128
+//     threads) folds the npar partials of each of the sequence's units and
+//     writes the fp16 output.
 #include <math.h>
 
 #include <atomic>
@@ -327,35 +328,44 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
 }
 
-// One CTA per (sequence, head), thread = output dim: fold the sequence's
-// units x npar partials (online rescale, batches of 8 in flight) and write
-// fp16 out. Block (0, 0) resets the claim counter for the next launch.
+// One CTA per (sequence, head), 4 groups of 128 threads (thread = output dim):
+// group g folds the sequence's partials g, g + 4, ... (online rescale, batches
+// of 8 in flight), the four group states meet in shared memory and threads
+// 0..127 write the fp16 output. Block (0, 0) resets the claim counter for the
+// next launch.
 constexpr int kRgMergeBatch = 8;
+constexpr int kRgMergeGroups = 4;
+constexpr int kRgMergeThreads = 128 * kRgMergeGroups;
 
-__global__ void __launch_bounds__(128) merge_ragged_kernel(const RaggedArgs a, uint32_t npar) {
-    __shared__ uint32_t part_s[4];
+__global__ void __launch_bounds__(kRgMergeThreads) merge_ragged_kernel(const RaggedArgs a, uint32_t npar) {
+    __shared__ uint32_t part_s[kRgMergeThreads / 32];
+    __shared__ float grp_m[kRgMergeGroups], grp_l[kRgMergeGroups];
+    __shared__ float grp_o[kRgMergeGroups][128];
     pdl_wait_primary();
     pdl_launch_dependents();
     const uint32_t unit_tokens = __ldcg(a.unit_word);  // written by the decode kernel
-    const uint32_t b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-    if (b == 0 && h == 0 && d == 0) *a.counter = 0u;
+    const uint32_t b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const uint32_t d = tid & 127, grp = tid >> 7;
+    if (b == 0 && h == 0 && tid == 0) *a.counter = 0u;
     // units of the sequences before b
     uint32_t before = 0;
-    for (uint32_t j = d; j < b; j += 128) before += (rg_len(a, j) + unit_tokens - 1) / unit_tokens;
+    for (uint32_t j = tid; j < b; j += kRgMergeThreads) before += (rg_len(a, j) + unit_tokens - 1) / unit_tokens;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) before += __shfl_xor_sync(0xffffffffu, before, off);
-    if ((d & 31) == 0) part_s[d >> 5] = before;
+    if ((tid & 31) == 0) part_s[tid >> 5] = before;
     __syncthreads();
-    before = part_s[0] + part_s[1] + part_s[2] + part_s[3];
+    before = 0;
+#pragma unroll
+    for (int w = 0; w < kRgMergeThreads / 32; ++w) before += part_s[w];
     const uint32_t units = (rg_len(a, b) + unit_tokens - 1) / unit_tokens;
     const uint32_t p0 = before * npar, n = units * npar;
     const uint32_t H = a.num_heads;
     float M = -INFINITY, L = 0.f, O = 0.f;
-    for (uint32_t base = 0; base < n; base += kRgMergeBatch) {
+    for (uint32_t base = grp; base < n; base += kRgMergeBatch * kRgMergeGroups) {
         float mv[kRgMergeBatch], lv[kRgMergeBatch], ov[kRgMergeBatch];
 #pragma unroll
         for (int u = 0; u < kRgMergeBatch; ++u) {
-            const uint32_t c = base + u;
+            const uint32_t c = base + u * kRgMergeGroups;
             const uint64_t p = static_cast<uint64_t>(p0 + c) * H + h;
             mv[u] = c < n ? __ldg(a.pm + p) : -INFINITY;
             lv[u] = c < n ? __ldg(a.pl + p) : 0.f;
@@ -376,7 +386,24 @@ __global__ void __launch_bounds__(128) merge_ragged_kernel(const RaggedArgs a, u
             L = fmaf(w, lv[u], L);
         }
     }
-    a.out[static_cast<uint64_t>(b) * a.out_seq_stride + h * 128 + d] = __float2half_rn(L > 0.f ? O / L : 0.f);
+    grp_o[grp][d] = O;
+    if (d == 0) {
+        grp_m[grp] = M;
+        grp_l[grp] = L;
+    }
+    __syncthreads();
+    if (grp != 0) return;
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < kRgMergeGroups; ++g) Mx = fmaxf(Mx, grp_m[g]);
+    float Ox = 0.f, Lx = 0.f;
+#pragma unroll
+    for (int g = 0; g < kRgMergeGroups; ++g) {
+        const float sc = grp_m[g] == -INFINITY ? 0.f : expf(grp_m[g] - Mx);
+        Ox = fmaf(sc, grp_o[g][d], Ox);
+        Lx = fmaf(sc, grp_l[g], Lx);
+    }
+    a.out[static_cast<uint64_t>(b) * a.out_seq_stride + h * 128 + d] = __float2half_rn(Lx > 0.f ? Ox / Lx : 0.f);
 }
 
 int device_sms_rg() {
@@ -516,5 +543,5 @@ extern "C" int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t 
         default: st = launch_ragged_kvh<8>(a, mk, mv, grid, smem, stream); break;
     }
     if (st != B2_OK) return st;
-    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(128), 0, stream, a, npar);
+    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(kRgMergeThreads), 0, stream, a, npar);
 }

@@ -355,11 +355,20 @@ def run_ragged(args, rank, world, dev):
     def step(st):
         for l in range(LAYERS):
             row = qkv[l]
-            b200attn.launch_rope_and_store_kv_ragged(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[l, 0],
-                                                     cache[l, 1], RG_MAX * KV_DIM, d_cos, d_sin, B, H, KVH, D, QKV,
-                                                     QKV, pos, RG_MAX, (l + 1) % 4 != 0, stream=st)
-            b200attn.launch_causal_attention_decode_ragged(row, QKV, cache[l, 0], cache[l, 1], RG_MAX * KV_DIM, pos, 1,
-                                                           RG_MAX, out[l], 0, B, H, KVH, D, ws, ws_bytes, stream=st)
+            rotate = (l + 1) % 4 != 0
+            if args.unfused:
+                # the two-launch form: ragged RoPE/append, then the ragged decode
+                b200attn.launch_rope_and_store_kv_ragged(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[l, 0],
+                                                         cache[l, 1], RG_MAX * KV_DIM, d_cos, d_sin, B, H, KVH, D,
+                                                         QKV, QKV, pos, RG_MAX, rotate, stream=st)
+                b200attn.launch_causal_attention_decode_ragged(row, QKV, cache[l, 0], cache[l, 1], RG_MAX * KV_DIM,
+                                                               pos, 1, RG_MAX, out[l], 0, B, H, KVH, D, ws, ws_bytes,
+                                                               stream=st)
+            else:
+                b200attn.launch_decode_step_ragged_fused(row, QKV, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], QKV,
+                                                         cache[l, 0], cache[l, 1], RG_MAX * KV_DIM, d_cos, d_sin,
+                                                         RG_MAX, rotate, pos, RG_MAX, out[l], 0, B, H, KVH, D, ws,
+                                                         ws_bytes, stream=st)
 
     with torch.cuda.stream(stream):
         step(stream)
@@ -408,7 +417,11 @@ def run_ragged(args, rank, world, dev):
             "workload": RG_WORKLOAD, "steps": steps, "ms_per_step": round(ms / steps, 4),
             "gpu_launches": per_step * steps, "sequences_per_rank": B,
             "parallelism": f"sequences over {world} GPU(s), greedy longest-first",
-            "roofline": {"bound": "hbm", "kernel": "decode_ragged_kernel + merge_ragged_kernel (+ ragged RoPE/append)",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("decode_ragged_kernel + merge_ragged_kernel (+ ragged RoPE/append kernel)"
+                                    if args.unfused else
+                                    "decode_ragged_kernel<fused step> (RoPE + append + split attention) + "
+                                    "merge_ragged_kernel"),
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                          "avg_layer_us": round(launch_ms * 1e3, 3), "algorithmic_bytes_per_layer": mine_layer,

@@ -390,6 +390,30 @@ int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t q_seq_strid
                                              size_t num_kv_heads, size_t head_dim, void* d_workspace,
                                              size_t workspace_bytes, b2_stream_t stream);
 
+/* The ragged decode step in one call (the two launches above, fused): for
+ * each sequence b, with p = d_pos[b] (its new token's position and cache row):
+ *  - the new K row (d_k_new + b * kv_new_stride, [num_kv_heads][128]) rotated
+ *    at p when apply_rotation, and the V row, are written to row p of
+ *    sequence b's cache before that row is attended (d_k_new == NULL appends
+ *    nothing);
+ *  - Q row b (d_q + b * q_seq_stride, read, never written) is rotated at p
+ *    when apply_rotation;
+ *  - out[b] = attention of the rotated Q over rows [0, min(p + 1, max_kv_len)).
+ * A position outside [0, rope_rows) with apply_rotation appends nothing,
+ * leaves Q unrotated and sets bit 1 of b2_device_error_word; p < 0 gives a
+ * zero output. kv_new_stride 0 = packed (num_kv_heads * 128). Results equal
+ * b2_launch_rope_and_store_kv_ragged followed by
+ * b2_launch_causal_attention_decode_ragged (kv_len d_pos, bias 1); same
+ * shapes, alignment and workspace as the decode. */
+int b2_launch_decode_step_ragged_fused(const void* d_q, size_t q_seq_stride, const void* d_k_new,
+                                       const void* d_v_new, size_t kv_new_stride, void* d_k_cache,
+                                       void* d_v_cache, size_t cache_seq_stride, const void* d_cos,
+                                       const void* d_sin, size_t rope_rows, bool apply_rotation,
+                                       const int32_t* d_pos, size_t max_kv_len, void* d_out,
+                                       size_t out_seq_stride, size_t num_seqs, size_t num_heads,
+                                       size_t num_kv_heads, size_t head_dim, void* d_workspace,
+                                       size_t workspace_bytes, b2_stream_t stream);
+
 /* ---- Decode without a caller workspace ------------------------------------
  * No counterpart in the reference (whose decode launchers always take the
  * three partial arrays). For callers that cannot provide scratch memory: a

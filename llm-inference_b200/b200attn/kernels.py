@@ -28,6 +28,7 @@ __all__ = [
     "decode_step_workspace_bytes", "launch_decode_step_fused", "launch_decode_step_fused_rank_partial",
     "launch_rope_and_store_kv_ragged", "decode_ragged_workspace_bytes", "launch_causal_attention_decode_ragged",
     "decode_exchange_bytes", "launch_decode_step_fused_exchange", "ExchangeBuffers",
+    "launch_decode_step_ragged_fused",
 ]
 
 
@@ -302,6 +303,20 @@ def launch_causal_attention_decode_ragged(d_q, q_seq_stride, d_k_cache, d_v_cach
         _ptr(d_q), q_seq_stride, _ptr(d_k_cache), _ptr(d_v_cache), cache_seq_stride, _ptr(d_kv_len),
         int(kv_len_bias), max_kv_len, _ptr(d_out), out_seq_stride, num_seqs, num_heads, num_kv_heads, head_dim,
         _ptr(d_workspace), workspace_bytes, _stream(stream)), "launch_causal_attention_decode_ragged")
+
+
+def launch_decode_step_ragged_fused(d_q, q_seq_stride, d_k_new, d_v_new, kv_new_stride, d_k_cache, d_v_cache,
+                                    cache_seq_stride, d_cos, d_sin, rope_rows, apply_rotation, d_pos, max_kv_len,
+                                    d_out, out_seq_stride, num_seqs, num_heads, num_kv_heads, head_dim, d_workspace,
+                                    workspace_bytes, stream=None):
+    """The ragged decode step in one call: each sequence's new K/V row appended
+    at row d_pos[b] (K rotated), Q rotated in the kernel, attention over rows
+    [0, d_pos[b]] -- launch_rope_and_store_kv_ragged + the ragged decode."""
+    check(lib().b2_launch_decode_step_ragged_fused(
+        _ptr(d_q), q_seq_stride, _ptr(d_k_new), _ptr(d_v_new), kv_new_stride, _ptr(d_k_cache), _ptr(d_v_cache),
+        cache_seq_stride, _ptr(d_cos), _ptr(d_sin), rope_rows, bool(apply_rotation), _ptr(d_pos), max_kv_len,
+        _ptr(d_out), out_seq_stride, num_seqs, num_heads, num_kv_heads, head_dim, _ptr(d_workspace),
+        workspace_bytes, _stream(stream)), "launch_decode_step_ragged_fused")
 
 
 # ---- KV-split decode across ranks --------------------------------------------

@@ -84,6 +84,19 @@ struct RaggedArgs {
     uint32_t group;
     uint32_t stages;
     float scale_log2;
+    // fused step only: kv_len holds each sequence's new-token position (bias
+    // 1); the new K/V rows (b at k_new / v_new + b * kv_new_stride) are
+    // appended at that row of the sequence's cache, Q is rotated in registers
+    const __half* k_new;    // nullptr: no append
+    const __half* v_new;
+    uint64_t kv_new_stride;
+    __half* k_cache;        // writable views of the cached rows
+    __half* v_cache;
+    uint64_t cache_seq_stride;
+    const __half* cos;      // RoPE tables [table_rows][64]
+    const __half* sin;
+    uint32_t rotate;
+    uint32_t table_rows;
 };
 
 __device__ __forceinline__ uint32_t rg_len(const RaggedArgs& a, uint32_t b) {
@@ -92,7 +105,13 @@ __device__ __forceinline__ uint32_t rg_len(const RaggedArgs& a, uint32_t b) {
     return static_cast<uint32_t>(n);
 }
 
-template <uint32_t KVH>
+// Bytes of one Q slot: the H query rows.
+__host__ __device__ constexpr uint32_t rg_qslot_bytes(uint32_t heads, bool) { return heads * 256; }
+
+// kStep: the fused step -- RoPE of each sequence's new token (the producer
+// rotates Q into the Q slot, and rotates K and appends it with V before it
+// copies the tile holding that row), then the same split attention.
+template <uint32_t KVH, bool kStep>
 __global__ void __launch_bounds__(kRgThreads, 1)
     decode_ragged_kernel(const RaggedArgs a, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v) {
@@ -104,6 +123,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     __shared__ uint32_t lens[kRgMaxSeqs];
     __shared__ uint32_t st_valid[32], st_unit[32], st_local[32];
     __shared__ uint32_t unit_s;
+    __shared__ int32_t rawpos[kStep ? kRgMaxSeqs : 1];  // fused step: the new token's position
 
     pdl_wait_primary();  // lengths, Q and the caches may come from the previous kernel
     pdl_launch_dependents();
@@ -116,6 +136,12 @@ __global__ void __launch_bounds__(kRgThreads, 1)
             const uint32_t len = rg_len(a, b);
             lens[b] = len;
             tiles += (len + kTile - 1) / kTile;
+            if constexpr (kStep) {
+                const int32_t p = __ldg(a.kv_len + b);
+                rawpos[b] = p;
+                if (a.rotate && !(p >= 0 && static_cast<uint32_t>(p) < a.table_rows) && blockIdx.x == 0)
+                    atomicOr(&g_device_error, kErrBadPosition);
+            }
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) tiles += __shfl_xor_sync(0xffffffffu, tiles, off);
@@ -143,9 +169,10 @@ __global__ void __launch_bounds__(kRgThreads, 1)
 
     const uint32_t stages = a.stages;
     const uint32_t q_bytes = a.num_heads * 256;
+    const uint32_t qslot_bytes = rg_qslot_bytes(a.num_heads, kStep);
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* qslots = ring + stages * 2 * tile_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(qslots + kRgQSlots * q_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(qslots + kRgQSlots * qslot_bytes);
     uint64_t* empty = full + stages;
     uint64_t* qfull = empty + stages;
     uint64_t* qempty = qfull + kRgQSlots;
@@ -189,20 +216,47 @@ __global__ void __launch_bounds__(kRgThreads, 1)
             const uint32_t t_end = min(len, t_begin + unit_tokens);
             const uint32_t ntiles = (t_end - t_begin + kTile - 1) / kTile;
             const uint32_t nstages = (ntiles + npar - 1) / npar * npar;
-            // the sequence's Q row into Q slot k % 2
-            const uint32_t qs = k % kRgQSlots;
-            bool w_ok = true;
-            if (lane == 0) {
-                if (k >= kRgQSlots) w_ok = mbar_wait(&qempty[qs], ((k / kRgQSlots) - 1) & 1);
-                if (w_ok) {
-                    mbar_arrive_expect_tx(&qfull[qs], q_bytes);
-                    bulk_g2s_plain(qslots + qs * q_bytes, a.q + static_cast<uint64_t>(b) * a.q_seq_stride, q_bytes,
-                                   &qfull[qs]);
-                }
+            // fused step: rotate Q (position in the tables), append the new row
+            // (its unit is the sequence's last; the position is in the cache)
+            int32_t p = 0;
+            bool rot = false, app = false;
+            if constexpr (kStep) {
+                p = rawpos[b];
+                const bool in_table = p >= 0 && static_cast<uint32_t>(p) < a.table_rows;
+                rot = a.rotate && in_table;
+                app = a.k_new != nullptr && (!a.rotate || in_table) && p >= 0 &&
+                      static_cast<uint32_t>(p) < a.max_kv_len && t_end == len;
             }
+            // the sequence's Q row into Q slot k % 2: one bulk copy, or (fused
+            // step with RoPE) rotated by the warp's lanes and stored, 16 bytes
+            // of a head's first and second half per piece
+            const uint32_t qs = k % kRgQSlots;
+            uint8_t* slot = qslots + qs * qslot_bytes;
+            bool w_ok = true;
+            if (lane == 0 && k >= kRgQSlots) w_ok = mbar_wait(&qempty[qs], ((k / kRgQSlots) - 1) & 1);
             if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
                 ok = false;
                 break;
+            }
+            const __half* qsrc = a.q + static_cast<uint64_t>(b) * a.q_seq_stride;
+            if (rot) {
+                for (uint32_t gi = lane; gi < a.num_heads * 8; gi += 32) {
+                    const uint32_t hh = gi >> 3, e = (gi & 7) * 8;
+                    uint4 lo4 = *reinterpret_cast<const uint4*>(qsrc + hh * 128 + e);
+                    uint4 hi4 = *reinterpret_cast<const uint4*>(qsrc + hh * 128 + 64 + e);
+                    const uint64_t ti = static_cast<uint64_t>(p) * 64 + e;
+                    rot8_pairs(lo4, hi4, *reinterpret_cast<const uint4*>(a.cos + ti),
+                               *reinterpret_cast<const uint4*>(a.sin + ti));
+                    *reinterpret_cast<uint4*>(slot + (hh * 128 + e) * 2) = lo4;
+                    *reinterpret_cast<uint4*>(slot + (hh * 128 + 64 + e) * 2) = hi4;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&qfull[qs]);
+            } else if (lane == 0) {
+                // the slot may hold rotated rows stored through the generic proxy
+                if constexpr (kStep) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&qfull[qs], q_bytes);
+                bulk_g2s_plain(slot, qsrc, q_bytes, &qfull[qs]);
             }
             for (uint32_t j = 0; j < nstages; ++j, ++i) {
                 const uint32_t s = i % stages, round = i / stages;
@@ -210,6 +264,32 @@ __global__ void __launch_bounds__(kRgThreads, 1)
                 if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
                     ok = false;
                     break;
+                }
+                if (kStep && app && j + 1 == ntiles) {
+                    // the new token's K (rotated) and V into row p before the tile
+                    // that holds it is copied; the warp's stores reach the tensor
+                    // copy through the proxy fence of every lane and the warp sync
+                    const uint64_t row = static_cast<uint64_t>(b) * a.cache_seq_stride + static_cast<uint64_t>(p) * (KVH * 128);
+                    const __half* kn = a.k_new + static_cast<uint64_t>(b) * a.kv_new_stride;
+                    const __half* vn = a.v_new + static_cast<uint64_t>(b) * a.kv_new_stride;
+                    for (uint32_t gi = lane; gi < KVH * 8; gi += 32) {
+                        const uint32_t hh = gi >> 3, e = (gi & 7) * 8;
+                        uint4 lo4 = *reinterpret_cast<const uint4*>(kn + hh * 128 + e);
+                        uint4 hi4 = *reinterpret_cast<const uint4*>(kn + hh * 128 + 64 + e);
+                        if (a.rotate) {
+                            const uint64_t ti = static_cast<uint64_t>(p) * 64 + e;
+                            rot8_pairs(lo4, hi4, *reinterpret_cast<const uint4*>(a.cos + ti),
+                                       *reinterpret_cast<const uint4*>(a.sin + ti));
+                        }
+                        *reinterpret_cast<uint4*>(a.k_cache + row + hh * 128 + e) = lo4;
+                        *reinterpret_cast<uint4*>(a.k_cache + row + hh * 128 + 64 + e) = hi4;
+                        *reinterpret_cast<uint4*>(a.v_cache + row + hh * 128 + e) =
+                            *reinterpret_cast<const uint4*>(vn + hh * 128 + e);
+                        *reinterpret_cast<uint4*>(a.v_cache + row + hh * 128 + 64 + e) =
+                            *reinterpret_cast<const uint4*>(vn + hh * 128 + 64 + e);
+                    }
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    __syncwarp();
                 }
                 if (lane == 0) {
                     const uint32_t t0 = t_begin + j * kTile;
@@ -282,7 +362,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
                     break;
                 }
                 if (static_cast<uint32_t>(g) < a.group) {
-                    const uint8_t* qrow = qslots + qs * q_bytes + (kvh * a.group + g) * 256;
+                    const uint8_t* qrow = qslots + qs * qslot_bytes + (kvh * a.group + g) * 256;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const uint4 w = lds128(qrow + (32 * j + 8 * t) * 2);
@@ -406,6 +486,8 @@ __global__ void __launch_bounds__(kRgMergeThreads) merge_ragged_kernel(const Rag
     a.out[static_cast<uint64_t>(b) * a.out_seq_stride + h * 128 + d] = __float2half_rn(Lx > 0.f ? Ox / Lx : 0.f);
 }
 
+bool rg_kvh_ok(size_t kvh) { return kvh == 1 || kvh == 2 || kvh == 4 || kvh == 8; }
+
 int device_sms_rg() {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -430,7 +512,7 @@ RgWorkspace rg_layout(size_t num_seqs, size_t num_heads, size_t num_kv_heads, si
     return w;
 }
 
-template <uint32_t KVH>
+template <uint32_t KVH, bool kStep>
 int launch_ragged_kvh(const RaggedArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, uint32_t grid, size_t smem,
                       cudaStream_t stream) {
     static std::atomic<uint64_t> attr_done{0};
@@ -438,13 +520,137 @@ int launch_ragged_kvh(const RaggedArgs& a, const CUtensorMap& mk, const CUtensor
     if (cudaGetDevice(&dev) != cudaSuccess) return B2_ERR_CUDA;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_done.load() & bit)) {
-        const int st = cuda_status(cudaFuncSetAttribute(decode_ragged_kernel<KVH>,
+        const int st = cuda_status(cudaFuncSetAttribute(decode_ragged_kernel<KVH, kStep>,
                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                         static_cast<int>(kRgSmemLimit)));
         if (st != B2_OK) return st;
         attr_done.fetch_or(bit);
     }
-    return launch_pdl(decode_ragged_kernel<KVH>, dim3(grid), dim3(kRgThreads), smem, stream, a, mk, mv);
+    return launch_pdl(decode_ragged_kernel<KVH, kStep>, dim3(grid), dim3(kRgThreads), smem, stream, a, mk, mv);
+}
+
+// Inputs of one ragged launch (the plain decode, or the fused step).
+struct RaggedCall {
+    const void* q;
+    size_t q_seq_stride;
+    const void* k_cache;
+    const void* v_cache;
+    size_t cache_seq_stride;
+    const int32_t* kv_len;
+    int32_t kv_len_bias;
+    size_t max_kv_len;
+    void* out;
+    size_t out_seq_stride;
+    size_t num_seqs, num_heads, num_kv_heads, head_dim;
+    void* workspace;
+    size_t workspace_bytes;
+    // fused step
+    bool step;
+    const void* k_new;
+    const void* v_new;
+    size_t kv_new_stride;
+    const void* cos;
+    const void* sin;
+    size_t rope_rows;
+    bool rotate;
+};
+
+int launch_ragged(RaggedCall c, cudaStream_t stream) {
+    if (c.num_seqs == 0 || c.max_kv_len == 0 || c.num_kv_heads == 0 || c.head_dim == 0) return B2_NOTHING_TO_DO;
+    if (c.num_heads % c.num_kv_heads != 0) return B2_NOTHING_TO_DO;
+    if (!c.q || !c.k_cache || !c.v_cache || !c.kv_len || !c.out || !c.workspace) return B2_ERR_INVALID_ARG;
+    const size_t group = c.num_heads / c.num_kv_heads;
+    if (c.head_dim != 128 || !rg_kvh_ok(c.num_kv_heads) || group > 8 || c.num_seqs > kRgMaxSeqs ||
+        c.max_kv_len > 0x7fffffffull)
+        return B2_ERR_UNSUPPORTED;
+    const size_t kv_dim = c.num_kv_heads * c.head_dim;
+    if (c.q_seq_stride == 0) c.q_seq_stride = c.num_heads * c.head_dim;
+    if (c.out_seq_stride == 0) c.out_seq_stride = c.num_heads * c.head_dim;
+    if (c.cache_seq_stride == 0) c.cache_seq_stride = c.max_kv_len * kv_dim;
+    if (c.q_seq_stride < c.num_heads * c.head_dim || c.out_seq_stride < c.num_heads * c.head_dim)
+        return B2_ERR_INVALID_ARG;
+    if (c.num_seqs > 1 && c.cache_seq_stride < c.max_kv_len * kv_dim) return B2_ERR_INVALID_ARG;  // caches overlap
+    if (!aligned16(c.q) || !aligned16(c.k_cache) || !aligned16(c.v_cache) || !aligned16(c.workspace) ||
+        c.q_seq_stride % 8 != 0 || c.cache_seq_stride % 8 != 0)
+        return B2_ERR_ALIGNMENT;
+    if (c.step) {
+        if (c.k_new && !c.v_new) return B2_ERR_INVALID_ARG;
+        if (c.rotate && (!c.cos || !c.sin || c.rope_rows == 0)) return B2_ERR_INVALID_ARG;
+        if (c.rope_rows > 0x7fffffffull) return B2_ERR_UNSUPPORTED;
+        if (c.kv_new_stride == 0) c.kv_new_stride = kv_dim;
+        if (c.k_new && c.kv_new_stride < kv_dim) return B2_ERR_INVALID_ARG;
+        if ((c.k_new && (!aligned16(c.k_new) || !aligned16(c.v_new) || c.kv_new_stride % 8 != 0)) ||
+            (c.rotate && (!aligned16(c.cos) || !aligned16(c.sin))))
+            return B2_ERR_ALIGNMENT;
+    }
+    const RgWorkspace w = rg_layout(c.num_seqs, c.num_heads, c.num_kv_heads, c.max_kv_len);
+    if (c.workspace_bytes < w.total_bytes) return B2_ERR_WORKSPACE;
+    const uint32_t kvh = static_cast<uint32_t>(c.num_kv_heads);
+    const uint32_t npar = rg_npar(kvh);
+    const size_t stage_bytes = 2ull * kTile * kvh * 256;
+    const size_t fixed = 1024 + kRgQSlots * rg_qslot_bytes(static_cast<uint32_t>(c.num_heads), c.step) + 256;
+    uint32_t stages = static_cast<uint32_t>((kRgSmemLimit - fixed) / stage_bytes) / npar * npar;
+    if (stages > 32) stages = 32 / npar * npar;
+    if (stages == 0) return B2_ERR_UNSUPPORTED;
+
+    float* ws = static_cast<float*>(c.workspace);
+    RaggedArgs a{};
+    a.q = static_cast<const __half*>(c.q);
+    a.q_seq_stride = c.q_seq_stride;
+    a.kv_len = c.kv_len;
+    a.kv_len_bias = c.kv_len_bias;
+    a.max_kv_len = static_cast<uint32_t>(c.max_kv_len);
+    a.out = static_cast<__half*>(c.out);
+    a.out_seq_stride = c.out_seq_stride;
+    a.po = ws + w.po;
+    a.pm = ws + w.pm;
+    a.pl = ws + w.pl;
+    a.counter = reinterpret_cast<uint32_t*>(ws + w.counter);
+    a.unit_word = a.counter + 1;
+    a.num_seqs = static_cast<uint32_t>(c.num_seqs);
+    a.num_heads = static_cast<uint32_t>(c.num_heads);
+    a.group = static_cast<uint32_t>(group);
+    a.stages = stages;
+    a.scale_log2 = kLog2e / sqrtf(static_cast<float>(c.head_dim));
+    if (c.step) {
+        a.k_new = static_cast<const __half*>(c.k_new);
+        a.v_new = static_cast<const __half*>(c.v_new);
+        a.kv_new_stride = c.kv_new_stride;
+        a.k_cache = static_cast<__half*>(const_cast<void*>(c.k_cache));
+        a.v_cache = static_cast<__half*>(const_cast<void*>(c.v_cache));
+        a.cache_seq_stride = c.cache_seq_stride;
+        a.cos = static_cast<const __half*>(c.cos);
+        a.sin = static_cast<const __half*>(c.sin);
+        a.rotate = c.rotate ? 1u : 0u;
+        a.table_rows = static_cast<uint32_t>(c.rope_rows);
+    }
+
+    CUtensorMap mk, mv;
+    if (encode_token_rows_by_column_block_seqs(&mk, c.k_cache, c.max_kv_len, kvh * 256, c.num_seqs,
+                                               c.cache_seq_stride * 2, kTile) != 0 ||
+        encode_token_rows_by_column_block_seqs(&mv, c.v_cache, c.max_kv_len, kvh * 256, c.num_seqs,
+                                               c.cache_seq_stride * 2, kTile) != 0)
+        return B2_ERR_CUDA;
+    const size_t smem = fixed + stages * stage_bytes + 2 * (stages + kRgQSlots) * sizeof(uint64_t);
+    const uint32_t grid = static_cast<uint32_t>(device_sms_rg());
+    int st;
+    if (c.step) {
+        switch (kvh) {
+            case 1: st = launch_ragged_kvh<1, true>(a, mk, mv, grid, smem, stream); break;
+            case 2: st = launch_ragged_kvh<2, true>(a, mk, mv, grid, smem, stream); break;
+            case 4: st = launch_ragged_kvh<4, true>(a, mk, mv, grid, smem, stream); break;
+            default: st = launch_ragged_kvh<8, true>(a, mk, mv, grid, smem, stream); break;
+        }
+    } else {
+        switch (kvh) {
+            case 1: st = launch_ragged_kvh<1, false>(a, mk, mv, grid, smem, stream); break;
+            case 2: st = launch_ragged_kvh<2, false>(a, mk, mv, grid, smem, stream); break;
+            case 4: st = launch_ragged_kvh<4, false>(a, mk, mv, grid, smem, stream); break;
+            default: st = launch_ragged_kvh<8, false>(a, mk, mv, grid, smem, stream); break;
+        }
+    }
+    if (st != B2_OK) return st;
+    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(kRgMergeThreads), 0, stream, a, npar);
 }
 
 }  // namespace
@@ -462,13 +668,9 @@ int clear_device_error_ragged() {
 
 }  // namespace b2
 
-namespace {
-bool rg_kvh_ok(size_t kvh) { return kvh == 1 || kvh == 2 || kvh == 4 || kvh == 8; }
-}  // namespace
-
 extern "C" size_t b2_decode_ragged_workspace_bytes(size_t num_seqs, size_t num_heads, size_t num_kv_heads,
                                                    size_t max_kv_len) {
-    if (!rg_kvh_ok(num_kv_heads)) return 0;
+    if (!b2::rg_kvh_ok(num_kv_heads)) return 0;
     return b2::rg_layout(num_seqs, num_heads, num_kv_heads, max_kv_len).total_bytes;
 }
 
@@ -479,69 +681,58 @@ extern "C" int b2_launch_causal_attention_decode_ragged(const void* d_q, size_t 
                                                         size_t num_seqs, size_t num_heads, size_t num_kv_heads,
                                                         size_t head_dim, void* d_workspace, size_t workspace_bytes,
                                                         b2_stream_t stream_handle) {
-    using namespace b2;
-    if (num_seqs == 0 || max_kv_len == 0 || num_kv_heads == 0 || head_dim == 0) return B2_NOTHING_TO_DO;
-    if (num_heads % num_kv_heads != 0) return B2_NOTHING_TO_DO;
-    if (!d_q || !d_k_cache || !d_v_cache || !d_kv_len || !d_out || !d_workspace) return B2_ERR_INVALID_ARG;
-    const size_t group = num_heads / num_kv_heads;
-    if (head_dim != 128 || !rg_kvh_ok(num_kv_heads) || group > 8 || num_seqs > kRgMaxSeqs ||
-        max_kv_len > 0x7fffffffull)
-        return B2_ERR_UNSUPPORTED;
-    const size_t kv_dim = num_kv_heads * head_dim;
-    if (q_seq_stride == 0) q_seq_stride = num_heads * head_dim;
-    if (out_seq_stride == 0) out_seq_stride = num_heads * head_dim;
-    if (cache_seq_stride == 0) cache_seq_stride = max_kv_len * kv_dim;
-    if (q_seq_stride < num_heads * head_dim || out_seq_stride < num_heads * head_dim) return B2_ERR_INVALID_ARG;
-    if (num_seqs > 1 && cache_seq_stride < max_kv_len * kv_dim) return B2_ERR_INVALID_ARG;  // caches overlap
-    if (!aligned16(d_q) || !aligned16(d_k_cache) || !aligned16(d_v_cache) || !aligned16(d_workspace) ||
-        q_seq_stride % 8 != 0 || cache_seq_stride % 8 != 0)
-        return B2_ERR_ALIGNMENT;
-    const RgWorkspace w = rg_layout(num_seqs, num_heads, num_kv_heads, max_kv_len);
-    if (workspace_bytes < w.total_bytes) return B2_ERR_WORKSPACE;
-    const uint32_t kvh = static_cast<uint32_t>(num_kv_heads);
-    const uint32_t npar = rg_npar(kvh);
-    const size_t stage_bytes = 2ull * kTile * kvh * 256;
-    const size_t fixed = 1024 + kRgQSlots * num_heads * 256 + 256;
-    uint32_t stages = static_cast<uint32_t>((kRgSmemLimit - fixed) / stage_bytes) / npar * npar;
-    if (stages > 32) stages = 32 / npar * npar;
-    if (stages == 0) return B2_ERR_UNSUPPORTED;
+    b2::RaggedCall c{};
+    c.q = d_q;
+    c.q_seq_stride = q_seq_stride;
+    c.k_cache = d_k_cache;
+    c.v_cache = d_v_cache;
+    c.cache_seq_stride = cache_seq_stride;
+    c.kv_len = d_kv_len;
+    c.kv_len_bias = kv_len_bias;
+    c.max_kv_len = max_kv_len;
+    c.out = d_out;
+    c.out_seq_stride = out_seq_stride;
+    c.num_seqs = num_seqs;
+    c.num_heads = num_heads;
+    c.num_kv_heads = num_kv_heads;
+    c.head_dim = head_dim;
+    c.workspace = d_workspace;
+    c.workspace_bytes = workspace_bytes;
+    return b2::launch_ragged(c, reinterpret_cast<cudaStream_t>(stream_handle));
+}
 
-    float* ws = static_cast<float*>(d_workspace);
-    RaggedArgs a{};
-    a.q = static_cast<const __half*>(d_q);
-    a.q_seq_stride = q_seq_stride;
-    a.kv_len = d_kv_len;
-    a.kv_len_bias = kv_len_bias;
-    a.max_kv_len = static_cast<uint32_t>(max_kv_len);
-    a.out = static_cast<__half*>(d_out);
-    a.out_seq_stride = out_seq_stride;
-    a.po = ws + w.po;
-    a.pm = ws + w.pm;
-    a.pl = ws + w.pl;
-    a.counter = reinterpret_cast<uint32_t*>(ws + w.counter);
-    a.unit_word = a.counter + 1;
-    a.num_seqs = static_cast<uint32_t>(num_seqs);
-    a.num_heads = static_cast<uint32_t>(num_heads);
-    a.group = static_cast<uint32_t>(group);
-    a.stages = stages;
-    a.scale_log2 = kLog2e / sqrtf(static_cast<float>(head_dim));
-
-    CUtensorMap mk, mv;
-    if (encode_token_rows_by_column_block_seqs(&mk, d_k_cache, max_kv_len, kvh * 256, num_seqs,
-                                               cache_seq_stride * 2, kTile) != 0 ||
-        encode_token_rows_by_column_block_seqs(&mv, d_v_cache, max_kv_len, kvh * 256, num_seqs,
-                                               cache_seq_stride * 2, kTile) != 0)
-        return B2_ERR_CUDA;
-    const size_t smem = fixed + stages * stage_bytes + 2 * (stages + kRgQSlots) * sizeof(uint64_t);
-    const uint32_t grid = static_cast<uint32_t>(device_sms_rg());
-    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
-    int st;
-    switch (kvh) {
-        case 1: st = launch_ragged_kvh<1>(a, mk, mv, grid, smem, stream); break;
-        case 2: st = launch_ragged_kvh<2>(a, mk, mv, grid, smem, stream); break;
-        case 4: st = launch_ragged_kvh<4>(a, mk, mv, grid, smem, stream); break;
-        default: st = launch_ragged_kvh<8>(a, mk, mv, grid, smem, stream); break;
-    }
-    if (st != B2_OK) return st;
-    return launch_pdl(merge_ragged_kernel, dim3(a.num_seqs, a.num_heads), dim3(kRgMergeThreads), 0, stream, a, npar);
+extern "C" int b2_launch_decode_step_ragged_fused(const void* d_q, size_t q_seq_stride, const void* d_k_new,
+                                                  const void* d_v_new, size_t kv_new_stride, void* d_k_cache,
+                                                  void* d_v_cache, size_t cache_seq_stride, const void* d_cos,
+                                                  const void* d_sin, size_t rope_rows, bool apply_rotation,
+                                                  const int32_t* d_pos, size_t max_kv_len, void* d_out,
+                                                  size_t out_seq_stride, size_t num_seqs, size_t num_heads,
+                                                  size_t num_kv_heads, size_t head_dim, void* d_workspace,
+                                                  size_t workspace_bytes, b2_stream_t stream_handle) {
+    b2::RaggedCall c{};
+    c.q = d_q;
+    c.q_seq_stride = q_seq_stride;
+    c.k_cache = d_k_cache;
+    c.v_cache = d_v_cache;
+    c.cache_seq_stride = cache_seq_stride;
+    c.kv_len = d_pos;
+    c.kv_len_bias = 1;
+    c.max_kv_len = max_kv_len;
+    c.out = d_out;
+    c.out_seq_stride = out_seq_stride;
+    c.num_seqs = num_seqs;
+    c.num_heads = num_heads;
+    c.num_kv_heads = num_kv_heads;
+    c.head_dim = head_dim;
+    c.workspace = d_workspace;
+    c.workspace_bytes = workspace_bytes;
+    c.step = true;
+    c.k_new = d_k_new;
+    c.v_new = d_v_new;
+    c.kv_new_stride = kv_new_stride;
+    c.cos = d_cos;
+    c.sin = d_sin;
+    c.rope_rows = rope_rows;
+    c.rotate = apply_rotation;
+    return b2::launch_ragged(c, reinterpret_cast<cudaStream_t>(stream_handle));
 }

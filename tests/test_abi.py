@@ -204,5 +204,26 @@ def test_ragged_decode_validation_without_cuda():
                                                 NULL) == -1
     assert L.b2_launch_rope_and_store_kv_ragged(f, f, f, f, f, 100, f, f, 4, 16, 4, 128, 0, 0, f, 64, True,
                                                 NULL) == -1
+
+
+def test_fused_ragged_step_validation_without_cuda():
+    """b2_launch_decode_step_ragged_fused checks everything before its first CUDA call."""
+    L = b200attn.lib()
+    f = 0x1000
+    ws = L.b2_decode_ragged_workspace_bytes(8, 16, 4, 4096)
+
+    def call(q=f, qs=0, kn=f, vn=f, kns=0, k=f, v=f, cs=0, cos=f, sin=f, rows=4096, rot=True, pos=f, mx=4096,
+             out=f, os_=0, B=8, H=16, KVH=4, d=128, w=f, wb=ws):
+        return L.b2_launch_decode_step_ragged_fused(q, qs, kn, vn, kns, k, v, cs, cos, sin, rows, rot, pos, mx, out,
+                                                    os_, B, H, KVH, d, w, wb, NULL)
+    assert call(B=0) == 1 and call(mx=0) == 1 and call(KVH=3) == 1            # silent skips
+    assert call(q=None) == -1 and call(pos=None) == -1 and call(w=None) == -1
+    assert call(vn=None) == -1                                                 # K without V
+    assert call(cos=None) == -1 and call(rows=0) == -1                         # RoPE inputs
+    assert call(kns=100) == -1                                                 # K/V rows overlap
+    assert call(d=64) == -2 and call(B=2000) == -2
+    assert call(kn=f + 4) == -3 and call(kns=516) == -3 and call(cos=f + 2) == -3
+    # NoPE needs no tables: this call gets as far as the workspace check
+    assert call(rot=False, cos=None, sin=None, rows=0, wb=16) == -5
     assert L.b2_launch_rope_and_store_kv_ragged(f, f, f, f, f, 0, f, f, 0, 16, 4, 128, 0, 0, f, 64, True,
                                                 NULL) == 1

@@ -188,3 +188,143 @@ def test_ragged_rope_nope_and_out_of_range(cuda):
     np.testing.assert_array_equal(bits(host(kc)), bits(ek))
     np.testing.assert_array_equal(bits(host(vc)), bits(ev))
     np.testing.assert_array_equal(bits(host(dqkv)), bits(qkv))   # NoPE leaves Q untouched
+
+
+def _fused_ragged(qkv_d, kc, vc, cache_seq_stride, cos_d, sin_d, rope_rows, rotate, pos, max_len, B, H, KVH,
+                  ws=None, append=True):
+    import torch
+    total = H * D + 2 * KVH * D
+    out = torch.full((B, H * D), -7.0, dtype=torch.float16, device="cuda")
+    if ws is None:
+        ws = _workspace(B, H, KVH, max_len)
+    b200attn.launch_decode_step_ragged_fused(qkv_d, total, qkv_d[:, H * D:] if append else None,
+                                             qkv_d[:, H * D + KVH * D:] if append else None, total, kc, vc,
+                                             cache_seq_stride, cos_d if rotate else None, sin_d if rotate else None,
+                                             rope_rows, rotate, pos, max_len, out, 0, B, H, KVH, D, ws[0], ws[1])
+    _sync()
+    return host(out)
+
+
+def _oracle_ragged_step(qkv, kh, vh, pos, cos, sin, rotate, H, KVH, max_len):
+    """Per sequence: RoPE + append at row p (the reference's launch_rope_and_store_kv,
+    rope.hip.cpp:138-196), then decode over rows [0, p]."""
+    B = len(pos)
+    ek, ev = kh.copy(), vh.copy()
+    outs = []
+    qd, kd = H * D, KVH * D
+    for b, p in enumerate(pos):
+        oq, ok, ov = qkv[b, :qd].copy(), qkv[b, qd:qd + kd].copy(), qkv[b, qd + kd:].copy()
+        if 0 <= p < max_len:
+            oracle.rope_and_store_kv(oq, ok, ov, ek[b], ev[b], cos, sin, 1, H, KVH, D, qd, kd, p, rotate)
+        n = min(p + 1, max_len) if p >= 0 else 0
+        if n == 0:
+            outs.append(None)
+            continue
+        _, o32 = oracle.decode_attention(oq, ek[b], ev[b], n, H, KVH, D)
+        outs.append(o32.reshape(-1))
+    return ek, ev, outs
+
+
+@pytest.mark.parametrize("rotate", [True, False])
+def test_ragged_fused_step_vs_oracle(cuda, rotate):
+    """One call per layer: RoPE of each sequence's new token, its K/V append and
+    the ragged decode; caches bit-exact vs the oracle, outputs within tolerance,
+    the QKV rows untouched. Positions at 0, tile and unit edges, and the last row."""
+    import torch
+    H, KVH, max_len = 16, 4, 2048
+    pos = [0, 1, 15, 16, 255, 256, 287, 288, 767, 768, 1000, max_len - 1]
+    B = len(pos)
+    total = H * D + 2 * KVH * D
+    cos, sin = b200attn.rope_tables_host(max_len, D, THETA)
+    kh = seeded_f16((B, max_len, KVH * D), 81)
+    vh = seeded_f16((B, max_len, KVH * D), 82)
+    qkv = seeded_f16((B, total), 83)
+    kc, vc, dqkv = dev(kh), dev(vh), dev(qkv)
+    dpos = torch.tensor(pos, dtype=torch.int32, device=cuda)
+    got = _fused_ragged(dqkv, kc, vc, max_len * KVH * D, dev(cos), dev(sin), max_len, rotate, dpos, max_len, B, H, KVH)
+    ek, ev, outs = _oracle_ragged_step(qkv, kh, vh, pos, cos, sin, rotate, H, KVH, max_len)
+    np.testing.assert_array_equal(bits(host(kc)), bits(ek))
+    np.testing.assert_array_equal(bits(host(vc)), bits(ev))
+    np.testing.assert_array_equal(bits(host(dqkv)), bits(qkv))  # Q / K / V rows are read, not written
+    for b, o32 in enumerate(outs):
+        assert_attention_close(got[b], o32)
+    assert b200attn.lib().b2_device_error_word() == 0
+
+
+def test_ragged_fused_step_equals_two_launches(cuda):
+    """Same inputs through launch_rope_and_store_kv_ragged + the ragged decode:
+    identical caches and bit-identical outputs (same rounding of the rotated Q,
+    same units and merge), config-5-like lengths, one workspace for both."""
+    import torch
+    H, KVH, max_len, B = 16, 4, 4096, 24
+    pos = [int(x) for x in np.random.default_rng(9).integers(0, max_len, B)]
+    total = H * D + 2 * KVH * D
+    cos, sin = b200attn.rope_tables_host(max_len, D, THETA)
+    kh = seeded_f16((B, max_len, KVH * D), 91)
+    vh = seeded_f16((B, max_len, KVH * D), 92)
+    qkv = seeded_f16((B, total), 93)
+    ws = _workspace(B, H, KVH, max_len)
+    dpos = torch.tensor(pos, dtype=torch.int32, device=cuda)
+    kc, vc = dev(kh), dev(vh)
+    got = _fused_ragged(dev(qkv), kc, vc, max_len * KVH * D, dev(cos), dev(sin), max_len, True, dpos, max_len, B, H,
+                        KVH, ws=ws)
+    kc2, vc2, dq2 = dev(kh), dev(vh), dev(qkv)
+    b200attn.launch_rope_and_store_kv_ragged(dq2, dq2[:, H * D:], dq2[:, H * D + KVH * D:], kc2, vc2,
+                                             max_len * KVH * D, dev(cos), dev(sin), B, H, KVH, D, total, total, dpos,
+                                             max_len, True)
+    out2 = torch.empty((B, H * D), dtype=torch.float16, device=cuda)
+    b200attn.launch_causal_attention_decode_ragged(dq2, total, kc2, vc2, max_len * KVH * D, dpos, 1, max_len, out2,
+                                                   0, B, H, KVH, D, ws[0], ws[1])
+    _sync()
+    np.testing.assert_array_equal(bits(host(kc)), bits(host(kc2)))
+    np.testing.assert_array_equal(bits(host(vc)), bits(host(vc2)))
+    np.testing.assert_array_equal(bits(got), bits(host(out2)))
+
+
+def test_ragged_fused_step_bad_and_empty_positions(cuda):
+    """A position outside the RoPE table appends nothing, leaves Q unrotated and
+    sets bit 1 of the device error word; a negative position gives a zero output;
+    without K/V rows nothing is appended."""
+    import torch
+    H, KVH, max_len = 16, 4, 512
+    rope_rows = 300
+    pos = [10, 400, -1, 299]
+    B = len(pos)
+    total = H * D + 2 * KVH * D
+    cos, sin = b200attn.rope_tables_host(rope_rows, D, THETA)
+    kh = seeded_f16((B, max_len, KVH * D), 101)
+    vh = seeded_f16((B, max_len, KVH * D), 102)
+    qkv = seeded_f16((B, total), 103)
+    kc, vc = dev(kh), dev(vh)
+    dpos = torch.tensor(pos, dtype=torch.int32, device=cuda)
+    assert b200attn.lib().b2_device_error_word() == 0
+    got = _fused_ragged(dev(qkv), kc, vc, max_len * KVH * D, dev(cos), dev(sin), rope_rows, True, dpos, max_len, B,
+                        H, KVH)
+    assert b200attn.lib().b2_device_error_word() & 2
+    assert b200attn.lib().b2_clear_device_error_word() == 0
+    ek, ev = kh.copy(), vh.copy()
+    qd, kd = H * D, KVH * D
+    for b in (0, 3):  # in-table positions are appended as usual
+        oq, ok, ov = qkv[b, :qd].copy(), qkv[b, qd:qd + kd].copy(), qkv[b, qd + kd:].copy()
+        oracle.rope_and_store_kv(oq, ok, ov, ek[b], ev[b], cos, sin, 1, H, KVH, D, qd, kd, pos[b], True)
+        _, o32 = oracle.decode_attention(oq, ek[b], ev[b], pos[b] + 1, H, KVH, D)
+        assert_attention_close(got[b], o32.reshape(-1))
+    np.testing.assert_array_equal(bits(host(kc)), bits(ek))  # nothing appended at 400 or -1
+    np.testing.assert_array_equal(bits(host(vc)), bits(ev))
+    # position 400: unrotated Q over the 401 stored rows
+    _, o32 = oracle.decode_attention(qkv[1, :qd].copy(), kh[1], vh[1], 401, H, KVH, D)
+    assert_attention_close(got[1], o32.reshape(-1))
+    assert np.all(got[2] == 0)
+    # no K/V rows: nothing appended, attention over the stored rows
+    kc3, vc3 = dev(kh), dev(vh)
+    got3 = _fused_ragged(dev(qkv), kc3, vc3, max_len * KVH * D, dev(cos), dev(sin), rope_rows, True,
+                         torch.tensor([10, 20, 30, 40], dtype=torch.int32, device=cuda), max_len, B, H, KVH,
+                         append=False)
+    np.testing.assert_array_equal(bits(host(kc3)), bits(kh))
+    for b, p in enumerate([10, 20, 30, 40]):
+        oq = qkv[b, :qd].copy()
+        oracle.rope_and_store_kv(oq, qkv[b, qd:qd + kd].copy(), None, None, None, cos, sin, 1, H, KVH, D, qd, kd, p,
+                                 True)
+        _, o32 = oracle.decode_attention(oq, kh[b], vh[b], p + 1, H, KVH, D)
+        assert_attention_close(got3[b], o32.reshape(-1))
+    assert b200attn.lib().b2_device_error_word() == 0  # every position of this call is in the table

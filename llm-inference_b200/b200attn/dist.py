@@ -324,15 +324,17 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
     H, KVH, D, L = st.H, st.KVH, st.D, st.L
     q_dim, kv_dim = H * D, KVH * D
     total = q_dim + 2 * kv_dim
-    pos_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    # one pinned position word per step, written before any copy is queued (a
+    # host write into a word an earlier queued copy still reads would race)
+    n_pos = max(warmup, steps)
+    pos_host = torch.arange(past, past + n_pos, dtype=torch.int32).pin_memory()
     pos_dev = torch.zeros(1, dtype=torch.int32, device=qkv.device)
 
     def step(s):
         pos = past + s
         qkv.copy_(qkv_host, non_blocking=True)
         if mode == "fused":
-            pos_host[0] = pos
-            pos_dev.copy_(pos_host, non_blocking=True)
+            pos_dev.copy_(pos_host[s:s + 1], non_blocking=True)
             for l in range(L):
                 row = qkv[l]
                 K.launch_decode_step_fused(row, row[q_dim:], row[q_dim + kv_dim:], cache.get_k_cache(l),

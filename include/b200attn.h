@@ -259,16 +259,17 @@ int b2_launch_merge_partials_strided(const float* d_o, const float* d_m, const f
 /* d_pos[0] += delta on the stream (one thread), for device-resident positions. */
 int b2_advance_position(int32_t* d_pos, int32_t delta, b2_stream_t stream);
 
-/* ---- Fused decode step (two kernels per layer) ----------------------------
+/* ---- Fused decode step (one kernel per layer) -----------------------------
  * No single counterpart in the reference: it replaces, for one decode token
  * of one layer, the reference's launch_rope_and_store_kv
  * (src/kernels/rope.hip.cpp:138-196) followed by
  * launch_causal_attention_decode and its merge
  * (src/kernels/causal_attention.hip.cpp:840-921), i.e. the three nodes per
  * layer of include/model_inference.hpp:96-123, with one graph-static call:
- * a split-attention kernel that also does the RoPE and the append, whose
- * CTAs take 16-token tiles from a shared counter until none are left, then
- * the merge kernel.
+ * one split-attention kernel that also does the RoPE and the append, whose
+ * CTAs take 16-token tiles from a shared counter until none are left and
+ * whose first min(splits, num_heads) CTAs then merge the split partials of
+ * one head each.
  *  - kv_len = clamp(d_kv_len[0] + kv_len_bias, 0, max_kv_len), read at launch.
  *  - Q (d_q, [num_heads][128], before RoPE) is rotated in registers at
  *    position d_pos[0] when apply_rotation; d_q is read, never written.

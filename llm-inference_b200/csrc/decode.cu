@@ -168,10 +168,12 @@ constexpr uint32_t kStepMaxSplits = 256;      // partial slots in a fused-step w
 // 12 consumer warps (KV head x tile parity) run the MMA tile math; the CTA's
 // states are combined into one (o, m, l) partial per head.
 // Static (reference launchers): CTA `split` owns a contiguous token range.
-// kFused (the fused decode step): CTAs claim tiles from a global counter, so
-// all CTAs finish together whatever their DRAM share; Q is rotated in
-// registers, and the CTA that claims the tile holding row kv_len - 1 appends
-// the new token's K/V there before copying that tile.
+// kFused (the fused decode step): each CTA streams an even share of ~2/3 of
+// the tiles, then claims tiles from a global counter, so all CTAs finish
+// together whatever their DRAM share; Q is rotated in registers; consumer
+// warp 0 of the last split appends the new token's K/V at row kv_len - 1
+// before its producer copies the tile holding that row; splits
+// 0 .. min(S, H) - 1 then merge the split partials (step_merge).
 // ---- in-kernel merge of the fused step -------------------------------------
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {

@@ -215,19 +215,22 @@ __device__ __forceinline__ uint2 ld_pair_sys(const uint2* p) {
     return v;
 }
 
-// Publish this rank's partial (O over the 128 dims held by threads 0..127,
-// M, L) of head h to every rank, wait (bounded) for every rank's partial of
-// head h for exchange e, and write the merged fp16 output. Threads 0..127
-// of the CTA take part; returns false on a timeout.
+// Publish this rank's partial of head h for dims d0 .. d0 + nd - 1 (O of dim
+// d0 + i held by thread i; M, L) to every rank, wait (bounded) for every
+// rank's words of those dims for exchange e, and write the merged fp16
+// output there. Threads 0 .. nd - 1 of the CTA take part (two CTAs may serve
+// the two halves of a head: both write the same M and L words); returns
+// false on a timeout.
 __device__ __noinline__ bool step_exchange_head(const StepExt& x, uint32_t H, uint32_t h, uint32_t e, float O,
-                                                float M, float L) {
-    const uint32_t slot = e & 1, world = x.world, d = threadIdx.x;
-    if (d >= 128) return true;
+                                                float M, float L, uint32_t d0, uint32_t nd) {
+    const uint32_t slot = e & 1, world = x.world;
+    if (threadIdx.x >= nd) return true;
+    const uint32_t d = d0 + threadIdx.x;
     for (uint32_t r = 0; r < world; ++r) {
         uint2* dst = reinterpret_cast<uint2*>(x.peers[r]) +
                      ((static_cast<uint64_t>(slot) * world + x.rank) * H + h) * kExchangePitch;
         st_pair_sys(dst + d, O, e);
-        if (d == 0) {
+        if (threadIdx.x == 0) {
             st_pair_sys(dst + 128, M, e);
             st_pair_sys(dst + 129, L, e);
         }
@@ -311,26 +314,27 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Every CTA has written its partials [H][S][128] / [H][S] (natural-log m)
-// and adds one to the arrival counter counters[1] with a release reduction;
-// the counter only grows, and counters[2] holds its value at the start of
-// the launch (`base`, read after the dependency wait). Splits r < R =
-// min(S, H) merge heads r, r + R, ...: once the counter reaches base + S
-// (acquire) the CTA copies the head's S partial rows into shared memory with
-// one bulk copy while its threads reduce the S maxima and weight sums, then
-// 12 warps sum the weighted rows (rows w, w + 12, ... in warp w, four dims
-// per lane) and 128 threads add the 12 sums.
-// Merging split 0 resets the tile counter and records base + S for the next
-// launch (no other CTA reads either word again in this launch). The merging
-// CTAs wait for CTAs that may start after them, which every launch can
-// schedule: there is one CTA per SM and at most as many CTAs as SMs.
+// Every CTA has written its partials -- o as [H][2 halves][S][64] (each half
+// head's rows contiguous), m (natural log) and l as [H][S] -- and adds one to
+// the arrival counter counters[1] with a release reduction; the counter only
+// grows, and counters[2] holds its value at the start of the launch (`base`,
+// read after the dependency wait). Splits r < R = min(S, 2H) merge the half
+// heads r, r + R, ...: once the counter reaches base + S (acquire) the CTA
+// copies the half head's S rows of 64 floats into shared memory with one
+// bulk copy while its threads reduce the head's S maxima and weight sums,
+// then 12 warps sum the weighted rows (two rows per warp step, four dims per
+// lane, 24 interleaved row groups) and 64 threads add the group sums. Merging
+// split 0 resets the tile counter and records base + S for the next launch
+// (no other CTA reads either word again in this launch). The merging CTAs
+// wait for CTAs that may start after them, which every launch can schedule:
+// there is one CTA per SM and at most as many CTAs as SMs.
 // epoch_next: the exchange number of this launch (world > 1).
 __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x, uint32_t S, uint32_t split,
                                            uint8_t* smem, uint64_t* bar, uint32_t base, uint32_t epoch_next) {
     __shared__ uint32_t ok_s;
     __shared__ float red_s[2][kTmaThreads / 32];
     const uint32_t H = a.num_heads;
-    const uint32_t R = min(S, H);
+    const uint32_t R = min(S, 2 * H);
     // the CTA's partial stores happen before thread 0's release
     __syncthreads();
     const bool merger = split < R;
@@ -362,14 +366,16 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
     if (ok_s == 0u) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kWarps = kTmaThreads / 32;
-    float* rows = reinterpret_cast<float*>(smem);  // [S][128]
-    float* wts = rows + static_cast<size_t>(S) * 128;  // [S]
-    float* sums = wts + kStepMaxSplits;               // [12][128]
+    float* rows = reinterpret_cast<float*>(smem);     // [S][64]
+    float* wts = rows + static_cast<size_t>(S) * 64;  // [S]
+    float* sums = wts + kStepMaxSplits;              // [24][64]
+    const uint32_t sub = static_cast<uint32_t>(lane) >> 4, col4 = static_cast<uint32_t>(lane) & 15;
     uint32_t phase = 0;
-    for (uint32_t h = split; h < H; h += R, phase ^= 1u) {
+    for (uint32_t item = split; item < 2 * H; item += R, phase ^= 1u) {
+        const uint32_t h = item >> 1, d0 = (item & 1) * 64;
         if (threadIdx.x == 0) {
-            mbar_arrive_expect_tx(bar, S * 512u);
-            bulk_g2s_plain(rows, a.po + static_cast<uint64_t>(h) * S * 128, S * 512u, bar);
+            mbar_arrive_expect_tx(bar, S * 256u);
+            bulk_g2s_plain(rows, a.po + static_cast<uint64_t>(item) * S * 64, S * 256u, bar);
         }
         const uint32_t c = threadIdx.x;
         const float m = c < S ? __ldcg(a.pm + static_cast<uint64_t>(h) * S + c) : -INFINITY;
@@ -394,29 +400,30 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) L += red_s[1][w];
         if (warp < 12) {
-            // warp w sums rows w, w + 12, ... for dims 4*lane .. 4*lane + 3
+            // row group g = 2 * warp + sub sums rows g, g + 24, ... for dims 4 * col4 .. + 3
+            const uint32_t g = 2 * static_cast<uint32_t>(warp) + sub;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-            for (uint32_t cc = warp; cc < S; cc += 12) {
+            for (uint32_t cc = g; cc < S; cc += 24) {
                 const float wc = wts[cc];
-                const float4 r4 = reinterpret_cast<const float4*>(rows + cc * 128)[lane];
+                const float4 r4 = reinterpret_cast<const float4*>(rows + cc * 64)[col4];
                 acc.x = fmaf(wc, r4.x, acc.x);
                 acc.y = fmaf(wc, r4.y, acc.y);
                 acc.z = fmaf(wc, r4.z, acc.z);
                 acc.w = fmaf(wc, r4.w, acc.w);
             }
-            reinterpret_cast<float4*>(sums + warp * 128)[lane] = acc;
+            reinterpret_cast<float4*>(sums + g * 64)[col4] = acc;
         }
         __syncthreads();
-        if (threadIdx.x < 128) {
+        if (threadIdx.x < 64) {
             const uint32_t d = threadIdx.x;
             float O = 0.f;
 #pragma unroll
-            for (int w = 0; w < 12; ++w) O += sums[w * 128 + d];
-            if (x.world <= 1) step_store(x, h, d, O, M, L);
-            else (void)step_exchange_head(x, H, h, epoch_next, O, M, L);
+            for (int g = 0; g < 24; ++g) O += sums[g * 64 + d];
+            if (x.world <= 1) step_store(x, h, d0 + d, O, M, L);
+            else (void)step_exchange_head(x, H, h, epoch_next, O, M, L, d0, 64);
         }
-        __syncthreads();  // rows, weights and sums are reused by the next head
+        __syncthreads();  // rows, weights and sums are reused by the next item
     }
 }
 
@@ -456,10 +463,11 @@ __device__ __forceinline__ uint8_t* stg_of(uint8_t* ring, uint32_t s, uint32_t t
 // KV head h are h, h + KVH, ... (one per tile parity); warps of parity >= 1
 // leave their state in shared memory `sm` and the parity-0 warp of each KV
 // head folds them into its own registers -- every lane reads the fragment
-// positions it holds itself -- and writes the partial from registers:
-// po [head][splits][128], pm (natural-log max) and pl [head][splits].
-// Every thread of the CTA calls it (one barrier when npar > 1).
-template <uint32_t KVH>
+// positions it holds itself -- and writes the partial from registers: po
+// [head][splits][128] (kHalves: [head][2][splits][64], the fused step's
+// merge layout), pm (natural-log max) and pl [head][splits]. Every thread of
+// the CTA calls it (one barrier when npar > 1).
+template <uint32_t KVH, bool kHalves>
 __device__ __forceinline__ void combine_split(WarpState& st, uint32_t warp, uint32_t lane, float* sm, uint32_t group,
                                               uint32_t split, uint32_t splits, float* po, float* pm, float* pl) {
     constexpr uint32_t npar = kTmaConsumers / KVH;
@@ -514,8 +522,8 @@ __device__ __forceinline__ void combine_split(WarpState& st, uint32_t warp, uint
         st.l0 = L0;
         st.l1 = L1;
     }
-    store_warp_partial(st, po, pm, pl, static_cast<uint64_t>(splits) * 128, 128, splits, 1, split, warp * group,
-                       group, g, t);
+    store_warp_partial(st, po, pm, pl, static_cast<uint64_t>(splits) * 128, kHalves ? 64 : 128,
+                       kHalves ? static_cast<uint64_t>(splits) * 64 : 64, splits, 1, split, warp * group, group, g, t);
 }
 
 template <bool kFused, uint32_t KVH>
@@ -584,7 +592,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             if (x.world > 1) {
                 // nothing to attend here, but the other ranks wait for this rank's partials
                 for (uint32_t h = 0; h < a.num_heads; ++h)
-                    (void)step_exchange_head(x, a.num_heads, h, epoch_next, 0.f, -INFINITY, 0.f);
+                    (void)step_exchange_head(x, a.num_heads, h, epoch_next, 0.f, -INFINITY, 0.f, 0, 128);
                 if (threadIdx.x == 0) *x.epoch = epoch_next;
             } else {
                 step_write_empty(a.num_heads, x, threadIdx.x, blockDim.x);
@@ -819,7 +827,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     // All ring reads and copies are done: reuse the ring for the combine.
     __syncthreads();
-    combine_split<KVH>(st, static_cast<uint32_t>(warp), static_cast<uint32_t>(lane), reinterpret_cast<float*>(ring),
+    combine_split<KVH, kFused>(st, static_cast<uint32_t>(warp), static_cast<uint32_t>(lane), reinterpret_cast<float*>(ring),
                        a.group, split, ext.splits, a.po, a.pm, a.pl);
     if (!ok) atomicOr(&g_device_error, kErrWaitTimeout);
     if constexpr (kFused) {

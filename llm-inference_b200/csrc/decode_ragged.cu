@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
             if (u == kNoUnit || kl != cur_local) {
                 if (cur_local != kNoUnit) {
                     state_finish(st);
-                    store_warp_partial(st, a.po, a.pm, a.pl, 128, static_cast<uint64_t>(a.num_heads) * 128, 1,
+                    store_warp_partial(st, a.po, a.pm, a.pl, 128, static_cast<uint64_t>(a.num_heads) * 128, 64, 1,
                                        a.num_heads, cur_unit * npar + par, kvh * a.group, a.group, g, t);
                     state_init(st);
                 }

@@ -227,11 +227,13 @@ __device__ __forceinline__ void load_v_frags(const uint8_t* vt, uint32_t row_byt
 
 // Write one warp's state (after state_finish) as partial p of its KV head's
 // query heads head0 .. head0 + group - 1: o of (head, p) at
-// po + head * o_hs + p * o_ps (128 floats), m (natural log) and l at
+// po + head * o_hs + p * o_ps, dims 0..63 there and dims 64..127 o_half
+// floats later (64 for contiguous rows), m (natural log) and l at
 // pm / pl + head * ml_hs + p * ml_ps.
 __device__ __forceinline__ void store_warp_partial(const WarpState& st, float* po, float* pm, float* pl,
-                                                   uint64_t o_hs, uint64_t o_ps, uint64_t ml_hs, uint64_t ml_ps,
-                                                   uint32_t p, uint32_t head0, uint32_t group, int g, int t) {
+                                                   uint64_t o_hs, uint64_t o_ps, uint64_t o_half, uint64_t ml_hs,
+                                                   uint64_t ml_ps, uint32_t p, uint32_t head0, uint32_t group, int g,
+                                                   int t) {
 #pragma unroll
     for (int hsel = 0; hsel < 2; ++hsel) {
         const uint32_t hh = 2 * t + hsel;
@@ -240,8 +242,8 @@ __device__ __forceinline__ void store_warp_partial(const WarpState& st, float* p
         float* o = po + head * o_hs + p * o_ps;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-            const int d = 64 * (mt >> 2) + 8 * g + 2 * (mt & 3);
-            *reinterpret_cast<float2*>(o + d) =
+            const int d = 8 * g + 2 * (mt & 3);  // within the half mt >> 2
+            *reinterpret_cast<float2*>(o + (mt >> 2) * o_half + d) =
                 hsel == 0 ? make_float2(st.o[mt][0], st.o[mt][2]) : make_float2(st.o[mt][1], st.o[mt][3]);
         }
         if (g == 0) {

@@ -622,11 +622,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             // Tile order of split s: its even share [s*per, (s+1)*per) of ~2/3
             // of the tiles (the last split puts the last tile, which holds the
             // new row, after its first two, once consumer warp 0 has appended
-            // the row), then tiles of the pool
-            // [S*per, total - 1), claimed kClaim at a time from the counter with
-            // the next claim in flight while the current one streams, so CTAs
-            // that run ahead take more.
-            constexpr uint32_t kClaim = 2;
+            // the row), then tiles of the pool [S*per, total - 1), claimed one
+            // at a time from the counter with the next two claims in flight
+            // (`claimed`, `claimed2`, used in turn: each read sits in its own
+            // branch so it waits for its own round trip only), so CTAs that
+            // run ahead take more.
             const uint32_t total = (ext.kv_len + kTile - 1) / kTile;
             const uint32_t per = fused_share(total, ext.splits);  // per * S <= total - 1
             const uint32_t pool = per * ext.splits, pool_end = total - 1;
@@ -634,7 +634,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             uint32_t own = split * per, own_end = own + per;
             // With an own share the first claim goes out after the first copy
             // (its round trip is hidden behind the share); without one, now.
-            uint32_t claimed = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], kClaim) : 0u;
+            uint32_t claimed = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], 1u) : 0u;
+            uint32_t claimed2 = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], 1u) : 0u;
+            bool toggle = false;
             bool first_claim = per != 0 && pool < pool_end;
             // The tiles after the ones warmed before the wait: HBM starts on
             // them while the first copies come from L2.
@@ -660,9 +662,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                     tile = own++;
                 } else {
                     if (cur_left == 0) {
-                        cur = pool + __shfl_sync(0xffffffffu, claimed, 0);
-                        cur_left = cur < pool_end ? min(kClaim, pool_end - cur) : 0u;
-                        if (lane == 0 && cur_left != 0) claimed = atomicAdd(&x.counters[0], kClaim);
+                        if (toggle) {
+                            cur = pool + __shfl_sync(0xffffffffu, claimed2, 0);
+                            cur_left = cur < pool_end ? 1u : 0u;
+                            if (lane == 0 && cur_left != 0) claimed2 = atomicAdd(&x.counters[0], 1u);
+                        } else {
+                            cur = pool + __shfl_sync(0xffffffffu, claimed, 0);
+                            cur_left = cur < pool_end ? 1u : 0u;
+                            if (lane == 0 && cur_left != 0) claimed = atomicAdd(&x.counters[0], 1u);
+                        }
+                        toggle = !toggle;
                     }
                     tile = cur_left != 0 ? cur++ : total;
                     if (cur_left != 0) --cur_left;
@@ -698,7 +707,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                 }
                 if (first_claim) {
                     first_claim = false;
-                    if (lane == 0) claimed = atomicAdd(&x.counters[0], kClaim);
+                    if (lane == 0) {
+                        claimed = atomicAdd(&x.counters[0], 1u);
+                        claimed2 = atomicAdd(&x.counters[0], 1u);
+                    }
                 }
                 __syncwarp();
             }

@@ -40,7 +40,9 @@ class _TokenizerStub:
 
 
 def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None) -> None:
-    ref_root = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+    if "REFERENCE_ROOT" not in os.environ:
+        raise SystemExit("set REFERENCE_ROOT to the reference checkout (the directory holding python/reference.py)")
+    ref_root = Path(os.environ["REFERENCE_ROOT"])
     sys.path.insert(0, str(ref_root / "python"))
     import torch
     import transformers

@@ -15,9 +15,9 @@ dumps on the attention hot path:
 Each is raw little-endian FP16 exactly as python/reference.py:18-22 writes
 it. ``meta.json`` records the geometry, seed and library versions.
 
-It needs the reference checkout (set REFERENCE_ROOT, default the read-only
-mount this build was made against) and runs on CPU only. Nothing on a GPU box
-runs it; the tests read only the committed outputs.
+It needs the reference checkout (set REFERENCE_ROOT to the directory that
+holds python/reference.py) and runs on CPU only. Nothing on a GPU box runs
+it; the tests read only the committed outputs.
 """
 from __future__ import annotations
 

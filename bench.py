@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 GQA attention hot path.
 
-Workload (long-context decode): batch 1, a 65,536-token
+Workload (benchmark config 4, long-context decode): batch 1, a 65,536-token
 FP16 KV cache ~N(0, 0.5) per layer, 16 query / 4 KV heads, head_dim 128,
 36 layers. One step = one generated token through all 36 layers: per layer
 RoPE of the new token (NoPE on every 4th layer) + KV-cache append at
@@ -56,13 +56,13 @@ WORKLOAD = ("config4: long-context decode, batch 1, KV 65536 tokens ~N(0,0.5) FP
             "36 layers x 1 token per step (RoPE+append+split-KV decode+merge), KV_CHUNK 256")
 
 
-# BASELINE config 3 (prefill): 4 sequences x 8192 tokens, 36 layers, NoPE every 4th layer
+# benchmark config 3 (prefill): 4 sequences x 8192 tokens, 36 layers, NoPE every 4th layer
 PF_B, PF_S = 4, 8192
 PF_WORKLOAD = ("config3: causal GQA prefill, batch 4 x 8192 tokens, 16/4 heads, head_dim 128, N(0,1) FP16, "
                "36 layers x (RoPE theta 5e6 / NoPE every 4th layer + KV append + causal attention)")
 
 
-# BASELINE config 5 (ragged decode): 64 sequences, per-sequence caches of 16384 rows
+# benchmark config 5 (ragged decode): 64 sequences, per-sequence caches of 16384 rows
 RG_B, RG_MAX = 64, 16384
 RG_WORKLOAD = ("config5: ragged decode, 64 sequences, KV lengths numpy default_rng(2024).integers(512, 16385, 64) "
                "(length after the new token's append), per-sequence cache of 16384 rows, N(0,1) FP16, 16/4 heads, "

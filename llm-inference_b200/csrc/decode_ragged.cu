@@ -1,6 +1,6 @@
 // Ragged batched flash-decode for sm_100a: one new query token for each of B
 // sequences whose caches hold different numbers of tokens (the continuous-
-// batching decode step: 64 sequences, 512..16384 tokens).
+// batching decode step; benchmark config 5: 64 sequences, 512..16384 tokens).
 //
 // The reference engine decodes one sequence at a time
 // (src/kernels/causal_attention.hip.cpp:840-921 launch_causal_attention_decode);

@@ -10,7 +10,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
-# BASELINE acceptance for attention outputs against the FP32 CPU oracle.
+# Acceptance bar for attention outputs against the FP32 CPU oracle.
 MAX_ABS = 1e-2
 REL_L2 = 2e-3
 

@@ -200,7 +200,7 @@ def test_rank_partials_and_strided_merge(cuda, ranks):
 
 
 def test_config2_append_then_decode(cuda):
-    """cache 4096 tokens ~N(0,1), the new token RoPE'd at 4096 and
+    """benchmark config 2: cache 4096 tokens ~N(0,1), the new token RoPE'd at 4096 and
     appended, kv_len 4097, chunk 256 (17 chunks) + merge -- against the oracle."""
     import torch
     H, KVH, d, past = 16, 4, 128, 4096
@@ -237,7 +237,7 @@ def test_config2_append_then_decode(cuda):
 
 @pytest.mark.parametrize("kv_len", [65536, 65536 + 63])
 def test_long_context_64k_one_layer(cuda, kv_len):
-    """BASELINE config 4 size: 64K cached tokens ~N(0, 0.5), one layer, vs the oracle."""
+    """benchmark config 4 size: 64K cached tokens ~N(0, 0.5), one layer, vs the oracle."""
     import torch
     H, KVH, d = 16, 4, 128
     k = seeded_f16((kv_len, KVH * d), 21, std=0.5)

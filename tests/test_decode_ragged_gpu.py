@@ -1,5 +1,5 @@
 """Ragged batched decode (one new token for each of B sequences of different
-lengths) on the GPU vs the CPU oracle, per sequence.
+lengths; benchmark config 5) on the GPU vs the CPU oracle, per sequence.
 The oracle is the reference's single-sequence algebra
 (src/kernels/rope.hip.cpp:61-134, src/kernels/causal_attention.hip.cpp:493-838)
 applied to each sequence in turn."""
@@ -67,7 +67,7 @@ def test_ragged_lengths_vs_oracle(cuda, kvh, heads):
 
 
 def test_ragged_config5_shape(cuda):
-    """64 sequences, lengths U[512, 16384] from
+    """benchmark config 5: 64 sequences, lengths U[512, 16384] from
     numpy default_rng(seed).integers(512, 16385, 64), 16/4 heads, one layer."""
     import torch
     H, KVH, max_len, B = 16, 4, 16384, 64

@@ -245,7 +245,7 @@ def test_fused_step_other_gqa_shapes(cuda, kvh, heads):
 
 
 def test_fused_step_64k(cuda):
-    """BASELINE config 4 size (65,536 cached tokens + the new one) through the fused step."""
+    """benchmark config 4 size (65,536 cached tokens + the new one) through the fused step."""
     import torch
     past = 65536
     cap = past + 64

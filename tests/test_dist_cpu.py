@@ -28,7 +28,7 @@ def test_split_kv_plan_covers_range(past, world):
 
 def test_assign_sequences_balanced_and_complete():
     rng = np.random.default_rng(0)
-    lens = rng.integers(512, 16385, 64)
+    lens = rng.integers(512, 16385, 64)   # benchmark config 5
     for world in (1, 2, 4, 8):
         parts = bdist.assign_sequences(lens, world)
         got = sorted(i for p in parts for i in p)

@@ -1,4 +1,4 @@
-"""KV-split decode across GPUs (BASELINE config 4's multi-GPU path), one
+"""KV-split decode across GPUs (benchmark config 4's multi-GPU path), one
 process per GPU: each rank attends over its contiguous KV range, the tail rank
 appends the new token, and the per-head (o, m, l) partials are merged across
 ranks -- inside the fused kernel over CUDA-IPC peer memory ("peer") or by an

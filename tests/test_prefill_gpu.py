@@ -129,7 +129,7 @@ def test_prefill_batched_matches_per_sequence(cuda):
 
 @pytest.mark.parametrize("S", [8192])
 def test_prefill_config3_unit_sampled(cuda, S):
-    """One (sequence, KV head) unit of BASELINE config 3 at full length, sampled rows."""
+    """One (sequence, KV head) unit of benchmark config 3 at full length, sampled rows."""
     H, KVH, d = 16, 4, 128
     q = seeded_f16((S, H * d), 81)
     k = seeded_f16((S, KVH * d), 82)

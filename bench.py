@@ -526,11 +526,14 @@ def run_b200(args, rank, world):
         launch_ms = dec_ms
         timing = "CUDA events around isolated launches on the decode stream"
     achieved = dec_bytes / (launch_ms / 1e3) / 1e9
+    # ncu DRAM bytes of one 64K launch, scaled to this rank's launch by its
+    # algorithmic bytes (the same on one GPU; a 1/N range of the cache on N)
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+            t = json.load(f)
+        traffic = int(round(dec_bytes * t["bytes_per_launch"] / t["algorithmic_bytes"]))
 
     # ---- e2e: reference-facing C-ABI calls, host buffers in and out every step
     e2e = None

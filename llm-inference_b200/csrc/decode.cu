@@ -145,14 +145,15 @@ struct StepExt {
     const int32_t* pos_dev;  // RoPE position of the new token
     uint32_t rotate;         // 1 = RoPE, 0 = NoPE layer
     uint32_t table_rows;
-    uint32_t* counters;      // [0] next unclaimed tile, [1] CTAs done, [2] merges done; 0 at launch
+    uint32_t* counters;      // [0] next unclaimed pool tile (0 at launch), [1] CTA arrivals (only
+                             // grows), [2] the arrivals count at launch start
     __half* out;             // [H][128] fp16 result, or the rank partial below
     float* rank_o;
     float* rank_m;
     float* rank_l;
     // Cross-GPU exchange (world > 1): every rank's exchange buffer, mapped
     // into this process (peers[rank] is this rank's own); layout in
-    // exchange_layout(). epoch: this rank's count of exchanges so far.
+    // exchange_words(). epoch: this rank's count of exchanges so far.
     uint32_t world;
     uint32_t rank;
     uint32_t* epoch;
@@ -1290,7 +1291,8 @@ int launch_decode(const void* d_q, const void* d_k, const void* d_v, void* d_out
 }
 
 // Workspace of the fused step: partials for up to kStepMaxSplits splits
-// ([H][S][128] o, [H][S] m, [H][S] l, floats), then 3 counters.
+// ([H][2 halves][S][64] o, [H][S] m, [H][S] l, floats), then the 3 counter
+// words of StepExt::counters.
 struct StepWorkspace {
     size_t po, pm, pl, counter, total_bytes;
 };

@@ -227,3 +227,22 @@ def test_fused_ragged_step_validation_without_cuda():
     assert call(rot=False, cos=None, sin=None, rows=0, wb=16) == -5
     assert L.b2_launch_rope_and_store_kv_ragged(f, f, f, f, f, 0, f, f, 0, 16, 4, 128, 0, 0, f, 64, True,
                                                 NULL) == 1
+
+
+def test_python_bindings_match_header():
+    """Every function include/b200attn.h declares is bound in the ctypes table
+    with the same number of parameters (guards the Python mirror against ABI
+    drift)."""
+    import re
+    from b200attn._lib import SIGNATURES
+    src = open(os.path.join(ROOT, "include", "b200attn.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"//.*", "", src)
+    decls = re.findall(r"\b(?:int|size_t|unsigned int|uint64_t|const char\s*\*|void)\s+\*?\s*(b2_\w+)\s*\(([^)]*)\)\s*;",
+                       src)
+    assert len(decls) >= 30
+    for name, args in decls:
+        args = args.strip()
+        n = 0 if args in ("", "void") else len(args.split(","))
+        assert name in SIGNATURES, name
+        assert len(SIGNATURES[name][1]) == n, (name, n, len(SIGNATURES[name][1]))

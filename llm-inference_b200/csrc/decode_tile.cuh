@@ -331,8 +331,9 @@ __device__ __forceinline__ void state_to_smem(const WarpState& st, int slot, flo
 }
 
 // Combine `nslots` warp states of one KV head (slots first, first+stride, ...)
-// into the partial of (head kvh*group + hh, split), idx = hh*128 + d.
-// (Generic form; the persistent kernels use combine_tile<NPAR> below.)
+// into the partial of (head kvh*group + hh, split), idx = hh*128 + d (the
+// per-chunk split kernel; the persistent kernels fold warp states in
+// registers instead).
 __device__ __forceinline__ void combine_write(const float* sm_m, const float* sm_l, const float* sm_o, int first,
                                               int stride, int nslots, uint32_t kvh, uint32_t group, uint32_t split,
                                               uint32_t splits, float* po, float* pm, float* pl, uint32_t idx) {
@@ -352,123 +353,6 @@ __device__ __forceinline__ void combine_write(const float* sm_m, const float* sm
     if (d == 0) {
         pm[state] = M == -INFINITY ? -INFINITY : M * kLn2;
         pl[state] = L;
-    }
-}
-
-
-// Combine the NPAR warp states of each KV head held in shared memory (slots
-// h, h + KVH, ..., written by state_to_smem) and write one partial per
-// (query head, split): o [H][splits][128], m / l [H][splits]; m in natural-log
-// units. Fully unrolled over the slots.
-template <int NPAR>
-__device__ __forceinline__ void combine_tile(const float* sm_m, const float* sm_l, const float* sm_o, uint32_t kvh_count,
-                                             uint32_t group, uint32_t split, uint32_t splits, float* po, float* pm,
-                                             float* pl, uint32_t tid, uint32_t nthreads) {
-    const uint32_t total = kvh_count * group * 128;
-    for (uint32_t idx = tid; idx < total; idx += nthreads) {
-        const uint32_t head = idx >> 7, d = idx & 127;  // head = kvh * group + hh
-        const uint32_t kvh = head / group, hh = head - kvh * group;
-        float mv[NPAR], M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NPAR; ++w) {
-            mv[w] = sm_m[(kvh + kvh_count * w) * 8 + hh];
-            M = fmaxf(M, mv[w]);
-        }
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < NPAR; ++w) {
-            const uint32_t sl = kvh + kvh_count * w;
-            const float sc = mv[w] == -INFINITY ? 0.f : ex2(mv[w] - M);
-            L = fmaf(sc, sm_l[sl * 8 + hh], L);
-            O = fmaf(sc, sm_o[(sl * 8 + hh) * kOStride + d], O);
-        }
-        const uint64_t state = static_cast<uint64_t>(head) * splits + split;
-        po[state * 128 + d] = O;
-        if (d == 0) {
-            pm[state] = M == -INFINITY ? -INFINITY : M * kLn2;
-            pl[state] = L;
-        }
-    }
-}
-
-// Dispatch on the consumer warps per KV head of the persistent kernels.
-__device__ __forceinline__ void combine_tile_any(uint32_t npar, const float* sm_m, const float* sm_l, const float* sm_o,
-                                                 uint32_t kvh_count, uint32_t group, uint32_t split, uint32_t splits,
-                                                 float* po, float* pm, float* pl, uint32_t tid, uint32_t nthreads) {
-    switch (npar) {
-        case 1: combine_tile<1>(sm_m, sm_l, sm_o, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-        case 3: combine_tile<3>(sm_m, sm_l, sm_o, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-        case 6: combine_tile<6>(sm_m, sm_l, sm_o, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-        default: combine_tile<12>(sm_m, sm_l, sm_o, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-    }
-}
-
-// Combine for the persistent kernel, in two phases over all `nthreads`
-// threads: (1) one thread per query head computes the max M over its NPAR
-// slots, their scales 2^(m_w - M) (into `sc_s`, [heads][NPAR]) and L, and
-// writes m (natural log) and l of the partial; (2) every (head, dim) item sums
-// its NPAR scaled slot values, several items per thread in flight at once.
-template <int NPAR>
-__device__ __forceinline__ void combine_tile2(const float* sm_m, const float* sm_l, const float* sm_o, float* sc_s,
-                                              uint32_t kvh_count, uint32_t group, uint32_t split, uint32_t splits,
-                                              float* po, float* pm, float* pl, uint32_t tid, uint32_t nthreads) {
-    const uint32_t heads = kvh_count * group;
-    if (tid < heads) {
-        const uint32_t kvh = tid / group, hh = tid - kvh * group;
-        float mv[NPAR], M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NPAR; ++w) {
-            mv[w] = sm_m[(kvh + kvh_count * w) * 8 + hh];
-            M = fmaxf(M, mv[w]);
-        }
-        float L = 0.f;
-#pragma unroll
-        for (int w = 0; w < NPAR; ++w) {
-            const float sc = mv[w] == -INFINITY ? 0.f : ex2(mv[w] - M);
-            sc_s[tid * NPAR + w] = sc;
-            L = fmaf(sc, sm_l[(kvh + kvh_count * w) * 8 + hh], L);
-        }
-        const uint64_t state = static_cast<uint64_t>(tid) * splits + split;
-        pm[state] = M == -INFINITY ? -INFINITY : M * kLn2;
-        pl[state] = L;
-    }
-    __syncthreads();
-    constexpr int kUnroll = 4;
-    const uint32_t total = heads * 128;
-    for (uint32_t base = tid; base < total; base += nthreads * kUnroll) {
-        float O[kUnroll];
-        uint32_t idx[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            idx[u] = base + u * nthreads;
-            O[u] = 0.f;
-            if (idx[u] < total) {
-                const uint32_t head = idx[u] >> 7, d = idx[u] & 127;
-                const uint32_t kvh = head / group, hh = head - kvh * group;
-#pragma unroll
-                for (int w = 0; w < NPAR; ++w)
-                    O[u] = fmaf(sc_s[head * NPAR + w], sm_o[((kvh + kvh_count * w) * 8 + hh) * kOStride + d], O[u]);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            if (idx[u] < total) {
-                const uint32_t head = idx[u] >> 7, d = idx[u] & 127;
-                po[(static_cast<uint64_t>(head) * splits + split) * 128 + d] = O[u];
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void combine_tile2_any(uint32_t npar, const float* sm_m, const float* sm_l,
-                                                  const float* sm_o, float* sc_s, uint32_t kvh_count, uint32_t group,
-                                                  uint32_t split, uint32_t splits, float* po, float* pm, float* pl,
-                                                  uint32_t tid, uint32_t nthreads) {
-    switch (npar) {
-        case 1: combine_tile2<1>(sm_m, sm_l, sm_o, sc_s, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-        case 3: combine_tile2<3>(sm_m, sm_l, sm_o, sc_s, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-        case 6: combine_tile2<6>(sm_m, sm_l, sm_o, sc_s, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
-        default: combine_tile2<12>(sm_m, sm_l, sm_o, sc_s, kvh_count, group, split, splits, po, pm, pl, tid, nthreads); break;
     }
 }
 

@@ -6,11 +6,17 @@ Each CUDA translation unit under csrc/ is compiled by nvcc with
 ``-gencode arch=compute_100a,code=sm_100a`` into _build/, then linked with the
 static CUDA runtime into b200attn/libb200attn.so. ptxas resource usage
 (registers, spills, shared memory) is kept in _build/ptxas.log.
+
+Freshness is decided by content, not file times: the SHA-256 of the sources,
+headers, flags and nvcc version is written to libb200attn.so.sha256 after a
+link, and a build whose hash differs (or has none) compiles again. build()
+prints whether it compiled or reused the library.
 """
 from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import hashlib
 import os
 import shutil
 import subprocess
@@ -22,6 +28,8 @@ CSRC = os.path.join(PKG_ROOT, "csrc")
 BUILD = os.path.join(PKG_ROOT, "_build")
 INCLUDE = os.path.join(REPO_ROOT, "include")
 LIB = os.path.join(PKG_ROOT, "b200attn", "libb200attn.so")
+# source hash of the linked library (written after a successful link)
+STAMP = LIB + ".sha256"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", *ARCH, "-Xcompiler", "-fPIC,-O3",
@@ -56,15 +64,45 @@ def _compile(src: str, verbose: bool) -> tuple[str, str]:
     return obj, res.stderr
 
 
+def _nvcc_version() -> str:
+    res = subprocess.run([_nvcc(), "--version"], capture_output=True, text=True)
+    return res.stdout.strip().splitlines()[-1] if res.returncode == 0 and res.stdout else "unknown"
+
+
+def source_hash() -> str:
+    """SHA-256 over every source and header (path and bytes), the compile and
+    link flags, this script and the nvcc version: the identity of a build."""
+    h = hashlib.sha256()
+    for p in sorted(sources() + _headers() + [os.path.abspath(__file__)]):
+        h.update(os.path.relpath(p, REPO_ROOT).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
+    h.update(" ".join(NVCC_FLAGS + ARCH).encode())
+    h.update(_nvcc_version().encode())
+    return h.hexdigest()
+
+
+def built_hash() -> str | None:
+    """The source hash recorded when the library in the tree was linked."""
+    try:
+        with open(STAMP) as f:
+            return f.read().strip() or None
+    except OSError:
+        return None
+
+
 def needs_build() -> bool:
-    if not os.path.exists(LIB):
-        return True
-    t = os.path.getmtime(LIB)
-    return any(os.path.getmtime(p) > t for p in sources() + _headers() + [os.path.abspath(__file__)])
+    return not os.path.exists(LIB) or built_hash() != source_hash()
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, quiet: bool = False) -> str:
+    """Compile and link when the library is missing or its recorded source
+    hash differs from the tree's; otherwise reuse it. Prints which (unless
+    quiet), so a run on another machine shows whether it rebuilt."""
+    want = source_hash()
+    if not force and os.path.exists(LIB) and built_hash() == want:
+        if not quiet:
+            print(f"b200attn build: reused {os.path.relpath(LIB, REPO_ROOT)} (sources {want[:16]})", flush=True)
         return LIB
     os.makedirs(BUILD, exist_ok=True)
     srcs = sources()
@@ -81,6 +119,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, LIB)
+    stamp_tmp = STAMP + f".tmp{os.getpid()}"
+    with open(stamp_tmp, "w") as f:
+        f.write(want + "\n")
+    os.replace(stamp_tmp, STAMP)
+    if not quiet:
+        print(f"b200attn build: compiled {os.path.relpath(LIB, REPO_ROOT)} (sources {want[:16]})", flush=True)
     return LIB
 
 

@@ -18,6 +18,7 @@ Parity pins for this oracle (see tests/test_oracle.py):
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import os
 import subprocess
 import threading
@@ -35,13 +36,29 @@ _lib = None
 CFLAGS = ["-O3", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off", "-std=c11"]
 
 
+def _source_hash() -> str:
+    h = hashlib.sha256()
+    for p in _SRC + [os.path.join(_HERE, "oracle.h")]:
+        with open(p, "rb") as f:
+            h.update(f.read())
+    h.update(" ".join(CFLAGS).encode())
+    return h.hexdigest()
+
+
 def build(force: bool = False) -> str:
-    """Compile oracle.c into liboracle.so next to it (gcc, a second or two)."""
-    newest_src = max(os.path.getmtime(p) for p in _SRC + [os.path.join(_HERE, "oracle.h")])
-    if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < newest_src:
+    """Compile oracle.c into liboracle.so next to it (gcc, a second or two)
+    when the library is missing or was built from other sources or flags
+    (content hash kept in liboracle.so.sha256)."""
+    want = _source_hash()
+    stamp = _SO + ".sha256"
+    have = open(stamp).read().strip() if os.path.exists(stamp) else None
+    if force or not os.path.exists(_SO) or have != want:
         tmp = _SO + f".tmp{os.getpid()}"
         subprocess.check_call(["gcc", *CFLAGS, *_SRC, "-o", tmp, "-lm"])
         os.replace(tmp, _SO)
+        with open(stamp + f".tmp{os.getpid()}", "w") as f:
+            f.write(want + "\n")
+        os.replace(stamp + f".tmp{os.getpid()}", stamp)
     return _SO
 
 

@@ -431,7 +431,10 @@ int b2_launch_decode_step_ragged_fused(const void* d_q, size_t q_seq_stride, con
  *  - The call allocates nothing: no cudaMalloc, no cudaFree, no allocating
  *    library routine. The first call on each device looks up the array's
  *    device address (cudaGetSymbolAddress) with that device current; make
- *    that first call before any stream capture.
+ *    that first call before any stream capture. The address is kept per
+ *    device together with the id of the context it was read in; after a
+ *    context reset (cudaDeviceReset, primary context released) the next
+ *    call looks it up again, so it too belongs outside a capture.
  *  - All calls share the one array, which keeps the last call's contents.
  *    Nothing in it needs to start at zero: each call writes every partial
  *    it reads. Calls whose kernels can overlap on the GPU (different streams

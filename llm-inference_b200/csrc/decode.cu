@@ -46,6 +46,8 @@
 #include <atomic>
 #include <mutex>
 
+#include <cuda.h>
+
 #include "b2_common.cuh"
 #include "b2_ptx.cuh"
 #include "decode_tile.cuh"
@@ -395,8 +397,11 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
         if (lane == 0) red_s[1][warp] = v;
-        (void)mbar_wait(bar, phase);
-        __syncthreads();
+        // every thread must see the bulk copy land before the rows are read;
+        // after a timeout (error word already set) the CTA leaves the loop
+        // together instead of summing rows that never arrived or reusing the
+        // buffer and barrier under a copy that may still be in flight
+        if (!__syncthreads_and(mbar_wait(bar, phase) ? 1 : 0)) return;
         float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) L += red_s[1][w];
@@ -1652,10 +1657,41 @@ namespace b2 {
 namespace {
 
 std::mutex g_noalloc_mutex;
-float* g_noalloc_ptr[64] = {};  // device address of the array, per device
+// device address of the array per device, with the id of the context it was
+// looked up in: a context torn down and recreated (cudaDeviceReset, primary
+// context released) loads the module again, possibly at another address
+float* g_noalloc_ptr[64] = {};
+unsigned long long g_noalloc_ctx[64] = {};
 
-// Resolve the array's device address for the current device (once per device).
-// The name is a host-side stand-in in host code; the kernels need the address.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context (0 when it cannot be read).
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+    if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Resolve the array's device address for the current device, once per device
+// and context. The name is a host-side stand-in in host code; the kernels need
+// the address.
 int noalloc_scratch(float** out) {
     int dev = 0;
     const cudaError_t e = cudaGetDevice(&dev);
@@ -1664,8 +1700,11 @@ int noalloc_scratch(float** out) {
         return B2_ERR_CUDA;
     }
     if (dev < 0 || dev >= 64) return B2_ERR_UNSUPPORTED;
+    // 0 until the runtime has made the device's context current on this
+    // thread; the symbol lookup below does that, and the id is read again
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    if (g_noalloc_ptr[dev] == nullptr || ctx == 0 || g_noalloc_ctx[dev] != ctx) {
         void* p = nullptr;
         const cudaError_t s = cudaGetSymbolAddress(&p, g_b2_noalloc_scratch);
         if (s != cudaSuccess || p == nullptr) {
@@ -1673,6 +1712,7 @@ int noalloc_scratch(float** out) {
             return B2_ERR_CUDA;
         }
         g_noalloc_ptr[dev] = static_cast<float*>(p);
+        g_noalloc_ctx[dev] = ctx != 0 ? ctx : current_context_id();
     }
     *out = g_noalloc_ptr[dev];
     return B2_OK;

@@ -333,49 +333,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
-// 2^x for a pair on the FMA pipe instead of the special-function unit (which
-// is as busy as the tensor core otherwise): x = n + f with n = rint(x) from
-// the 1.5 * 2^23 rounding trick, 2^f on [-1/2, 1/2] by a cubic fitted here
-// for relative error (max 2.2e-4, under fp16's half ulp), and n added to the
-// exponent bits. x is clamped at -125 so the result stays a normal float
-// (2^-125 rounds to 0 in fp16, and -inf gives the same).
-constexpr bool kPolyPacked = true;  // exp2_poly2 on f32x2 pairs
-
-__device__ __forceinline__ float exp2_poly(float x) {
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    x = fmaxf(x, -125.f);
-    const float t = x + kMagic;
-    const float f = x - (t - kMagic);
-    float p = fmaf(0.05286743491888046f, f, 0.2421518862247467f);
-    p = fmaf(p, f, 0.6935867667198181f);
-    p = fmaf(p, f, 0.9999627470970154f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-    if (kPolyPacked) {
-        constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-        x0 = fmaxf(x0, -125.f);
-        x1 = fmaxf(x1, -125.f);
-        float t0, t1, n0, n1, f0, f1, p0, p1;
-        fadd2(t0, t1, x0, x1, kMagic, kMagic);
-        fadd2(n0, n1, t0, t1, -kMagic, -kMagic);
-        fadd2(f0, f1, x0, x1, -n0, -n1);
-        ffma2(p0, p1, f0, f1, 0.05286743491888046f, 0.05286743491888046f, 0.2421518862247467f,
-              0.2421518862247467f);
-        ffma2(p0, p1, p0, p1, f0, f1, 0.6935867667198181f, 0.6935867667198181f);
-        ffma2(p0, p1, p0, p1, f0, f1, 0.9999627470970154f, 0.9999627470970154f);
-        y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-        y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-    } else {
-        y0 = exp2_poly(x0);
-        y1 = exp2_poly(x1);
-    }
-}
-
-// One pair of exponentials in four goes through exp2_poly2 (the special
-// function unit alone is as busy as the tensor core otherwise).
-constexpr bool kPolyExp = false;
-
 // Softmax warpgroup of one head: rows of the 128-query tile, one per thread.
 __device__ __forceinline__ bool pair_softmax(const PrefillArgs& a, PairBars* bars, uint32_t tbase, uint32_t x,
                                              uint32_t h, uint32_t b, uint32_t qt, uint32_t n_kv, uint32_t quarter,
@@ -442,13 +399,7 @@ __device__ __forceinline__ bool pair_softmax(const PrefillArgs& a, PairBars* bar
                 float x0, x1;
                 ffma2(x0, x1, __uint_as_float(sr[64 * c + 2 * i]), __uint_as_float(sr[64 * c + 2 * i + 1]), sc, sc,
                       nm, nm);
-                float p0, p1;
-                if (kPolyExp && (i & 3) == 3) {
-                    exp2_poly2(x0, x1, p0, p1);  // this pair on the FMA pipe
-                } else {
-                    p0 = ex2f(x0);
-                    p1 = ex2f(x1);
-                }
+                const float p0 = ex2f(x0), p1 = ex2f(x1);
                 fadd2(rsum[(i & 3) * 2], rsum[(i & 3) * 2 + 1], rsum[(i & 3) * 2], rsum[(i & 3) * 2 + 1], p0, p1);
                 packed[i] = pack_half2(p0, p1);
             }

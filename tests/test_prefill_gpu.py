@@ -164,3 +164,56 @@ def test_prefill_batched_head_block_into_wider_output(cuda):
     for b in range(B):
         _, o32 = oracle.causal_attention(q[b], k[b], v[b], S, H, KVH, d)
         assert_attention_close(got[b, :, g0 * G * d:], o32[:, g0 * G * d:])
+
+
+@pytest.mark.parametrize("layer", [2, 3])
+def test_prefill_config3_full_batched_launch(cuda, layer):
+    """The bench's config-3 launch as it runs: 4 sequences x 8192 tokens of
+    interleaved [Q|K|V] rows (stride 3072), RoPE/append into a 36-layer cache
+    per sequence (batch stride 36 * 2 * 8192 * 512; layer 2 rotates, layer 3
+    is a NoPE layer, (l + 1) % 4 == 0), then one batched prefill launch over
+    all 4 x 4 (sequence, KV head) units. Sampled rows of every sequence and
+    every head against the FP32 oracle; sequence 0's cache rows bit-exact
+    against the oracle's RoPE/append."""
+    import torch
+    B, S, H, KVH, d, L = 4, 8192, 16, 4, 128, 36
+    QD, KD = H * d, KVH * d
+    QKV = QD + 2 * KD
+    rotate = (layer + 1) % 4 != 0
+    qkv_h = seeded_f16((B, S, QKV), 300 + layer)
+    qkv = dev(qkv_h)
+    cache = torch.zeros((B, L, 2, S, KD), dtype=torch.float16, device=cuda)
+    cos, sin = b200attn.rope_tables_host(S, d, 5.0e6)
+    dcos, dsin = dev(cos), dev(sin)
+    for b in range(B):
+        row = qkv[b]
+        b200attn.launch_rope_and_store_kv(row, row[:, QD:], row[:, QD + KD:], cache[b, layer, 0], cache[b, layer, 1],
+                                          dcos, dsin, S, H, KVH, d, QKV, QKV, 0, rotate)
+    out = torch.full((B, S, QD), float("nan"), dtype=torch.float16, device=cuda)
+    b200attn.launch_causal_attention_prefill_batched(qkv, cache[0, layer, 0], cache[0, layer, 1], out, B, S, H, KVH,
+                                                     d, QKV, KD, S * QKV, L * 2 * S * KD, S * QD)
+    _sync()
+    assert b200attn.lib().b2_device_error_word() == 0
+    got = host(out)
+    assert np.all(np.isfinite(got.astype(np.float32)))
+    # the neighbouring layers of the cache stay untouched
+    assert not bool(cache[:, layer - 1].any()) and not bool(cache[:, layer + 1].any())
+    # sequence 0: RoPE/append bit-exact against the oracle
+    q0 = np.ascontiguousarray(qkv_h[0, :, :QD])
+    k0 = np.ascontiguousarray(qkv_h[0, :, QD:QD + KD])
+    v0 = np.ascontiguousarray(qkv_h[0, :, QD + KD:])
+    kc = np.zeros((S, KD), np.float16)
+    vc = np.zeros((S, KD), np.float16)
+    oracle.rope_and_store_kv(q0, k0, v0, kc, vc, cos, sin, S, H, KVH, d, QD, KD, 0, rotate)
+    np.testing.assert_array_equal(bits(host(cache[0, layer, 0])), bits(kc))
+    np.testing.assert_array_equal(bits(host(cache[0, layer, 1])), bits(vc))
+    # every sequence, every head: sampled rows vs the FP32 oracle on the
+    # device's own rotated Q and cache rows
+    q_rot = host(qkv[:, :, :QD])
+    rng = np.random.default_rng(layer)
+    for b in range(B):
+        rows = sorted(set([0, 127, 128, 8191 - 128, S - 1] + list(rng.integers(0, S, 11))))
+        kb = host(cache[b, layer, 0])
+        vb = host(cache[b, layer, 1])
+        _, o32 = oracle.causal_attention(np.ascontiguousarray(q_rot[b]), kb, vb, S, H, KVH, d, rows=rows)
+        assert_attention_close(got[b][rows], o32)

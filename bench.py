@@ -13,22 +13,38 @@ position 65,536 + step, split-KV flash-decode over kv_len = position + 1
 value : whole-job KV-read throughput in GB/s with the inputs resident in HBM;
         one captured CUDA graph per step (device-resident positions), CUDA
         events on the launching stream, max over ranks.
-e2e   : the same metric through the reference-facing C-ABI calls
-        (launch_rope_and_store_kv + launch_causal_attention_decode_vectorized
-        per layer) with the step's Q/K/V rows copied from pinned host memory
-        and the attention outputs copied back every step.
+e2e   : the same metric through the C ABI with host buffers: every step
+        copies the step's Q/K/V rows and position in from pinned host memory,
+        issues one fused-step call per layer (eager) and copies the attention
+        outputs back; e2e.reference_launchers (one GPU) times the reference
+        engine's own call sequence (launch_rope_and_store_kv +
+        launch_causal_attention_decode_vectorized per layer) the same way.
 Algorithmic bytes per layer-step: K+V read 2*kv_len*512*2 + Q 4 KiB +
 output 4 KiB + appended K/V row 2 KiB (partial-workspace traffic excluded).
 
+Sub-measurements in the same line: `prefill` (config 3: 36 layers of
+RoPE/append + batched causal prefill, TFLOP/s, with its own e2e and CPU
+baseline), `ragged` (config 5, GB/s, e2e and CPU baseline) and, on one GPU,
+`small` (configs 1 and 2, latency-bound single layers: per-call device time
+eager and graphed, e2e, CPU baselines in full). CPU baselines (rank 0, one
+GPU) time the C oracle (the double-precision restatement of
+tests/test_causal_attention.cpp:176-196) and the python/reference.py:62-92
+path on CPU torch (FP16, FP32) with every host thread, on bounded samples.
+
 --impl reference times the reference algorithm's CPU implementation (the
 C oracle restating it, all host threads) on a bounded sample of the same
-workload (one layer-step at the same kv_len per step) and prints the same line.
+workload (one layer-step at the same kv_len per step), with the
+python/reference.py path on the same layer-step reported beside it, and
+prints the same line.
 
 N > 1 (torchrun): the 64K KV range of every layer is split into N contiguous
 ranges, one per rank; the rank holding the tail appends the new token; each
-rank reduces its range to one (o, m, l) partial per head, the partials are
-all-gathered over NCCL and merged on every rank (strong scaling: total work
-fixed).
+rank reduces its range to one (o, m, l) partial per head and the partials are
+merged across ranks -- inside the fused kernel over CUDA-IPC peer memory
+(--exchange peer, default) or by an NCCL all-gather and a merge kernel
+(--exchange nccl). Strong scaling: total work fixed. Prefill shards
+(sequence, KV head) units and the ragged decode shards whole sequences
+(weak in units, no exchange).
 """
 from __future__ import annotations
 
@@ -68,6 +84,10 @@ RG_WORKLOAD = ("config5: ragged decode, 64 sequences, KV lengths numpy default_r
                "(length after the new token's append), per-sequence cache of 16384 rows, N(0,1) FP16, 16/4 heads, "
                "head_dim 128, 36 layers x 1 new token per sequence per step (RoPE / NoPE + append + ragged "
                "split-KV decode + merge)")
+
+
+TRAFFIC_NOTE = ("static ncu figure, not measured in this run: dram__bytes_read.sum + dram__bytes_write.sum of {what} "
+                "({f}), scaled to this launch by its algorithmic bytes")
 
 
 def prefill_flops(batch: int, seq: int, heads: int = 16) -> int:
@@ -157,7 +177,36 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU baseline
-def cpu_decode_sample(kv_len: int, threads: int, rng_seed: int = 7, budget_s: float = 12.0, min_reps: int = 2):
+def cpu_info() -> dict:
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "logical_cpus": os.cpu_count()}
+
+
+def _best(variants: dict, unit: str, threads: int, sample: str, scale_note: str | None = None) -> dict:
+    """cpu_baseline object: the fastest of the timed CPU implementations is the
+    value; every variant is listed beside it."""
+    name = max(variants, key=lambda k: variants[k]["value"])
+    out = {"value": variants[name]["value"], "unit": unit, "cores": threads, "kind": "port", "best": name,
+           "sample": sample, **cpu_info(), "variants": variants}
+    if scale_note:
+        out["extrapolated"] = scale_note
+    return out
+
+
+def _torch_threads(threads: int):
+    import torch
+    torch.set_num_threads(threads)
+
+
+def cpu_decode_sample(kv_len: int, threads: int, rng_seed: int = 7, budget_s: float = 8.0, min_reps: int = 2):
     """Oracle RoPE+append + decode attention for one layer-step at kv_len, repeated
     until budget_s; returns (GB/s, reps, seconds)."""
     import numpy as np
@@ -179,6 +228,111 @@ def cpu_decode_sample(kv_len: int, threads: int, rng_seed: int = 7, budget_s: fl
         if reps >= min_reps and el >= budget_s:
             break
     return layer_bytes(kv_len) * reps / el / 1e9, reps, el
+
+
+def torch_decode_sample(kv_len: int, threads: int, dtype_name: str, budget_s: float = 3.0):
+    """The python/reference.py path for one layer-step at kv_len (HF RoPE of
+    the new token, append, repeat_interleave + SDPA over the cache); GB/s."""
+    import torch
+    from oracle import torch_ref
+    _torch_threads(threads)
+    dt = getattr(torch, dtype_name)
+    kc = torch_ref.seeded((kv_len, KV_DIM), 7, 0.5).to(dt)
+    vc = torch_ref.seeded((kv_len, KV_DIM), 8, 0.5).to(dt)
+    row = torch_ref.seeded(QKV, 9).to(dt)
+    q, kn, vn = row[:Q_DIM], row[Q_DIM:Q_DIM + KV_DIM], row[Q_DIM + KV_DIM:]
+    per, reps = torch_ref.time_calls(lambda: torch_ref.decode(q, kn, vn, kc, vc, kv_len - 1, H, KVH, D), budget_s, 2)
+    return layer_bytes(kv_len) / per / 1e9, reps, per * reps
+
+
+def cpu_config4(threads: int, budget_s: float = 8.0) -> dict:
+    gbs, reps, el = cpu_decode_sample(PAST + 1, threads, budget_s=budget_s)
+    var = {"c_oracle_f64": {"value": round(gbs, 3), "reps": reps, "seconds": round(el, 2)}}
+    for dt in ("float16", "float32"):
+        g, r, e = torch_decode_sample(PAST + 1, threads, dt)
+        var[f"python_reference_{dt}"] = {"value": round(g, 3), "reps": r, "seconds": round(e, 2)}
+    return _best(var, "GB/s", threads, "one layer-step of the 64K decode (RoPE + append + attention at kv_len "
+                 "65537), repeated: the C oracle (test_causal_attention.cpp:176-196 double softmax, OpenMP) and the "
+                 "python/reference.py:62-92 path on CPU torch (HF apply_rotary_pos_emb, repeat_interleave, SDPA) in "
+                 "FP16 and FP32", "per layer-step; a 36-layer step is 36 of these")
+
+
+def cpu_prefill_unit(S: int, heads: int, kv_heads: int, threads: int, row_stride: int = 1, budget_s: float = 1.0):
+    """Causal prefill of S tokens, `heads` query heads over `kv_heads` KV heads
+    (RoPE + attention): TFLOP/s of the C oracle (every row_stride-th query row,
+    scaled to all rows by FLOP count) and of the python/reference.py path."""
+    import numpy as np
+    import torch
+    import oracle
+    from oracle import torch_ref
+    _torch_threads(threads)
+    rng = np.random.default_rng(11)
+    qd, kd = heads * D, kv_heads * D
+    q = rng.standard_normal((S, qd), dtype=np.float32).astype(np.float16)
+    k = rng.standard_normal((S, kd), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((S, kd), dtype=np.float32).astype(np.float16)
+    cos, sin = oracle.rope_tables(S, D, 5.0e6)
+    rows = None if row_stride == 1 else list(range(row_stride - 1, S, row_stride))
+    # FLOPs of the rows computed: 2 * heads * d * (keys per row) * 2
+    row_keys = S * (S + 1) // 2 if rows is None else sum(r + 1 for r in rows)
+    flops_done = 4 * heads * D * row_keys
+    flops_all = prefill_flops(1, S, heads)
+
+    def c_call():
+        qq, kk = q.copy(), k.copy()
+        oracle.rope_and_store_kv(qq, kk, None, None, None, cos, sin, S, heads, kv_heads, D, qd, kd, 0, True)
+        oracle.causal_attention(qq, kk, v, S, heads, kv_heads, D, rows=rows, threads=threads)
+    per, reps = torch_ref.time_calls(c_call, budget_s, warm=0)
+    var = {"c_oracle_f64": {"value": round(flops_done / per / 1e12, 6), "reps": reps, "seconds": round(per * reps, 2),
+                            "rows": "all" if rows is None else f"every {row_stride}th query row"}}
+    tq, tk, tv = torch.from_numpy(q), torch.from_numpy(k), torch.from_numpy(v)
+    for dt in ("float16", "float32"):
+        d_ = getattr(torch, dt)
+        per, reps = torch_ref.time_calls(lambda: torch_ref.prefill(tq, tk, tv, heads, kv_heads, D, dtype=d_),
+                                         budget_s, 2)
+        var[f"python_reference_{dt}"] = {"value": round(flops_all / per / 1e12, 6), "reps": reps,
+                                         "seconds": round(per * reps, 2)}
+    return var
+
+
+def cpu_config5(lens, threads: int) -> dict:
+    """One layer of the ragged decode on CPU (every sequence: RoPE + append +
+    attention at its length); the sequences' caches are windows of one seeded
+    pool of rows (timing only). GB/s of algorithmic bytes."""
+    import numpy as np
+    import torch
+    import oracle
+    from oracle import torch_ref
+    _torch_threads(threads)
+    n = max(lens)
+    rng = np.random.default_rng(13)
+    pool_k = rng.standard_normal((n, KV_DIM), dtype=np.float32).astype(np.float16)
+    pool_v = rng.standard_normal((n, KV_DIM), dtype=np.float32).astype(np.float16)
+    rows = rng.standard_normal((len(lens), QKV), dtype=np.float32).astype(np.float16)
+    cos, sin = oracle.rope_tables(n, D, 5.0e6)
+    nbytes = sum(2 * L_ * KV_DIM * 2 + Q_DIM * 4 + 2 * KV_DIM * 2 for L_ in lens)
+
+    def c_layer():
+        for i, L_ in enumerate(lens):
+            q, kn, vn = rows[i, :Q_DIM].copy(), rows[i, Q_DIM:Q_DIM + KV_DIM].copy(), rows[i, Q_DIM + KV_DIM:].copy()
+            oracle.rope_and_store_kv(q, kn, vn, pool_k, pool_v, cos, sin, 1, H, KVH, D, Q_DIM, KV_DIM, L_ - 1, True)
+            oracle.decode_attention(q, pool_k, pool_v, L_, H, KVH, D, threads=threads)
+    per, reps = torch_ref.time_calls(c_layer, 1.0, warm=0)
+    var = {"c_oracle_f64": {"value": round(nbytes / per / 1e9, 3), "reps": reps, "seconds": round(per * reps, 2)}}
+    for dt in ("float16", "float32"):
+        d_ = getattr(torch, dt)
+        kc, vc, tr = torch.from_numpy(pool_k).to(d_), torch.from_numpy(pool_v).to(d_), torch.from_numpy(rows).to(d_)
+
+        def t_layer():
+            for i, L_ in enumerate(lens):
+                torch_ref.decode(tr[i, :Q_DIM], tr[i, Q_DIM:Q_DIM + KV_DIM], tr[i, Q_DIM + KV_DIM:], kc, vc, L_ - 1,
+                                 H, KVH, D)
+        per, reps = torch_ref.time_calls(t_layer, 1.0)
+        var[f"python_reference_{dt}"] = {"value": round(nbytes / per / 1e9, 3), "reps": reps,
+                                         "seconds": round(per * reps, 2)}
+    return _best(var, "GB/s", threads, f"one layer of the {len(lens)} sequences (RoPE + append + attention at each "
+                 "length): C oracle and the python/reference.py path (FP16, FP32)",
+                 "one layer timed; the 36-layer step is 36 of these (GB/s unchanged)")
 
 
 def run_reference(args, rank, world):
@@ -211,6 +365,11 @@ def run_reference(args, rank, world):
         total += one(s)
     el = time.perf_counter() - t0
     val = total / el / 1e9
+    # the python/reference.py path on the same layer-step, beside the C oracle
+    py = {}
+    for dt in ("float16", "float32"):
+        g, r, e = torch_decode_sample(PAST + 1, threads, dt, budget_s=2.0)
+        py[dt] = {"value": round(g, 3), "unit": "GB/s", "reps": r, "seconds": round(e, 2)}
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
@@ -219,7 +378,12 @@ def run_reference(args, rank, world):
         "config": {"workload": WORKLOAD, "sample": "one layer-step per step (RoPE+append+decode at kv_len "
                    "65537+step) instead of 36 layers", "l2": "n/a (CPU)"},
         "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} layer-steps of the 64K decode, C oracle, {threads} OpenMP threads"},
+                         "sample": f"{args.steps} layer-steps of the 64K decode, C oracle "
+                                   f"(test_causal_attention.cpp:176-196 restated), {threads} OpenMP threads",
+                         **cpu_info()},
+        "python_reference_path": {"what": "python/reference.py:62-92 on CPU torch (HF apply_rotary_pos_emb, "
+                                          "repeat_interleave, SDPA), same layer-step, "
+                                          f"torch.set_num_threads({threads})", **py},
         "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -245,31 +409,31 @@ def run_prefill(args, rank, world, dev):
     stream = torch.cuda.Stream(device=dev)
     G = H // KVH
 
-    def layer(l, t_attn=None):
+    def layer(l, t_attn=None, qkv_=qkv, out_=out, st=stream):
         rotate = (l + 1) % 4 != 0
         for b in seqs:
-            row = qkv[b]
+            row = qkv_[b]
             b200attn.launch_rope_and_store_kv(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[b, l, 0],
                                               cache[b, l, 1], d_cos, d_sin, PF_S, H, KVH, D, QKV, QKV, 0, rotate,
-                                              stream=stream)
+                                              stream=st)
         if t_attn is not None:
-            t_attn[0].record(stream)
+            t_attn[0].record(st)
         if shard is not None:
             # one batched launch over this rank's block of sequences x KV heads
             s0, nb = shard.seq_begin, shard.seq_end - shard.seq_begin
             g0, ng = shard.kvh_begin, shard.kvh_end - shard.kvh_begin
             b200attn.launch_causal_attention_prefill_batched(
-                qkv[s0, :, g0 * G * D:], cache[s0, l, 0, :, g0 * D:], cache[s0, l, 1, :, g0 * D:],
-                out[s0, :, g0 * G * D:], nb, PF_S, ng * G, ng, D, QKV, KV_DIM, PF_S * QKV,
-                LAYERS * 2 * PF_S * KV_DIM, PF_S * Q_DIM, stream=stream, out_stride=Q_DIM)
+                qkv_[s0, :, g0 * G * D:], cache[s0, l, 0, :, g0 * D:], cache[s0, l, 1, :, g0 * D:],
+                out_[s0, :, g0 * G * D:], nb, PF_S, ng * G, ng, D, QKV, KV_DIM, PF_S * QKV,
+                LAYERS * 2 * PF_S * KV_DIM, PF_S * Q_DIM, stream=st, out_stride=Q_DIM)
         else:
             for b, g in units:
                 g0 = g * G
                 b200attn.launch_causal_attention_prefill(
-                    qkv[b, :, g0 * D:], cache[b, l, 0, :, g * D:], cache[b, l, 1, :, g * D:], out[b, :, g0 * D:],
-                    PF_S, H // KVH, 1, D, QKV, KV_DIM, stream=stream)
+                    qkv_[b, :, g0 * D:], cache[b, l, 0, :, g * D:], cache[b, l, 1, :, g * D:], out_[b, :, g0 * D:],
+                    PF_S, H // KVH, 1, D, QKV, KV_DIM, stream=st)
         if t_attn is not None:
-            t_attn[1].record(stream)
+            t_attn[1].record(st)
 
     steps = max(1, min(args.steps, args.prefill_steps))
     with torch.cuda.stream(stream):
@@ -300,6 +464,67 @@ def run_prefill(args, rank, world, dev):
     unit_flops = prefill_flops(1, PF_S, H // KVH) * len(units)     # this rank, one layer
     tf = total_flops / (ms / 1e3) / 1e12
     achieved = unit_flops / (attn_ms / 1e3) / 1e12
+
+    # ---- e2e: the same 36 layers with this rank's [Q|K|V] rows copied in from
+    # pinned host memory before every layer and its outputs copied back after
+    # it, through the C-ABI launchers; copies on their own streams, two device
+    # buffers, so layer l's copies overlap layers l +- 1's compute
+    s0, s1 = seqs[0], seqs[-1] + 1
+    nseq = s1 - s0
+    qkv_host = qkv[s0:s1].cpu().pin_memory()
+    out_host = torch.empty((nseq, PF_S, Q_DIM), dtype=torch.float16).pin_memory()
+    qkv_b = [qkv, torch.empty_like(qkv)]
+    out_b = [out, torch.empty_like(out)]
+    h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_h = [torch.cuda.Event() for _ in range(2)]
+    ev_c = [torch.cuda.Event() for _ in range(2)]
+    ev_d = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_steps(n):
+        i = 0
+        for _ in range(n):
+            for l in range(LAYERS):
+                bf = i & 1
+                if i >= 2:
+                    h2d_s.wait_event(ev_c[bf])          # layer i - 2 is done reading this buffer
+                with torch.cuda.stream(h2d_s):
+                    qkv_b[bf][s0:s1].copy_(qkv_host, non_blocking=True)
+                ev_h[bf].record(h2d_s)
+                stream.wait_event(ev_h[bf])
+                if i >= 2:
+                    stream.wait_event(ev_d[bf])         # its outputs have left the device
+                layer(l, None, qkv_b[bf], out_b[bf], stream)
+                ev_c[bf].record(stream)
+                d2h_s.wait_event(ev_c[bf])
+                with torch.cuda.stream(d2h_s):
+                    out_host.copy_(out_b[bf][s0:s1], non_blocking=True)
+                ev_d[bf].record(d2h_s)
+                i += 1
+        stream.wait_stream(h2d_s)
+        stream.wait_stream(d2h_s)
+
+    e2e_steps(1)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_steps(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        e2e_ms = bdist.max_over_ranks(e2e_ms, dev)
+    e2e = {"value": round(total_flops / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": LAYERS * qkv_host.numel() * 2, "d2h_bytes_per_step": LAYERS * out_host.numel() * 2,
+           "ms_per_step": round(e2e_ms / steps, 3),
+           "path": "per layer: this rank's [Q|K|V] rows H2D from pinned memory (own stream), C-ABI "
+                   "launch_rope_and_store_kv + launch_causal_attention_prefill_batched, outputs D2H (own stream); "
+                   "two device buffers so copies overlap the neighbouring layers' compute"}
+    del qkv_b, out_b
+
     # the attention launches are timed inside a long (power-capped) step: the
     # sustained tensor peak is the denominator, the burst one is reported beside
     peak, burst = 1400.0, 1590.0
@@ -311,6 +536,17 @@ def run_prefill(args, rank, world, dev):
         peak = float(pj.get("bf16_tflops_sustained", pj["bf16_tflops"]))
         burst = float(pj["bf16_tflops"])
         kind = "measured (bf16 sustained, back-to-back GEMMs under the power cap; fp16 runs at the same rate)"
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        var = cpu_prefill_unit(PF_S, H // KVH, 1, threads, row_stride=8)
+        cpu = _best(var, "TFLOP/s", threads,
+                    "one (sequence, KV head) unit of config 3 (8192 tokens, 4 query heads over 1 KV head, RoPE + "
+                    "causal attention): C oracle on every 8th query row (FLOP-scaled) and the python/reference.py "
+                    "path (FP16, FP32) on the whole unit",
+                    "the rate of one unit stands for the 16 units x 36 layers of a step (equal causal work per unit)")
+        cpu["ms_per_step_extrapolated"] = round(prefill_flops(PF_B, PF_S) * LAYERS / (cpu["value"] * 1e12) * 1e3, 1)
     return {"metric": "prefill TFLOP/s", "value": round(tf, 2), "unit": "TFLOP/s", "workload": PF_WORKLOAD,
             "clocks": clocks.summary(),
             "steps": steps, "ms_per_step": round(ms / steps, 3), "gpu_launches": launches,
@@ -321,7 +557,8 @@ def run_prefill(args, rank, world, dev):
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
                          "frac_of_burst": round(achieved / burst, 4),
                          "frac_of_nominal_2250": round(achieved / 2250.0, 4), "avg_launch_ms": round(attn_ms, 4),
-                         "algorithmic_flops_per_launch": unit_flops}}
+                         "algorithmic_flops_per_launch": unit_flops},
+            "e2e": e2e, "cpu_baseline": cpu}
 
 
 # --------------------------------------------------------------------------- ragged decode (config 5)
@@ -402,6 +639,47 @@ def run_ragged(args, rank, world, dev):
     # K+V rows read + Q + output + appended row, every sequence, every layer
     seq_bytes = lambda n: 2 * n * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + 2 * KV_DIM * 2
     total = sum(seq_bytes(n) for n in lens_all) * LAYERS * steps
+
+    # ---- e2e: every step copies this rank's 36 x B new [Q|K|V] rows and the
+    # positions in from pinned host memory, issues the 36 fused ragged calls
+    # through the C ABI (eager) and copies the 36 x B outputs back
+    qkv_host = qkv.cpu().pin_memory()
+    pos_host = pos.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        qkv.copy_(qkv_host, non_blocking=True)
+        pos.copy_(pos_host, non_blocking=True)
+        step(stream)
+        out_host.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        e2e_ms = bdist.max_over_ranks(e2e_ms, dev)
+    e2e = {"value": round(total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": qkv_host.numel() * 2 + pos_host.numel() * 4,
+           "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": round(e2e_ms / steps, 4),
+           "path": "per step: this rank's new rows and positions H2D from pinned memory, 36 eager C-ABI "
+                   + ("launch_rope_and_store_kv_ragged + launch_causal_attention_decode_ragged pairs"
+                      if args.unfused else "b2_launch_decode_step_ragged_fused calls") + ", outputs D2H"}
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        cpu = cpu_config5(lens_all, os.cpu_count() or 1)
     mine_layer = sum(seq_bytes(n) for n in lens)
     peak, peak_kind = load_peaks()
     launch_ms = ms / steps / LAYERS
@@ -424,8 +702,165 @@ def run_ragged(args, rank, world, dev):
                                     "merge_ragged_kernel"),
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                         "traffic_source": TRAFFIC_NOTE.format(f="profiles/ragged_traffic.json",
+                                                               what="one config-5 launch"),
                          "avg_layer_us": round(launch_ms * 1e3, 3), "algorithmic_bytes_per_layer": mine_layer,
-                         "timing": "timed region (graph replays) / 36 layers per step"}}
+                         "timing": "timed region (graph replays) / 36 layers per step"},
+            "e2e": e2e, "cpu_baseline": cpu}
+
+
+# --------------------------------------------------------------------------- configs 1 and 2 (latency-bound)
+C1_S = 254          # config 1: one prefill layer of the benchmark prompt length
+C2_PAST = 4096      # config 2: one decode layer, new token at position 4096
+C1_WORKLOAD = ("config1: one causal GQA prefill layer, batch 1, 254 tokens, 16/4 heads, head_dim 128, N(0,1) FP16, "
+               "RoPE theta 5e6 (launch_rope_and_store_kv + launch_causal_attention_prefill)")
+C2_WORKLOAD = ("config2: one decode layer, batch 1, KV cache 4096 tokens N(0,1) FP16, new token RoPE'd at 4096 and "
+               "appended (kv_len 4097), 16/4 heads, head_dim 128, KV_CHUNK 256 partials + merge")
+
+
+def _per_call_ms(fn, calls: int, stream, graph: bool):
+    """Device time per call of fn(i) over `calls` back-to-back calls, CUDA
+    events on `stream`: eager launches, or one captured graph of all calls."""
+    import torch
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(calls):
+                fn(i, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        g.reset()
+        return e0.elapsed_time(e1) / calls
+    with torch.cuda.stream(stream):
+        for i in range(calls):
+            fn(i, stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(calls):
+            fn(i, stream)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / calls
+
+
+def run_small(args, dev):
+    """Configs 1 and 2 on one GPU: per-call device time of the reference
+    launch sequence (and of the fused decode step) cycling through enough
+    copies of the inputs to exceed L2, eager and as one captured graph; e2e
+    through the C ABI with host buffers; CPU baselines in full."""
+    import numpy as np
+    import torch
+    import b200attn
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev).manual_seed(SEED + 300)
+    res = {}
+
+    # ---- config 1: RoPE/append + prefill of 254 tokens, 96 input copies (200 MB)
+    n1 = 96
+    qkv = torch.empty((n1, C1_S, QKV), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    cache = torch.zeros((n1, 2, C1_S, KV_DIM), dtype=torch.float16, device=dev)
+    out = torch.empty((n1, C1_S, Q_DIM), dtype=torch.float16, device=dev)
+    cos, sin = b200attn.rope_tables_host(C2_PAST + 8, D, 5.0e6)
+    d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+
+    def c1(i, st):
+        row = qkv[i]
+        b200attn.launch_rope_and_store_kv(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[i, 0], cache[i, 1],
+                                          d_cos, d_sin, C1_S, H, KVH, D, QKV, QKV, 0, True, stream=st)
+        b200attn.launch_causal_attention_prefill(row, cache[i, 0], cache[i, 1], out[i], C1_S, H, KVH, D, QKV, KV_DIM,
+                                                 stream=st)
+    fl = prefill_flops(1, C1_S)
+    eager = _per_call_ms(c1, n1, stream, False)
+    graphed = _per_call_ms(c1, n1, stream, True)
+    # e2e: each call copies its [Q|K|V] rows in from pinned memory and its output back
+    h_in = qkv[0].cpu().pin_memory()
+    h_out = torch.empty((C1_S, Q_DIM), dtype=torch.float16).pin_memory()
+
+    def c1_e2e(i, st):
+        qkv[i].copy_(h_in, non_blocking=True)
+        c1(i, st)
+        h_out.copy_(out[i], non_blocking=True)
+    e2e = _per_call_ms(c1_e2e, n1, stream, False)
+    res["config1"] = {
+        "workload": C1_WORKLOAD, "unit": "TFLOP/s", "algorithmic_flops_per_call": fl,
+        "eager": {"us_per_call": round(eager * 1e3, 2), "value": round(fl / (eager / 1e3) / 1e12, 2)},
+        "graph": {"us_per_call": round(graphed * 1e3, 2), "value": round(fl / (graphed / 1e3) / 1e12, 2)},
+        "e2e": {"value": round(fl / (e2e / 1e3) / 1e12, 2), "unit": "TFLOP/s", "us_per_call": round(e2e * 1e3, 2),
+                "h2d_bytes_per_step": h_in.numel() * 2, "d2h_bytes_per_step": h_out.numel() * 2},
+        "timing": f"CUDA events around {n1} back-to-back calls cycling through {n1} input copies (> L2)",
+        "gpu_launches_per_call": 2}
+    del qkv, cache, out
+
+    # ---- config 2: one decode layer at kv_len 4097, 24 caches (200 MB)
+    n2 = 24
+    rows = C2_PAST + 8
+    kc = torch.empty((n2, 2, rows, KV_DIM), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    new = torch.empty((n2, QKV), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    o2 = torch.empty((n2, Q_DIM), dtype=torch.float16, device=dev)
+    pos = torch.tensor([C2_PAST], dtype=torch.int32, device=dev)
+    sws_bytes = b200attn.decode_step_workspace_bytes(H, KVH)
+    sws = torch.zeros(sws_bytes, dtype=torch.uint8, device=dev)
+    nfl = b200attn.decode_workspace_floats(H, D, rows)
+    ws = torch.empty(nfl, dtype=torch.float32, device=dev)
+    ch = (rows + 255) // 256
+    po, pm, pl = ws[:H * ch * D], ws[H * ch * D:H * ch * (D + 1)], ws[H * ch * (D + 1):]
+
+    def c2_ref(i, st):
+        row = new[i]
+        b200attn.launch_rope_and_store_kv(row, row[Q_DIM:], row[Q_DIM + KV_DIM:], kc[i, 0], kc[i, 1], d_cos, d_sin,
+                                          1, H, KVH, D, QKV, QKV, C2_PAST, True, stream=st)
+        b200attn.launch_causal_attention_decode_vectorized(row, kc[i, 0], kc[i, 1], o2[i], po, pm, pl, 1, C2_PAST + 1,
+                                                           C2_PAST, H, KVH, D, QKV, KV_DIM, stream=st)
+
+    def c2_fused(i, st):
+        row = new[i]
+        b200attn.launch_decode_step_fused(row, row[Q_DIM:], row[Q_DIM + KV_DIM:], kc[i, 0], kc[i, 1], d_cos, d_sin,
+                                          rows, True, pos, pos, 1, rows, o2[i], sws, sws_bytes, H, KVH, D, stream=st)
+    nb = layer_bytes(C2_PAST + 1)
+    t = {name: {"eager": _per_call_ms(fn, n2, stream, False), "graph": _per_call_ms(fn, n2, stream, True)}
+         for name, fn in (("reference_launchers", c2_ref), ("fused_step", c2_fused))}
+    h_row = new[0].cpu().pin_memory()
+    h_o = torch.empty(Q_DIM, dtype=torch.float16).pin_memory()
+
+    def c2_e2e(i, st):
+        new[i].copy_(h_row, non_blocking=True)
+        c2_fused(i, st)
+        h_o.copy_(o2[i], non_blocking=True)
+    e2e2 = _per_call_ms(c2_e2e, n2, stream, False)
+    res["config2"] = {
+        "workload": C2_WORKLOAD, "unit": "GB/s", "algorithmic_bytes_per_call": nb,
+        **{name: {mode: {"us_per_call": round(v * 1e3, 2), "value": round(nb / (v / 1e3) / 1e9, 1)}
+                  for mode, v in d_.items()} for name, d_ in t.items()},
+        "e2e": {"value": round(nb / (e2e2 / 1e3) / 1e9, 1), "unit": "GB/s", "us_per_call": round(e2e2 * 1e3, 2),
+                "h2d_bytes_per_step": h_row.numel() * 2, "d2h_bytes_per_step": h_o.numel() * 2,
+                "path": "new [Q|K|V] row H2D, b2_launch_decode_step_fused, output D2H"},
+        "timing": f"CUDA events around {n2} back-to-back calls cycling through {n2} caches (> L2)",
+        "gpu_launches_per_call": {"reference_launchers": 3, "fused_step": 1}}
+    del kc, new, ws, sws
+    torch.cuda.empty_cache()
+
+    if not args.no_cpu:
+        threads = os.cpu_count() or 1
+        var = cpu_prefill_unit(C1_S, H, KVH, threads)
+        res["config1"]["cpu_baseline"] = _best(var, "TFLOP/s", threads, "config 1 in full (RoPE + causal attention "
+                                               "of 254 tokens): C oracle and the python/reference.py path (FP16, "
+                                               "FP32)")
+        g, r, e = cpu_decode_sample(C2_PAST + 1, threads, budget_s=1.0)
+        var2 = {"c_oracle_f64": {"value": round(g, 3), "reps": r, "seconds": round(e, 2)}}
+        for dt in ("float16", "float32"):
+            g, r, e = torch_decode_sample(C2_PAST + 1, threads, dt, budget_s=1.0)
+            var2[f"python_reference_{dt}"] = {"value": round(g, 3), "reps": r, "seconds": round(e, 2)}
+        res["config2"]["cpu_baseline"] = _best(var2, "GB/s", threads, "config 2 in full (RoPE + append + decode at "
+                                               "kv_len 4097): C oracle and the python/reference.py path (FP16, FP32)")
+    return res
 
 
 # --------------------------------------------------------------------------- GPU arm
@@ -536,11 +971,13 @@ def run_b200(args, rank, world):
         traffic = int(round(dec_bytes * t["bytes_per_launch"] / t["algorithmic_bytes"]))
 
     # ---- e2e: reference-facing C-ABI calls, host buffers in and out every step
-    e2e = None
-    if world == 1:
+    if world == 1 and args.unfused:
         e2e = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup, args.steps,
-                               stream, step_state, mode="reference" if args.unfused else "fused")
-        if not args.unfused:
+                               stream, step_state, mode="reference")
+    else:
+        e2e = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup, args.steps,
+                               stream, step_state, mode="fused", group=group)
+        if world == 1:
             ref_calls = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup,
                                          args.steps, stream, step_state, mode="reference")
             e2e["reference_launchers"] = {"value": ref_calls["value"], "ms_per_step": ref_calls["ms_per_step"],
@@ -549,15 +986,15 @@ def run_b200(args, rank, world):
     # ---- CPU baseline (rank 0, N=1): bounded sample
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
-        threads = os.cpu_count() or 1
-        gbs, reps, el = cpu_decode_sample(PAST + 1, threads)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{reps} layer-steps of the 64K decode (RoPE+append+attention) in {el:.1f} s, "
-                         f"C oracle, {threads} OpenMP threads"}
+        cpu = cpu_config4(os.cpu_count() or 1)
 
     prefill = None
     del cache
     torch.cuda.empty_cache()
+    small = None
+    if world == 1 and not args.no_small:
+        small = run_small(args, dev)
+        torch.cuda.empty_cache()
     if not args.no_prefill:
         prefill = run_prefill(args, rank, world, dev)
         torch.cuda.empty_cache()
@@ -584,7 +1021,10 @@ def run_b200(args, rank, world):
                                     if step_state.fused else "decode_tma_kernel + merge_partials_kernel"),
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "avg_launch_us": round(launch_ms * 1e3, 3),
+                         "traffic": traffic,
+                         "traffic_source": TRAFFIC_NOTE.format(f="profiles/decode_traffic.json",
+                                                               what="one 64K fused launch"),
+                         "avg_launch_us": round(launch_ms * 1e3, 3),
                          "isolated_launch_us": round(dec_ms * 1e3, 3), "timing": timing,
                          "algorithmic_bytes_per_launch": dec_bytes},
             "clocks": clocks.summary(),
@@ -592,6 +1032,7 @@ def run_b200(args, rank, world):
             "cpu_baseline": cpu,
             "prefill": prefill,
             "ragged": ragged,
+            "small": small,
         }
         print(json.dumps(line), flush=True)
     graph.reset()
@@ -607,6 +1048,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sub-measurement")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-5 ragged decode sub-measurement")
+    ap.add_argument("--no-small", action="store_true", help="skip the config-1/2 (latency-bound) sub-measurement")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
                          "all-gather of the rank partials and a merge kernel")

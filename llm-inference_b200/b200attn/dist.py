@@ -180,9 +180,10 @@ class DecodeStepState:
         return self.local_const, 0
 
 
-def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stream, group=None):
+def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stream, group=None, advance=True):
     """One token through every layer: RoPE + append (tail rank), decode over the
-    local KV range, exchange + merge across ranks, then advance the position."""
+    local KV range, exchange + merge across ranks, then advance the position
+    (unless advance is False: the caller writes st.pos before each step)."""
     import torch
     from . import kernels as K
     H, KVH, D = st.H, st.KVH, st.D
@@ -236,7 +237,8 @@ def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stre
                                                 src, bias, st.capacity, H, KVH, D, kv_dim, part[:H * D],
                                                 part[H * D:H * D + H], part[H * D + H:], stream=stream)
             _exchange_and_merge(st, l, part, out, group, stream)
-    K.advance_position(st.pos, 1, stream=stream)
+    if advance:
+        K.advance_position(st.pos, 1, stream=stream)
 
 
 def _exchange_and_merge(st: DecodeStepState, l, part, out, group, stream):
@@ -311,14 +313,17 @@ def time_decode_launches(st: DecodeStepState, cache, qkv, out, stream, reps=3, d
 
 
 def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, steps, stream, st,
-               mode="fused") -> dict:
+               mode="fused", group=None) -> dict:
     """The decode metric end to end through the C ABI with host buffers: every
     step copies its Q/K/V rows (and position) in from pinned host memory, runs
     36 layers, and copies the attention outputs back.
-    mode "fused": one b2_launch_decode_step_fused call per layer (the position
-    travels with the step's inputs); mode "reference": the reference engine's
-    calls, launch_rope_and_store_kv + launch_causal_attention_decode_vectorized
-    per layer with a host start_pos."""
+    mode "fused": one fused-step call per layer, eager (b2_launch_decode_step_fused
+    on one GPU; on N GPUs the rank's fused call with the cross-rank exchange,
+    peer or NCCL as st.exchange says); the position travels with the step's
+    inputs. mode "reference" (one GPU): the reference engine's calls,
+    launch_rope_and_store_kv + launch_causal_attention_decode_vectorized per
+    layer with a host start_pos. Returns this rank's device time; the caller
+    takes the max over ranks."""
     import torch
     from . import kernels as K
     H, KVH, D, L = st.H, st.KVH, st.D, st.L
@@ -328,19 +333,13 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
     # host write into a word an earlier queued copy still reads would race)
     n_pos = max(warmup, steps)
     pos_host = torch.arange(past, past + n_pos, dtype=torch.int32).pin_memory()
-    pos_dev = torch.zeros(1, dtype=torch.int32, device=qkv.device)
 
     def step(s):
         pos = past + s
         qkv.copy_(qkv_host, non_blocking=True)
         if mode == "fused":
-            pos_dev.copy_(pos_host[s:s + 1], non_blocking=True)
-            for l in range(L):
-                row = qkv[l]
-                K.launch_decode_step_fused(row, row[q_dim:], row[q_dim + kv_dim:], cache.get_k_cache(l),
-                                           cache.get_v_cache(l), d_cos, d_sin, st.max_global, (l + 1) % 4 != 0,
-                                           pos_dev, pos_dev, 1, st.capacity, out[l], st.step_ws, st.step_ws_bytes,
-                                           H, KVH, D, stream=stream)
+            st.pos.copy_(pos_host[s:s + 1], non_blocking=True)
+            enqueue_decode_step(st, cache, qkv, out, d_cos, d_sin, stream, group, advance=False)
         else:
             for l in range(L):
                 row = qkv[l]
@@ -356,6 +355,10 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         for s in range(warmup):
             step(s)
         torch.cuda.synchronize()
+        if st.plan.world > 1:
+            import torch.distributed as tdist
+            tdist.barrier()
+            torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for s in range(steps):
@@ -363,9 +366,16 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    if st.plan.world > 1:
+        ms = max_over_ranks(ms, qkv.device)
+    # whole-job bytes: every layer's full KV range (all ranks' shares)
     nbytes = sum(L * (2 * (past + 1 + s) * kv_dim * 2 + q_dim * 2 * 2 + 2 * kv_dim * 2) for s in range(steps))
     h2d = int(qkv_host.numel() * 2) + (4 if mode == "fused" else 0)
-    path = ("C-ABI b2_launch_decode_step_fused per layer (eager launches, device position copied in with the "
+    fused_call = ("b2_launch_decode_step_fused" if st.plan.world == 1 else
+                  "b2_launch_decode_step_fused_exchange (cross-rank merge over peer memory)"
+                  if st.exchange == "peer" else
+                  "b2_launch_decode_step_fused_rank_partial + NCCL all-gather + b2_launch_merge_partials_strided")
+    path = (f"C-ABI {fused_call} per layer (eager launches, device position copied in with the "
             "step's rows), pinned H2D/D2H each step" if mode == "fused" else
             "C-ABI launch_rope_and_store_kv + launch_causal_attention_decode_vectorized per layer (the reference "
             "engine's calls), host start_pos, pinned H2D/D2H each step")

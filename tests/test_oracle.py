@@ -209,3 +209,42 @@ def test_oracle_prefill_start_pos_and_rows():
     _, part32 = oracle.causal_attention(q[5:], k, v, S, H, KVH, d, start_pos=5, rows=rows)
     np.testing.assert_allclose(part32, full32[[r + 5 for r in rows]], rtol=0, atol=1e-6)
     assert rel_l2(full16, full32) < 1e-3
+
+
+def test_torch_reference_path_matches_golden():
+    """The CPU-baseline restatement of python/reference.py:62-92 (HF RoPE,
+    repeat_interleave, causal SDPA) reproduces the fixtures the reference's
+    own generator wrote, in FP16 as the reference runs it and in FP32."""
+    torch = pytest.importorskip("torch")
+    pytest.importorskip("transformers")
+    from oracle import torch_ref
+    meta, g = golden()
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    q, k, v = (torch.from_numpy(g[n].copy()) for n in ("q", "k", "v"))
+    # FP16 as the fixtures were made: within 2e-3; FP32 differs from the FP16
+    # fixtures by their own rounding (values up to ~3, fp16 step 2e-3): 1e-2
+    for dt, tol in ((torch.float16, 2e-3), (torch.float32, 1e-2)):
+        out = torch_ref.prefill(q, k, v, H, KVH, d, meta["rope_theta"], dtype=dt).float().numpy()
+        assert tensor_close_mismatches(out, g["attn"], 2e-2, 2e-2) == 0
+        assert max_abs(out, g["attn"]) <= tol
+
+
+def test_torch_reference_decode_matches_oracle():
+    """Its one-token form (append + attention over every cached row) against
+    the C oracle's double-precision decode."""
+    torch = pytest.importorskip("torch")
+    pytest.importorskip("transformers")
+    from oracle import torch_ref
+    H, KVH, d, past = 16, 4, 128, 300
+    total = H * d + 2 * KVH * d
+    cache_k = seeded_f16((past + 1, KVH * d), 41, std=0.5)
+    cache_v = seeded_f16((past + 1, KVH * d), 42, std=0.5)
+    new = seeded_f16(total, 43)
+    q, kn, vn = new[:H * d].copy(), new[H * d:H * d + KVH * d].copy(), new[H * d + KVH * d:].copy()
+    kc, vc = torch.from_numpy(cache_k.astype(np.float32)), torch.from_numpy(cache_v.astype(np.float32))
+    got = torch_ref.decode(torch.from_numpy(q), torch.from_numpy(kn), torch.from_numpy(vn), kc, vc, past, H, KVH, d)
+    cos, sin = oracle.rope_tables(past + 1, d, 5.0e6)
+    ck, cv = cache_k.copy(), cache_v.copy()
+    oracle.rope_and_store_kv(q, kn, vn, ck, cv, cos, sin, 1, H, KVH, d, H * d, KVH * d, past, True)
+    _, o32 = oracle.decode_attention(q, ck, cv, past + 1, H, KVH, d)
+    assert_attention_close(got.numpy(), o32.reshape(-1))

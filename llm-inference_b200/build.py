@@ -77,7 +77,9 @@ def source_hash() -> str:
         h.update(os.path.relpath(p, REPO_ROOT).encode())
         with open(p, "rb") as f:
             h.update(f.read())
-    h.update(" ".join(NVCC_FLAGS + ARCH).encode())
+    # flags with this checkout's paths made relative, so the same tree hashes
+    # the same on every machine it is copied to
+    h.update(" ".join(f.replace(REPO_ROOT, ".") for f in NVCC_FLAGS + ARCH).encode())
     h.update(_nvcc_version().encode())
     return h.hexdigest()
 

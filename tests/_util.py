@@ -23,12 +23,15 @@ def load_build_module():
     return mod
 
 
-def golden():
-    meta = json.load(open(os.path.join(GOLDEN, "meta.json")))
+def golden(subset: str = ""):
+    """The committed fixtures: the 40-token set, or subset "sharp" (160 tokens,
+    peaked softmax)."""
+    base = os.path.join(GOLDEN, subset) if subset else GOLDEN
+    meta = json.load(open(os.path.join(base, "meta.json")))
     S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
 
     def ld(name, cols):
-        return np.fromfile(os.path.join(GOLDEN, name + ".bin"), dtype=np.float16).reshape(S, cols)
+        return np.fromfile(os.path.join(base, name + ".bin"), dtype=np.float16).reshape(S, cols)
 
     return meta, {
         "q": ld("layer0_q_proj_out", H * d), "k": ld("layer0_k_proj_out", KVH * d),

@@ -18,6 +18,17 @@ it. ``meta.json`` records the geometry, seed and library versions.
 It needs the reference checkout (set REFERENCE_ROOT to the directory that
 holds python/reference.py) and runs on CPU only. Nothing on a GPU box runs
 it; the tests read only the committed outputs.
+
+Two sets are committed:
+
+    REFERENCE_ROOT=... python tests/golden/make_golden.py
+        40 tokens, seed 1234, initializer_range 0.04 (this directory);
+    REFERENCE_ROOT=... python tests/golden/make_golden.py --seq-len 160 \
+        --seed 4321 --init-range 0.08 --out tests/golden/sharp
+        160 tokens (across the 128-token tile edge), larger weights: the
+        attention logits have a standard deviation of about 13 instead of
+        about 3, so the softmax is peaked and the fixture pins its max and
+        normalisation, not only RoPE and the layout.
 """
 from __future__ import annotations
 
@@ -39,7 +50,7 @@ class _TokenizerStub:
         return " ".join(str(i) for i in ids)
 
 
-def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None) -> None:
+def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None, init_range: float = 0.04) -> None:
     if "REFERENCE_ROOT" not in os.environ:
         raise SystemExit("set REFERENCE_ROOT to the reference checkout (the directory holding python/reference.py)")
     ref_root = Path(os.environ["REFERENCE_ROOT"])
@@ -54,7 +65,7 @@ def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None) -> Non
     config = SmolLM3Config(
         vocab_size=1024, hidden_size=2048, intermediate_size=512,
         num_hidden_layers=1, num_attention_heads=16, num_key_value_heads=4,
-        max_position_embeddings=4096, initializer_range=0.04,
+        max_position_embeddings=4096, initializer_range=init_range,
         rope_parameters={"rope_type": "default", "rope_theta": 5.0e6},
         tie_word_embeddings=True, pad_token_id=0, bos_token_id=1, eos_token_id=2,
     )
@@ -67,13 +78,14 @@ def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None) -> Non
     input_ids = torch.randint(0, config.vocab_size, (1, seq_len), generator=gen)
 
     out = Path(out_dir) if out_dir else Path(__file__).resolve().parent
+    out.mkdir(parents=True, exist_ok=True)
     with tempfile.TemporaryDirectory() as tmp:
         reference.save_activations(model, _TokenizerStub(), Path(tmp), seq_len, input_ids)
         for name in KEEP:
             shutil.copyfile(Path(tmp) / f"{name}.bin", out / f"{name}.bin")
     meta = {
         "generator": "python/reference.py save_activations (reference checkout, unmodified)",
-        "model": "SmolLM3ForCausalLM, random init (initializer_range 0.04), 1 layer, fp16, CPU",
+        "model": f"SmolLM3ForCausalLM, random init (initializer_range {init_range}), 1 layer, fp16, CPU",
         "seq_len": seq_len, "num_heads": 16, "num_kv_heads": 4, "head_dim": 128,
         "rope_theta": 5.0e6, "seed": seed,
         "torch": torch.__version__, "transformers": transformers.__version__,
@@ -86,4 +98,11 @@ def main(seq_len: int = 40, seed: int = 1234, out_dir: str | None = None) -> Non
 
 
 if __name__ == "__main__":
-    main()
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--seq-len", type=int, default=40)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--init-range", type=float, default=0.04)
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args()
+    main(args.seq_len, args.seed, args.out, args.init_range)

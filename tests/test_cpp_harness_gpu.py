@@ -55,10 +55,11 @@ def test_harness_known_answer_sweep(cuda):
 @pytest.mark.gpu
 def test_harness_golden_fixture_tests(cuda):
     exe = build_harness()
-    res = subprocess.run([exe, "golden", os.path.join(ROOT, "tests", "golden")], capture_output=True, text=True,
-                         timeout=600)
-    assert res.returncode == 0, res.stdout + res.stderr
-    assert "0 failures" in res.stdout
+    for sub in ("", "sharp"):
+        res = subprocess.run([exe, "golden", os.path.join(ROOT, "tests", "golden", sub)], capture_output=True,
+                             text=True, timeout=600)
+        assert res.returncode == 0, res.stdout + res.stderr
+        assert "0 failures" in res.stdout
 
 
 @pytest.mark.gpu

@@ -61,11 +61,13 @@ def test_flash_decode_known_answer(cuda, entry, head_dim, kv_heads, padded):
         assert tensor_close_mismatches(got, exp, 2e-3, 2e-3) == 0, (length,)
 
 
+@pytest.mark.parametrize("subset", ["", "sharp"])
 @pytest.mark.parametrize("interleaved", [False, True])
-def test_decode_matches_golden_prefill_rows(cuda, interleaved):
+def test_decode_matches_golden_prefill_rows(cuda, interleaved, subset):
     """tests/test_causal_attention.cpp:80-150: decode at kv_len p+1 == prefill row p;
-    future cache rows hold 123, output guards -123."""
-    meta, g = golden()
+    future cache rows hold 123, output guards -123. Both fixture sets (the
+    160-token one has a peaked softmax)."""
+    meta, g = golden(subset)
     S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
     q_dim, kv_dim = H * d, KVH * d
     cache_k = np.full((S + 2, kv_dim), 123.0, np.float16)

@@ -248,3 +248,30 @@ def test_torch_reference_decode_matches_oracle():
     oracle.rope_and_store_kv(q, kn, vn, ck, cv, cos, sin, 1, H, KVH, d, H * d, KVH * d, past, True)
     _, o32 = oracle.decode_attention(q, ck, cv, past + 1, H, KVH, d)
     assert_attention_close(got.numpy(), o32.reshape(-1))
+
+
+def test_oracle_matches_sharp_golden():
+    """The 160-token fixture with a peaked softmax (logit std ~13): RoPE within
+    one fp16 step of the reference's FP16 path, attention within the
+    reference tolerance and the BASELINE bar."""
+    meta, g = golden("sharp")
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    cos, sin = oracle.rope_tables(4096, d, meta["rope_theta"])
+    q, k = g["q"].copy(), g["k"].copy()
+    assert oracle.rope_and_store_kv(q, k, None, None, None, cos, sin, S, H, KVH, d, H * d, KVH * d, 0, True) == 0
+    assert tensor_close_mismatches(q, g["q_rope"], 2e-2, 2e-2) == 0
+    assert tensor_close_mismatches(k, g["k_rope"], 2e-2, 2e-2) == 0
+    o16, o32 = oracle.causal_attention(g["q_rope"], g["k_rope"], g["v"], S, H, KVH, d)
+    assert tensor_close_mismatches(o16, g["attn"], 2e-2, 2e-2) == 0
+    assert_attention_close(g["attn"], o32)
+
+
+def test_torch_reference_path_matches_sharp_golden():
+    torch = pytest.importorskip("torch")
+    pytest.importorskip("transformers")
+    from oracle import torch_ref
+    meta, g = golden("sharp")
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    q, k, v = (torch.from_numpy(g[n].copy()) for n in ("q", "k", "v"))
+    out = torch_ref.prefill(q, k, v, H, KVH, d, meta["rope_theta"], dtype=torch.float16).float().numpy()
+    assert tensor_close_mismatches(out, g["attn"], 2e-2, 2e-2) == 0

@@ -47,6 +47,25 @@ def test_prefill_matches_golden_from_cache(cuda):
     assert_attention_close(got, o32)
 
 
+def test_prefill_matches_sharp_golden_from_cache(cuda):
+    """The 160-token fixture (peaked softmax, two query tiles) from a cache with
+    populated spare rows, against the fixture and the FP32 oracle."""
+    meta, g = golden("sharp")
+    S, H, KVH, d = meta["seq_len"], meta["num_heads"], meta["num_kv_heads"], meta["head_dim"]
+    cache = b200attn.KVCache(1, S + 2, KVH, d, device=cuda)
+    cache.buffer.fill_(123.0)
+    cache.get_k_cache(0)[:S] = dev(g["k_rope"])
+    cache.get_v_cache(0)[:S] = dev(g["v"])
+    out = dev(np.zeros((S, H * d), np.float16))
+    b200attn.launch_causal_attention_prefill(dev(g["q_rope"]), cache.get_k_cache(0), cache.get_v_cache(0), out, S, H,
+                                             KVH, d, H * d, KVH * d)
+    _sync()
+    got = host(out)
+    assert tensor_close_mismatches(got, g["attn"], 2e-2, 2e-2) == 0
+    _, o32 = oracle.causal_attention(g["q_rope"], g["k_rope"], g["v"], S, H, KVH, d)
+    assert_attention_close(got, o32)
+
+
 def test_prefill_on_interleaved_qkv_rows(cuda):
     """tests/test_qkv_gemm.cpp:87-117: RoPE then prefill straight on [Q|K|V] rows, stride 3072."""
     meta, g = golden()

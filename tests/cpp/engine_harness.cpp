@@ -25,6 +25,12 @@
 //       layer-0 fixtures: prefill from a cache with populated spare rows, and
 //       decode at every position (packed and interleaved Q) against the
 //       fixture's prefill rows, with output guards, tolerance 2e-2.
+//   weights <weights.bin> <chunk_bytes>
+//       include/b200attn/weights.hpp on a file the reference's exporter
+//       wrote: header, tokenizer JSON, pipelined upload (small chunks to run
+//       the two staging buffers many times), then every carved tensor copied
+//       back; prints one JSON line per tensor (name, elements, float64 sum
+//       and sum of squares, first values) for the pytest driver to check.
 //
 // Exit status 0 when every check passed; failures are printed.
 #include <cuda_fp16.h>
@@ -44,6 +50,7 @@
 
 #include "b200attn/kv_cache.hpp"
 #include "b200attn/rope_cache.hpp"
+#include "b200attn/weights.hpp"
 #include "kernels/kernels.hpp"
 
 using b200attn::KVCache;
@@ -382,6 +389,55 @@ int run_golden(const std::string& dir) {
     return g_failures == 0 ? 0 : 1;
 }
 
+// ----------------------------------------------------------------- weights
+int run_weights(const std::string& path, size_t chunk) {
+    b200attn::LoadedModel m = b200attn::load_weights_file(path, nullptr, chunk);
+    const auto& c = m.config;
+    std::fputs(std::format("{{\"header\": [{}, {}, {}, {}, {}, {}, {}, {}, {}, {}], \"tokenizer_bytes\": {}}}\n",
+                           c.vocab_size, c.hidden_size, c.num_layers, c.num_heads, c.num_kv_heads, c.head_dim,
+                           c.intermediate_size, c.max_seq_len, c.rms_norm_eps, c.rope_theta,
+                           m.tokenizer_json.size())
+                   .c_str(),
+               stdout);
+    std::fputs(("tokenizer " + m.tokenizer_json + "\n").c_str(), stdout);
+    const size_t h = c.hidden_size, q = size_t(c.num_heads) * c.head_dim, kv = size_t(c.num_kv_heads) * c.head_dim,
+                 inter = c.intermediate_size;
+    auto report = [](const std::string& name, const __half* dptr, size_t n) {
+        std::vector<__half> hbuf(n);
+        B2_CUDA_CHECK(cudaMemcpy(hbuf.data(), dptr, n * sizeof(__half), cudaMemcpyDeviceToHost));
+        double sum = 0., sumsq = 0.;
+        for (const __half x : hbuf) {
+            const double v = __half2float(x);
+            sum += v;
+            sumsq += v * v;
+        }
+        std::fputs(std::format("{{\"name\": \"{}\", \"n\": {}, \"sum\": {:.17g}, \"sumsq\": {:.17g}, \"first\": "
+                               "[{}, {}, {}, {}]}}\n",
+                               name, n, sum, sumsq, __half2float(hbuf[0]), __half2float(hbuf[1]),
+                               __half2float(hbuf[2]), __half2float(hbuf[3]))
+                       .c_str(),
+                   stdout);
+    };
+    const auto& w = m.weights;
+    report("embedding_tokens", w.embedding_tokens, size_t(c.vocab_size) * h);
+    for (size_t i = 0; i < w.transformer_blocks.size(); ++i) {
+        const auto& b = w.transformer_blocks[i];
+        const std::string p = std::format("layers.{}.", i);
+        report(p + "input_normalization", b.input_normalization, h);
+        report(p + "q_proj", b.q_proj, q * h);
+        report(p + "k_proj", b.k_proj, kv * h);
+        report(p + "v_proj", b.v_proj, kv * h);
+        report(p + "o_proj", b.o_proj, h * q);
+        report(p + "post_attn_norm", b.post_attn_norm, h);
+        report(p + "gate_proj", b.gate_proj, inter * h);
+        report(p + "up_proj", b.up_proj, inter * h);
+        report(p + "down_proj", b.down_proj, h * inter);
+    }
+    report("final_norm", w.final_norm, h);
+    report("lm_head", w.lm_head, size_t(c.vocab_size) * h);
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -390,7 +446,9 @@ int main(int argc, char** argv) {
         if (mode == "engine" && argc == 4) return run_engine(argv[2], argv[3]);
         if (mode == "known-answer" && argc == 2) return run_known_answer();
         if (mode == "golden" && argc == 3) return run_golden(argv[2]);
-        std::fputs("usage: engine_harness engine <in> <out> | known-answer | golden <dir>\n", stderr);
+        if (mode == "weights" && argc == 4) return run_weights(argv[2], std::stoull(argv[3]));
+        std::fputs("usage: engine_harness engine <in> <out> | known-answer | golden <dir> | weights <file> <chunk>\n",
+                   stderr);
         return 2;
     } catch (const std::exception& e) {
         std::fputs((std::string("error: ") + e.what() + "\n").c_str(), stderr);

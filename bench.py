@@ -26,7 +26,8 @@ Sub-measurements in the same line: `prefill` (config 3: 36 layers of
 RoPE/append + batched causal prefill, TFLOP/s, with its own e2e and CPU
 baseline), `ragged` (config 5, GB/s, e2e and CPU baseline) and, on one GPU,
 `small` (configs 1 and 2, latency-bound single layers: per-call device time
-eager and graphed, e2e, CPU baselines in full). CPU baselines (rank 0, one
+eager and graphed, e2e, CPU baselines in full) and `out_projection` (the
+path's consumer: the o_proj GEMM over config 3's tokens and the decode GEMV). CPU baselines (rank 0, one
 GPU) time the C oracle (the double-precision restatement of
 tests/test_causal_attention.cpp:176-196) and the python/reference.py:62-92
 path on CPU torch (FP16, FP32) with every host thread, on bounded samples.
@@ -863,6 +864,100 @@ def run_small(args, dev):
     return res
 
 
+# --------------------------------------------------------------------------- out projection (the consumer)
+OP_HIDDEN = 2048
+
+
+def run_out_proj(args, dev):
+    """The attention output projection at the benchmark shapes, one GPU:
+    prefill GEMM over config 3's 4 x 8192 tokens per layer (36 layers, a
+    distinct weight matrix per layer, fused residual add), and the decode GEMV
+    of config 4 (36 layers' weights, 302 MB, larger than L2)."""
+    import torch
+    import b200attn
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev).manual_seed(SEED + 400)
+    M, N, K = PF_B * PF_S, OP_HIDDEN, Q_DIM
+    x = torch.empty((M, K), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    w = torch.empty((LAYERS, N, K), dtype=torch.float16, device=dev).normal_(0.0, 0.02, generator=gen)
+    y = torch.empty((M, N), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    n0 = b200attn.kernel_launch_count()
+
+    def gemm_step(st):
+        for l in range(LAYERS):
+            b200attn.launch_attention_out_projection(x, y, w[l], M, N, H, D, 1.0, stream=st)
+    with torch.cuda.stream(stream):
+        gemm_step(stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(1, min(args.steps, args.prefill_steps))
+        with ClockSampler(dev.index) as clocks:
+            e0.record(stream)
+            for _ in range(steps):
+                gemm_step(stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps / LAYERS
+    flops = 2 * M * N * K
+    tf = flops / (ms / 1e3) / 1e12
+    peak = 1400.0
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        with open(pk) as f:
+            peak = float(json.load(f).get("bf16_tflops_sustained", peak))
+    del x, y
+    torch.cuda.empty_cache()
+
+    # decode GEMV: one token per layer, weights of all 36 layers cycled
+    xv = torch.empty((LAYERS, K), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    yv = torch.empty((LAYERS, N), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+
+    def gemv_step(st):
+        for l in range(LAYERS):
+            b200attn.launch_attention_out_projection_decode(xv[l], yv[l], w[l], N, H, D, 1.0, stream=st)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        gemv_step(stream)
+        torch.cuda.synchronize()
+    with torch.cuda.graph(g, stream=stream):
+        gemv_step(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    reps = 20
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    g.reset()
+    us = e0.elapsed_time(e1) / reps / LAYERS * 1e3
+    vbytes = N * K * 2 + K * 2 + 2 * N * 2
+    hbm, hbm_kind = load_peaks()
+    launches = b200attn.kernel_launch_count() - n0
+    del w, xv, yv
+    torch.cuda.empty_cache()
+    return {"workload": f"o_proj: prefill GEMM [{M} x {K}] @ W^T [{K} x {N}] + residual per layer (config 3 tokens), "
+                        f"decode GEMV W [{N} x {K}] per layer (config 4), 36 layers' weights, FP16 in/out, FP32 "
+                        "accumulate",
+            "prefill": {"value": round(tf, 1), "unit": "TFLOP/s", "ms_per_layer": round(ms, 4),
+                        "roofline": {"bound": "tensor", "kernel": "out_proj_gemm_kernel", "achieved": round(tf, 1),
+                                     "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
+                                     "frac_of_nominal_2250": round(tf / 2250.0, 4),
+                                     "algorithmic_flops_per_launch": flops, "peak_kind": "measured bf16 sustained"},
+                        "clocks": clocks.summary()},
+            "decode": {"value": round(vbytes / us / 1e3, 1), "unit": "GB/s", "us_per_layer": round(us, 3),
+                       "roofline": {"bound": "hbm", "kernel": "out_proj_gemv_kernel",
+                                    "achieved": round(vbytes / us / 1e3, 1), "peak": hbm, "unit": "GB/s",
+                                    "frac": round(vbytes / us / 1e3 / hbm, 4), "peak_kind": hbm_kind,
+                                    "algorithmic_bytes_per_launch": vbytes,
+                                    "timing": f"one CUDA graph of 36 launches (distinct weights), {reps} replays"}},
+            "gpu_launches": launches}
+
+
 # --------------------------------------------------------------------------- GPU arm
 def run_b200(args, rank, world):
     import numpy as np
@@ -995,6 +1090,10 @@ def run_b200(args, rank, world):
     if world == 1 and not args.no_small:
         small = run_small(args, dev)
         torch.cuda.empty_cache()
+    out_proj = None
+    if world == 1 and not args.no_out_proj:
+        out_proj = run_out_proj(args, dev)
+        torch.cuda.empty_cache()
     if not args.no_prefill:
         prefill = run_prefill(args, rank, world, dev)
         torch.cuda.empty_cache()
@@ -1033,6 +1132,7 @@ def run_b200(args, rank, world):
             "prefill": prefill,
             "ragged": ragged,
             "small": small,
+            "out_projection": out_proj,
         }
         print(json.dumps(line), flush=True)
     graph.reset()
@@ -1049,6 +1149,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill sub-measurement")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-5 ragged decode sub-measurement")
     ap.add_argument("--no-small", action="store_true", help="skip the config-1/2 (latency-bound) sub-measurement")
+    ap.add_argument("--no-out-proj", action="store_true", help="skip the attention output projection measurement")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
                          "all-gather of the rank partials and a merge kernel")

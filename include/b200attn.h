@@ -415,6 +415,31 @@ int b2_launch_decode_step_ragged_fused(const void* d_q, size_t q_seq_stride, con
                                        size_t num_kv_heads, size_t head_dim, void* d_workspace,
                                        size_t workspace_bytes, b2_stream_t stream);
 
+/* ---- Attention output projection (the path's consumer) ---------------------
+ * include/kernels/kernels.hpp:168-177 launch_attention_out_projection
+ * (src/kernels/attention_out_projection.hip.cpp:8-58): out[t][n] =
+ * sum_k in[t][k] * w[n][k] + beta * out[t][n] for t < seq_len, n <
+ * hidden_size, k < num_heads * head_dim; in is the packed attention output
+ * [seq][num_heads * head_dim], w the o_proj weights [hidden][num_heads *
+ * head_dim] (PyTorch [out, in]), out [seq][hidden] holds the residual on
+ * entry (beta = 1: the fused residual add) and is not read when beta = 0.
+ * FP16 in and out, FP32 accumulation. hidden a multiple of 256, K a multiple
+ * of 64 and 16-byte aligned rows run the tcgen05 GEMM; other shapes a SIMT
+ * kernel. seq_len, hidden or K of 0: B2_NOTHING_TO_DO. Adds a stream. */
+int b2_launch_attention_out_projection(const void* d_in, void* d_out, const void* d_o_proj_weights,
+                                       size_t seq_len, size_t hidden_size, size_t num_heads,
+                                       size_t head_dim, float beta, b2_stream_t stream);
+
+/* include/kernels/kernels.hpp:179-188 launch_attention_out_projection_decode
+ * (attention_out_projection.hip.cpp:60-71, launch_matrix_vector_mul): the same
+ * for one token, a bandwidth-bound GEMV (K a multiple of 256 up to 4096 and
+ * aligned rows; otherwise the SIMT kernel). The GEMV reads the weights before
+ * waiting for the kernel it follows on the stream (programmatic dependent
+ * launch), so the weights must not be written by that kernel. */
+int b2_launch_attention_out_projection_decode(const void* d_in, void* d_out, const void* d_o_proj_weights,
+                                              size_t hidden_size, size_t num_heads, size_t head_dim,
+                                              float beta, b2_stream_t stream);
+
 /* ---- Decode without a caller workspace ------------------------------------
  * No counterpart in the reference (whose decode launchers always take the
  * three partial arrays). For callers that cannot provide scratch memory: a

@@ -8,8 +8,9 @@
 // stay silent; anything else that fails throws std::runtime_error where the
 // reference would have exited through HIP_CHECK.
 //
-// The non-attention launchers of the reference header (embedding, RMSNorm,
-// GEMMs, SwiGLU, argmax) are not part of this library.
+// Of the reference header's non-attention launchers only the attention output
+// projection, the path's consumer, is here; embedding, RMSNorm, the other
+// GEMMs, SwiGLU and argmax are not part of this library.
 #pragma once
 
 #include <cstddef>
@@ -121,4 +122,24 @@ inline void update_causal_attention_decode_node(hipGraphExec_t graph_exec, hipGr
     b200attn::check(b2_update_causal_attention_decode_node(reinterpret_cast<b2_graph_exec_t>(graph_exec),
                                                            reinterpret_cast<b2_graph_node_t>(node), kv_cache_len),
                     "update_causal_attention_decode_node");
+}
+
+// kernels.hpp:168-177 (the stream parameter is an addition)
+inline void launch_attention_out_projection(const __half* d_in, __half* d_out, const __half* d_o_proj_weights,
+                                            size_t seq_len, size_t hidden_size, size_t num_heads, size_t head_dim,
+                                            float beta = 0.f, hipStream_t stream = nullptr) {
+    b200attn::check(b2_launch_attention_out_projection(d_in, d_out, d_o_proj_weights, seq_len, hidden_size,
+                                                       num_heads, head_dim, beta, b200attn::detail::s(stream)),
+                    "launch_attention_out_projection");
+}
+
+// kernels.hpp:179-188
+inline void launch_attention_out_projection_decode(const __half* d_in, __half* d_out,
+                                                   const __half* d_o_proj_weights, size_t hidden_size,
+                                                   size_t num_heads, size_t head_dim, float beta,
+                                                   hipStream_t stream = nullptr) {
+    b200attn::check(b2_launch_attention_out_projection_decode(d_in, d_out, d_o_proj_weights, hidden_size,
+                                                              num_heads, head_dim, beta,
+                                                              b200attn::detail::s(stream)),
+                    "launch_attention_out_projection_decode");
 }

@@ -28,7 +28,7 @@ __all__ = [
     "decode_step_workspace_bytes", "launch_decode_step_fused", "launch_decode_step_fused_rank_partial",
     "launch_rope_and_store_kv_ragged", "decode_ragged_workspace_bytes", "launch_causal_attention_decode_ragged",
     "decode_exchange_bytes", "launch_decode_step_fused_exchange", "ExchangeBuffers",
-    "launch_decode_step_ragged_fused",
+    "launch_decode_step_ragged_fused", "launch_attention_out_projection", "launch_attention_out_projection_decode",
 ]
 
 
@@ -350,3 +350,19 @@ def launch_causal_attention_prefill_batched(d_q, d_k, d_v, d_out, batch, seq_len
         _ptr(d_q), _ptr(d_k), _ptr(d_v), _ptr(d_out), batch, seq_len, num_heads, num_kv_heads, head_dim,
         q_stride, kv_stride, out_stride, q_batch_stride, kv_batch_stride, out_batch_stride, _stream(stream)),
         "launch_causal_attention_prefill_batched")
+
+
+def launch_attention_out_projection(d_in, d_out, d_o_proj_weights, seq_len, hidden_size, num_heads, head_dim,
+                                    beta=0.0, stream=None):
+    """kernels.hpp:168-177 (plus a stream): out = in @ W^T + beta * out."""
+    check(lib().b2_launch_attention_out_projection(
+        _ptr(d_in), _ptr(d_out), _ptr(d_o_proj_weights), seq_len, hidden_size, num_heads, head_dim, float(beta),
+        _stream(stream)), "launch_attention_out_projection")
+
+
+def launch_attention_out_projection_decode(d_in, d_out, d_o_proj_weights, hidden_size, num_heads, head_dim, beta,
+                                           stream=None):
+    """kernels.hpp:179-188: one token, out = W @ in + beta * out."""
+    check(lib().b2_launch_attention_out_projection_decode(
+        _ptr(d_in), _ptr(d_out), _ptr(d_o_proj_weights), hidden_size, num_heads, head_dim, float(beta),
+        _stream(stream)), "launch_attention_out_projection_decode")

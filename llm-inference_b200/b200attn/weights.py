@@ -100,7 +100,7 @@ def read_weights(path: str) -> HostWeights:
 def upload(w: HostWeights, device):
     """One device tensor holding the payload and views of it per name."""
     import torch
-    buf = torch.from_numpy(np.ascontiguousarray(w.payload)).to(device)
+    buf = torch.from_numpy(np.array(w.payload, copy=True)).to(device)
     views, cur = {}, 0
     for name, arr in w.tensors.items():
         n = arr.size

@@ -25,6 +25,8 @@ int clear_device_error_decode();
 int clear_device_error_prefill();
 unsigned int device_error_ragged();
 int clear_device_error_ragged();
+unsigned int device_error_outproj();
+int clear_device_error_outproj();
 
 // Turn the launch status of the kernel just enqueued into a b2 status.
 inline int launch_status() {

@@ -1,0 +1,353 @@
+// Attention output projection, the consumer of the attention path
+// (src/kernels/attention_out_projection.hip.cpp:8-58, launch_attention_out_
+// projection and its decode form): out[t][n] = sum_k attn[t][k] W[n][k] +
+// beta * out[t][n], attn [seq][num_heads * head_dim] (the packed rows the
+// prefill and decode kernels write), W [hidden][num_heads * head_dim]
+// (PyTorch [out, in]), out [seq][hidden] holding the residual on entry when
+// beta != 0. FP16 in and out, FP32 accumulation. beta == 0 never reads out.
+//
+// Prefill (seq > 1): a persistent tcgen05 GEMM. Output tiles of 128 tokens x
+// 256 hidden columns, K in 64-element steps. Warp 0 streams A (attn) and B
+// (W) tiles with tensor-map copies into a 4-stage ring (128-byte swizzle,
+// 48 KB a stage); warp 1 issues tcgen05.mma (M 128, N 256, K 16; f16 in,
+// f32 accumulate) into one of two 256-column TMEM accumulators; warps 4-7
+// drain the other accumulator (tcgen05.ld, + beta * residual, fp16 stores)
+// while the next tile's MMAs run. Both operands K-major, as the reference's
+// rocBLAS call (transpose W, keep X).
+// Decode (seq 1): a bandwidth-bound GEMV (the reference's
+// launch_matrix_vector_mul), one warp per output row, 16-byte loads of W
+// issued before the dependency wait.
+// Other shapes (hidden not a multiple of 256, K not a multiple of 64,
+// unaligned rows) take a plain SIMT kernel.
+#include <math.h>
+
+#include <atomic>
+
+#include "b2_common.cuh"
+#include "b2_ptx.cuh"
+#include "tcgen05.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr uint32_t kBM = 128, kBN = 256, kBK = 64;
+constexpr uint32_t kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kGemmSmem = kStages * kStageBytes + 1024 /*barriers*/ + 1024 /*alignment*/;
+constexpr int kGemmThreads = 256;             // 0 TMA, 1 MMA, 2-3 idle, 4-7 epilogue
+
+struct GemmArgs {
+    const __half* residual;  // = out (read only when beta != 0)
+    __half* out;
+    uint32_t M, N, K;
+    uint32_t tiles_m, tiles_n;
+    float beta;
+};
+
+struct GemmBars {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    out_proj_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const GemmArgs g) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    GemmBars* bars = reinterpret_cast<GemmBars*>(smem + kStages * kStageBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ntiles = g.tiles_m * g.tiles_n;
+    const uint32_t kb_count = g.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->acc_full[b], 1);
+            mbar_init(&bars->acc_empty[b], 4);
+        }
+        bars->abort = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tc::tmem_alloc(&bars->tmem_base, 512);
+    pdl_wait_primary();  // attn rows and the residual come from earlier kernels
+    pdl_launch_dependents();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tbase = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tc::prefetch_tensormap(&map_a);
+            tc::prefetch_tensormap(&map_b);
+            uint32_t i = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                // N-fastest order: consecutive CTAs share the A rows (L2 reuse)
+                const int32_t m0 = static_cast<int32_t>((tile / g.tiles_n) * kBM);
+                const int32_t n0 = static_cast<int32_t>((tile % g.tiles_n) * kBN);
+                for (uint32_t kb = 0; kb < kb_count; ++kb, ++i) {
+                    const uint32_t s = i % kStages, r = i / kStages;
+                    if (r > 0 && !(ok = mbar_wait(&bars->empty[s], (r - 1) & 1))) break;
+                    uint8_t* st = smem + s * kStageBytes;
+                    mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+                    tc::tma_load_3d(st, &map_a, static_cast<int32_t>(kb * kBK), m0, 0, &bars->full[s]);
+                    tc::tma_load_3d(st + kABytes, &map_b, static_cast<int32_t>(kb * kBK), n0, 0, &bars->full[s]);
+                }
+            }
+            if (!ok) bars->abort = 1;
+            // never leave with copies in flight into shared memory
+            for (uint32_t j = i > kStages ? i - kStages : 0; j < i; ++j)
+                (void)mbar_wait(&bars->full[j % kStages], (j / kStages) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(kBM, kBN, false, false);
+            uint32_t i = 0, t = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t) {
+                const uint32_t buf = t & 1;
+                // the epilogue has drained this accumulator (tile t - 2)
+                if (t >= 2 && !(ok = mbar_wait(&bars->acc_empty[buf], ((t >> 1) - 1) & 1))) break;
+                tc::fence_after_sync();
+                const uint32_t d = tbase + buf * kBN;
+                for (uint32_t kb = 0; kb < kb_count; ++kb, ++i) {
+                    const uint32_t s = i % kStages;
+                    if (!(ok = mbar_wait(&bars->full[s], (i / kStages) & 1))) break;
+                    tc::fence_after_sync();
+                    const uint32_t a = smem_u32(smem + s * kStageBytes), b = a + kABytes;
+#pragma unroll
+                    for (uint32_t ks = 0; ks < kBK / 16; ++ks)
+                        tc::mma_ss(d, tc::desc_kmajor_sw128(a + ks * 32), tc::desc_kmajor_sw128(b + ks * 32), idesc,
+                                   (kb | ks) != 0 ? 1u : 0u);
+                    tc::commit(&bars->empty[s]);  // the stage is free once these MMAs have read it
+                }
+                if (ok) tc::commit(&bars->acc_full[buf]);
+            }
+            if (!ok) bars->abort = 1;
+        }
+    } else if (warp >= 4) {
+        const uint32_t quarter = static_cast<uint32_t>(warp) & 3;
+        const uint32_t lane_addr = (quarter * 32) << 16;
+        uint32_t t = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t) {
+            const uint32_t buf = t & 1;
+            const uint32_t row = (tile / g.tiles_n) * kBM + quarter * 32 + lane;
+            const uint32_t n0 = (tile % g.tiles_n) * kBN;
+            const bool live = row < g.M;
+            const uint64_t base = static_cast<uint64_t>(row) * g.N + n0;
+            if (!(ok = mbar_wait(&bars->acc_full[buf], (t >> 1) & 1))) break;
+            tc::fence_after_sync();
+#pragma unroll 1
+            for (uint32_t half = 0; half < 2; ++half) {
+                // this half's 128 residual values in flight before the TMEM loads
+                uint4 res[16];
+                if (g.beta != 0.f && live) {
+#pragma unroll
+                    for (int v = 0; v < 16; ++v)
+                        res[v] = *reinterpret_cast<const uint4*>(g.residual + base + half * 128 + v * 8);
+                }
+#pragma unroll
+                for (uint32_t c = 0; c < 4; ++c) {
+                    uint32_t raw[32];
+                    tc::tmem_ld32(tbase + lane_addr + buf * kBN + half * 128 + c * 32, raw);
+                    tc::tmem_wait_ld();
+                    uint32_t o16[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float lo = __uint_as_float(raw[2 * j]), hi = __uint_as_float(raw[2 * j + 1]);
+                        if (g.beta != 0.f && live) {
+                            const uint32_t w = (&res[c * 4].x)[j];
+                            const __half2 r2 = *reinterpret_cast<const __half2*>(&w);
+                            const float2 rf = __half22float2(r2);
+                            lo = fmaf(g.beta, rf.x, lo);
+                            hi = fmaf(g.beta, rf.y, hi);
+                        }
+                        o16[j] = pack_half2(lo, hi);
+                    }
+                    if (live) {
+                        uint4* dst = reinterpret_cast<uint4*>(g.out + base + half * 128 + c * 32);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v)
+                            dst[v] = make_uint4(o16[4 * v], o16[4 * v + 1], o16[4 * v + 2], o16[4 * v + 3]);
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+        }
+        if (!ok) bars->abort = 1;
+    }
+    __syncthreads();
+    if (bars->abort && threadIdx.x == 0) atomicOr(&g_device_error, kErrWaitTimeout);
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tbase, 512);
+    }
+}
+
+// Decode GEMV: out[n] = W[n] . x + beta * out[n], one warp per row, K a
+// multiple of 256 and at most kGemvMaxK (each lane holds 8 halves of the row
+// per 256). The weights do not depend on the kernel this one follows on the
+// stream, so the row is loaded before the dependency wait: with programmatic
+// dependent launch the 8 MB weight stream overlaps the previous kernel's
+// tail, and only x and the residual are read after it.
+constexpr int kGemvWarps = 8;
+constexpr uint32_t kGemvMaxK = 4096;
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    out_proj_gemv_kernel(const __half* __restrict__ x, const __half* __restrict__ w, __half* out, uint32_t N,
+                         uint32_t K, float beta) {
+    constexpr int kMaxV = kGemvMaxK / 256;
+    pdl_launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t n = blockIdx.x * kGemvWarps + warp;
+    const bool live = n < N;
+    const __half* row = w + static_cast<uint64_t>(live ? n : 0) * K;
+    const uint32_t nv = K / 256;
+    uint4 wv[kMaxV];
+#pragma unroll
+    for (int u = 0; u < kMaxV; ++u)
+        wv[u] = (live && static_cast<uint32_t>(u) < nv) ? ldg_nc_v4(row + u * 256 + lane * 8)
+                                                          : make_uint4(0u, 0u, 0u, 0u);
+    pdl_wait_primary();  // x and the residual may come from the previous kernel
+    if (!live) return;
+    // the residual load goes out with the x loads, not after the reduction
+    const float resid = (lane == 0 && beta != 0.f) ? __half2float(out[n]) : 0.f;
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxV; ++u) {
+        if (static_cast<uint32_t>(u) < nv) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(x + u * 256 + lane * 8);
+            const __half2* a = reinterpret_cast<const __half2*>(&wv[u]);
+            const __half2* b = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 fa = __half22float2(a[j]), fb = __half22float2(b[j]);
+                acc = fmaf(fa.x, fb.x, acc);
+                acc = fmaf(fa.y, fb.y, acc);
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+        if (beta != 0.f) acc = fmaf(beta, resid, acc);
+        out[n] = __float2half_rn(acc);
+    }
+}
+
+// Any shape: one thread per output element, FP32 accumulation.
+__global__ void out_proj_simt_kernel(const __half* __restrict__ x, const __half* __restrict__ w, __half* out,
+                                     uint32_t M, uint32_t N, uint32_t K, float beta) {
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<uint64_t>(M) * N) return;
+    const uint32_t m = static_cast<uint32_t>(idx / N), n = static_cast<uint32_t>(idx % N);
+    const __half* a = x + static_cast<uint64_t>(m) * K;
+    const __half* b = w + static_cast<uint64_t>(n) * K;
+    float acc = 0.f;
+    for (uint32_t k = 0; k < K; ++k) acc = fmaf(__half2float(a[k]), __half2float(b[k]), acc);
+    if (beta != 0.f) acc = fmaf(beta, __half2float(out[idx]), acc);
+    out[idx] = __float2half_rn(acc);
+}
+
+int sm_count() {
+    static std::atomic<int> cached{0};
+    int v = cached.load();
+    if (v > 0) return v;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess || v <= 0)
+        v = 148;
+    cached.store(v);
+    return v;
+}
+
+int ensure_gemm_smem() {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return B2_ERR_CUDA;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load() & bit) return B2_OK;
+    const int st =
+        cuda_status(cudaFuncSetAttribute(out_proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+    if (st == B2_OK) done.fetch_or(bit);
+    return st;
+}
+
+int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, size_t N, size_t K, float beta,
+                    cudaStream_t stream, bool decode_form) {
+    if (M == 0 || N == 0 || K == 0) return B2_NOTHING_TO_DO;
+    if (!d_in || !d_out || !d_w) return B2_ERR_INVALID_ARG;
+    if (M > 0x7fffffffull || N > 0x7fffffffull || K > 0x7fffffffull) return B2_ERR_UNSUPPORTED;
+    const auto* x = static_cast<const __half*>(d_in);
+    const auto* w = static_cast<const __half*>(d_w);
+    auto* out = static_cast<__half*>(d_out);
+    const uint32_t m = static_cast<uint32_t>(M), n = static_cast<uint32_t>(N), k = static_cast<uint32_t>(K);
+    const bool aligned = aligned16(x) && aligned16(w) && aligned16(out);
+    if (decode_form || M == 1) {
+        if (aligned && K % 256 == 0 && K <= kGemvMaxK && M == 1)
+            return launch_pdl(out_proj_gemv_kernel, dim3((n + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32),
+                              0, stream, x, w, out, n, k, beta);
+    } else if (aligned && N % kBN == 0 && K % kBK == 0) {
+        int st = ensure_gemm_smem();
+        if (st != B2_OK) return st;
+        CUtensorMap ma, mb;
+        if (encode_tensor_map_3d_f16(&ma, x, K, M, 1, K * 2, 0, kBK, kBM) != 0 ||
+            encode_tensor_map_3d_f16(&mb, w, K, N, 1, K * 2, 0, kBK, kBN) != 0)
+            return B2_ERR_UNSUPPORTED;
+        GemmArgs g{};
+        g.residual = out;
+        g.out = out;
+        g.M = m;
+        g.N = n;
+        g.K = k;
+        g.tiles_m = (m + kBM - 1) / kBM;
+        g.tiles_n = n / kBN;
+        g.beta = beta;
+        const uint32_t tiles = g.tiles_m * g.tiles_n;
+        const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count()));
+        return launch_pdl(out_proj_gemm_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, stream, ma, mb, g);
+    }
+    const uint64_t total = static_cast<uint64_t>(m) * n;
+    return launch_pdl(out_proj_simt_kernel, dim3(static_cast<uint32_t>((total + 255) / 256)), dim3(256), 0, stream,
+                      x, w, out, m, n, k, beta);
+}
+
+}  // namespace
+
+unsigned int device_error_outproj() {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0;
+    return v;
+}
+
+int clear_device_error_outproj() {
+    const unsigned int zero = 0;
+    return cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+}
+
+}  // namespace b2
+
+extern "C" int b2_launch_attention_out_projection(const void* d_in, void* d_out, const void* d_o_proj_weights,
+                                                  size_t seq_len, size_t hidden_size, size_t num_heads,
+                                                  size_t head_dim, float beta, b2_stream_t stream) {
+    return b2::launch_out_proj(d_in, d_out, d_o_proj_weights, seq_len, hidden_size, num_heads * head_dim, beta,
+                               reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int b2_launch_attention_out_projection_decode(const void* d_in, void* d_out, const void* d_o_proj_weights,
+                                                         size_t hidden_size, size_t num_heads, size_t head_dim,
+                                                         float beta, b2_stream_t stream) {
+    return b2::launch_out_proj(d_in, d_out, d_o_proj_weights, 1, hidden_size, num_heads * head_dim, beta,
+                               reinterpret_cast<cudaStream_t>(stream), true);
+}

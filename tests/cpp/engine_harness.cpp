@@ -411,10 +411,10 @@ int run_weights(const std::string& path, size_t chunk) {
             sum += v;
             sumsq += v * v;
         }
+        auto at = [&hbuf](size_t i) { return static_cast<double>(__half2float(hbuf[i])); };
         std::fputs(std::format("{{\"name\": \"{}\", \"n\": {}, \"sum\": {:.17g}, \"sumsq\": {:.17g}, \"first\": "
-                               "[{}, {}, {}, {}]}}\n",
-                               name, n, sum, sumsq, __half2float(hbuf[0]), __half2float(hbuf[1]),
-                               __half2float(hbuf[2]), __half2float(hbuf[3]))
+                               "[{:.17g}, {:.17g}, {:.17g}, {:.17g}]}}\n",
+                               name, n, sum, sumsq, at(0), at(1), at(2), at(3))
                        .c_str(),
                    stdout);
     };

@@ -3,8 +3,12 @@
 
 Runs the reference's own exporter, python/export_weights.py:20-135
 (``export_model_weights``, unmodified), on a seeded random-init SmolLM3 model
-of a tiny geometry (vocab 128, hidden 64, 2 layers, 4 query / 2 KV heads of
-16, intermediate 96), saved to a temporary directory first. The tokenizer the
+of a tiny geometry (vocab 128, hidden 128, 2 layers, 4 query / 2 KV heads of
+32, intermediate 96), saved to a temporary directory first, and the
+reference's fixture generator, python/reference.py:40-96
+(``save_activations``, unmodified), on the same model and 40 seeded tokens;
+its layer-0 dumps on the attention path (q/k/v projections, rotated q/k,
+attention output, o_proj output) go to tests/golden/tiny/. The tokenizer the
 exporter serialises is replaced by a stub whose JSON is a short fixed string
 (the real tokenizer needs the hub), and from_pretrained is called without
 device_map (accelerate is not installed). tiny_weights.json records the header
@@ -37,6 +41,13 @@ class _TokStub:
     _tokenizer = _InnerTok()
 
 
+class _TokStub2:
+    """save_activations only decodes the greedy token."""
+
+    def decode(self, ids):
+        return " ".join(str(i) for i in ids)
+
+
 def main() -> None:
     if "REFERENCE_ROOT" not in os.environ:
         raise SystemExit("set REFERENCE_ROOT to the reference checkout (the directory holding python/)")
@@ -49,9 +60,9 @@ def main() -> None:
     from model_config import ModelConfig
 
     torch.manual_seed(77)
-    cfg = SmolLM3Config(vocab_size=128, hidden_size=64, intermediate_size=96, num_hidden_layers=2,
-                        num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=512,
-                        initializer_range=0.5, rope_parameters={"rope_type": "default", "rope_theta": 5.0e6},
+    cfg = SmolLM3Config(vocab_size=128, hidden_size=128, intermediate_size=96, num_hidden_layers=2,
+                        num_attention_heads=4, num_key_value_heads=2, head_dim=32, max_position_embeddings=512,
+                        initializer_range=0.1, rope_parameters={"rope_type": "default", "rope_theta": 5.0e6},
                         tie_word_embeddings=True, pad_token_id=0, bos_token_id=1, eos_token_id=2)
     model = SmolLM3ForCausalLM(cfg).eval()
     with torch.no_grad():   # norms away from 1.0 so a swapped tensor shows
@@ -75,6 +86,17 @@ def main() -> None:
         mc = ModelConfig(cfg)
         out = HERE / "tiny_weights.bin"
         export_weights.export_model_weights(mc, tmp, out)
+    # the fixture generator on the same model (fp16, as from_pretrained gives it)
+    import reference  # python/reference.py of the reference checkout
+    tiny = HERE / "tiny"
+    tiny.mkdir(exist_ok=True)
+    m16 = model.to(torch.float16).eval()
+    ids = torch.randint(0, cfg.vocab_size, (1, 40), generator=torch.Generator().manual_seed(78))
+    with tempfile.TemporaryDirectory() as tmp:
+        reference.save_activations(m16, _TokStub2(), Path(tmp), 40, ids)
+        for name in ("layer0_q_proj_out", "layer0_k_proj_out", "layer0_v_proj_out", "layer0_q_rope",
+                     "layer0_k_rope", "layer0_attn_out", "layer0_o_proj_out"):
+            (tiny / f"{name}.bin").write_bytes((Path(tmp) / f"{name}.bin").read_bytes())
     sd = {k: v.to(torch.float16).float().numpy().astype(np.float64) for k, v in model.state_dict().items()}
     order = ["model.embed_tokens.weight"]
     for i in range(cfg.num_hidden_layers):

@@ -2,10 +2,11 @@
 file written by the reference's own exporter (python/export_weights.py, see
 tests/golden/make_weights_fixture.py): header, tokenizer JSON, the payload
 offset and every tensor the loader carves, against the exporting model's
-state dict (tests/golden/tiny_weights.json)."""
+state dict (tests/golden/tiny_weights.json); and the layer-0 activations the
+reference's fixture generator dumped for that model (tests/golden/tiny/) run
+through RoPE, prefill and the o_proj carved from the loaded weights."""
 import json
 import os
-import shutil
 import subprocess
 
 import numpy as np
@@ -110,3 +111,67 @@ def test_python_upload_views(cuda):
     assert buf.numel() == w.payload.size
     for name, arr in w.tensors.items():
         np.testing.assert_array_equal(views[name].cpu().numpy(), arr)
+
+
+def _tiny_acts():
+    base = os.path.join(ROOT, "tests", "golden", "tiny")
+    h = META["header"]
+    H, KVH, d, hid = h["num_heads"], h["num_kv_heads"], h["head_dim"], h["hidden_size"]
+    S = 40
+
+    def ld(name, cols):
+        return np.fromfile(os.path.join(base, name + ".bin"), np.float16).reshape(S, cols)
+    return (S, H, KVH, d, hid, h["rope_theta"]), {
+        "q": ld("layer0_q_proj_out", H * d), "k": ld("layer0_k_proj_out", KVH * d),
+        "v": ld("layer0_v_proj_out", KVH * d), "q_rope": ld("layer0_q_rope", H * d),
+        "k_rope": ld("layer0_k_rope", KVH * d), "attn": ld("layer0_attn_out", H * d),
+        "o_proj": ld("layer0_o_proj_out", hid)}
+
+
+def test_oracle_on_the_exported_models_layer0():
+    """The CPU oracle reproduces the reference generator's layer-0 dumps of the
+    exported tiny model (head_dim 32), and the o_proj carved by the loader maps
+    its attention output to the generator's o_proj output."""
+    import oracle
+    from _util import tensor_close_mismatches
+    (S, H, KVH, d, hid, theta), g = _tiny_acts()
+    cos, sin = oracle.rope_tables(512, d, theta)
+    q, k = g["q"].copy(), g["k"].copy()
+    oracle.rope_and_store_kv(q, k, None, None, None, cos, sin, S, H, KVH, d, H * d, KVH * d, 0, True)
+    assert tensor_close_mismatches(q, g["q_rope"], 2e-2, 2e-2) == 0
+    assert tensor_close_mismatches(k, g["k_rope"], 2e-2, 2e-2) == 0
+    o16, _ = oracle.causal_attention(g["q_rope"], g["k_rope"], g["v"], S, H, KVH, d)
+    assert tensor_close_mismatches(o16, g["attn"], 2e-2, 2e-2) == 0
+    w = W.read_weights(FIX).tensors["layers.0.o_proj"].astype(np.float64)
+    proj = g["attn"].astype(np.float64) @ w.T
+    assert tensor_close_mismatches(proj, g["o_proj"], 2e-2, 2e-2) == 0
+
+
+@pytest.mark.gpu
+def test_exported_model_layer0_through_the_kernels(cuda):
+    """weights.bin loaded and uploaded by the loader; the layer-0 projections the
+    reference's generator dumped go through RoPE/append, causal prefill and the
+    o_proj GEMM whose weight is the loader's carved layers.0.o_proj view; every
+    stage against the generator's dump at the reference's tolerance."""
+    import torch
+    import b200attn
+    from _gpu import dev, host
+    from _util import tensor_close_mismatches
+    (S, H, KVH, d, hid, theta), g = _tiny_acts()
+    w = W.read_weights(FIX)
+    _, views = W.upload(w, cuda)
+    cos, sin = b200attn.rope_tables_host(512, d, theta)
+    q, k, v = dev(g["q"]), dev(g["k"]), dev(g["v"])
+    cache = b200attn.KVCache(1, 64, KVH, d, device=cuda)
+    b200attn.launch_rope_and_store_kv(q, k, v, cache.get_k_cache(0), cache.get_v_cache(0), dev(cos), dev(sin), S, H,
+                                      KVH, d, H * d, KVH * d, 0, True)
+    attn = torch.empty((S, H * d), dtype=torch.float16, device=cuda)
+    b200attn.launch_causal_attention_prefill(q, cache.get_k_cache(0), cache.get_v_cache(0), attn, S, H, KVH, d,
+                                             H * d, KVH * d)
+    out = torch.full((S, hid), float("nan"), dtype=torch.float16, device=cuda)
+    b200attn.launch_attention_out_projection(attn, out, views["layers.0.o_proj"], S, hid, H, d, 0.0)
+    torch.cuda.synchronize()
+    assert tensor_close_mismatches(host(q), g["q_rope"], 2e-2, 2e-2) == 0
+    assert tensor_close_mismatches(host(cache.get_k_cache(0))[:S], g["k_rope"], 2e-2, 2e-2) == 0
+    assert tensor_close_mismatches(host(attn), g["attn"], 2e-2, 2e-2) == 0
+    assert tensor_close_mismatches(host(out), g["o_proj"], 2e-2, 2e-2) == 0

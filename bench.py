@@ -958,6 +958,79 @@ def run_out_proj(args, dev):
             "gpu_launches": launches}
 
 
+def run_qkv_proj(args, dev):
+    """The QKV projection with RoPE and the KV append in its epilogue, at the
+    benchmark shapes, one GPU: per layer and per config-3 sequence, [8192 x
+    2048] @ W_qkv^T [2048 x 3072] into the [Q | K | V] rows, Q rotated in
+    place, rotated K and V into the sequence's cache rows (NoPE every 4th
+    layer), 36 layers' weights. Timed beside the two launches it replaces
+    (the GEMM, then the RoPE/append kernel over its rows)."""
+    import torch
+    import b200attn
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev).manual_seed(SEED + 500)
+    M, N, K = PF_S, QKV, OP_HIDDEN
+    x = torch.empty((PF_B, M, K), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    w = torch.empty((LAYERS, N, K), dtype=torch.float16, device=dev).normal_(0.0, 0.02, generator=gen)
+    qkv = torch.empty((PF_B, M, N), dtype=torch.float16, device=dev)
+    # one cache pair per sequence, reused by every layer (the write traffic is the same)
+    cache = torch.empty((PF_B, 2, M, KV_DIM), dtype=torch.float16, device=dev)
+    cos, sin = b200attn.rope_tables_host(M, D, 5.0e6)
+    dcos, dsin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    n0 = b200attn.kernel_launch_count()
+
+    def fused_step(st):
+        for l in range(LAYERS):
+            for b in range(PF_B):
+                b200attn.launch_qkv_gemm_rope_store_kv(x[b], qkv[b], w[l], cache[b, 0], cache[b, 1], dcos, dsin, M,
+                                                       K, H, KVH, D, 0, (l + 1) % 4 != 0, stream=st)
+
+    def two_launch_step(st):
+        for l in range(LAYERS):
+            for b in range(PF_B):
+                q = qkv[b]
+                b200attn.launch_qkv_gemm(x[b], q, w[l], M, K, N, stream=st)
+                b200attn.launch_rope_and_store_kv(q, q[:, Q_DIM:], q[:, Q_DIM + KV_DIM:], cache[b, 0], cache[b, 1],
+                                                  dcos, dsin, M, H, KVH, D, N, N, 0, (l + 1) % 4 != 0, stream=st)
+
+    steps = max(1, min(args.steps, args.prefill_steps))
+    res = {}
+    for name, fn in (("fused", fused_step), ("two_launches", two_launch_step)):
+        with torch.cuda.stream(stream):
+            fn(stream)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(dev.index) as clocks:
+                e0.record(stream)
+                for _ in range(steps):
+                    fn(stream)
+                e1.record(stream)
+                torch.cuda.synchronize()
+        res[name] = (e0.elapsed_time(e1) / steps / LAYERS, clocks.summary())
+    launches = b200attn.kernel_launch_count() - n0
+    flops = 2 * PF_B * M * N * K
+    ms, clk = res["fused"]
+    tf = flops / (ms / 1e3) / 1e12
+    peak = 1400.0
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        with open(pk) as f:
+            peak = float(json.load(f).get("bf16_tflops_sustained", peak))
+    del x, w, qkv, cache
+    torch.cuda.empty_cache()
+    return {"workload": f"QKV projection per layer: {PF_B} sequences x [{M} x {K}] @ W_qkv^T [{K} x {N}] (config 3 "
+                        "tokens), RoPE (NoPE every 4th layer) and the KV append in the GEMM epilogue, 36 layers' "
+                        "weights, FP16 in/out, FP32 accumulate",
+            "value": round(tf, 1), "unit": "TFLOP/s", "ms_per_layer": round(ms, 4),
+            "two_launches_ms_per_layer": round(res["two_launches"][0], 4),
+            "speedup_vs_two_launches": round(res["two_launches"][0] / ms, 3),
+            "roofline": {"bound": "tensor", "kernel": "qkv_rope_gemm_kernel", "achieved": round(tf, 1),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
+                         "frac_of_nominal_2250": round(tf / 2250.0, 4),
+                         "algorithmic_flops_per_launch": flops // PF_B, "peak_kind": "measured bf16 sustained"},
+            "clocks": clk, "gpu_launches": launches}
+
+
 # --------------------------------------------------------------------------- GPU arm
 def run_b200(args, rank, world):
     import numpy as np
@@ -1094,6 +1167,10 @@ def run_b200(args, rank, world):
     if world == 1 and not args.no_out_proj:
         out_proj = run_out_proj(args, dev)
         torch.cuda.empty_cache()
+    qkv_proj = None
+    if world == 1 and not args.no_qkv_proj:
+        qkv_proj = run_qkv_proj(args, dev)
+        torch.cuda.empty_cache()
     if not args.no_prefill:
         prefill = run_prefill(args, rank, world, dev)
         torch.cuda.empty_cache()
@@ -1133,6 +1210,7 @@ def run_b200(args, rank, world):
             "ragged": ragged,
             "small": small,
             "out_projection": out_proj,
+            "qkv_projection": qkv_proj,
         }
         print(json.dumps(line), flush=True)
     graph.reset()
@@ -1150,6 +1228,7 @@ def main():
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-5 ragged decode sub-measurement")
     ap.add_argument("--no-small", action="store_true", help="skip the config-1/2 (latency-bound) sub-measurement")
     ap.add_argument("--no-out-proj", action="store_true", help="skip the attention output projection measurement")
+    ap.add_argument("--no-qkv-proj", action="store_true", help="skip the QKV projection (+ RoPE/append) measurement")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
                          "all-gather of the rank partials and a merge kernel")

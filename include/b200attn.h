@@ -440,6 +440,43 @@ int b2_launch_attention_out_projection_decode(const void* d_in, void* d_out, con
                                               size_t hidden_size, size_t num_heads, size_t head_dim,
                                               float beta, b2_stream_t stream);
 
+/* include/kernels/kernels.hpp:29-36 launch_qkv_gemm
+ * (src/kernels/qkv_gemm.hip.cpp:7-100): qkv[t][n] = sum_k in[t][k] * w[n][k]
+ * for t < seq_len, n < total_qkv_dim, k < hidden_size; in the normed hidden
+ * states [seq][hidden], w the fused projection [total_qkv_dim][hidden] (Q, K,
+ * V weights stacked, PyTorch [out, in]), qkv [seq][total_qkv_dim] = the
+ * [t][Q | K | V] rows. FP16 in and out, FP32 accumulation; the same kernels
+ * and shape rules as b2_launch_attention_out_projection with beta 0. Adds a
+ * stream (the reference uses the rocBLAS handle's). */
+int b2_launch_qkv_gemm(const void* d_input_norm, void* d_qkv_out, const void* d_qkv_weights,
+                       size_t seq_len, size_t hidden_size, size_t total_qkv_dim, b2_stream_t stream);
+
+/* include/kernels/kernels.hpp:38-44 launch_qkv_decode
+ * (src/kernels/qkv_gemm.hip.cpp:102-115): the same for one token, the GEMV of
+ * b2_launch_attention_out_projection_decode (weights read before the
+ * dependency wait). */
+int b2_launch_qkv_decode(const void* d_input_norm, void* d_qkv_out, const void* d_qkv_weights,
+                         size_t hidden_size, size_t total_qkv_dim, b2_stream_t stream);
+
+/* launch_qkv_gemm followed by launch_rope_and_store_kv on its output, the
+ * engine's two steps (include/model_inference.hpp:266-281, q/k/v strides
+ * total_qkv_dim = (num_heads + 2 * num_kv_heads) * head_dim), in one kernel:
+ * the RoPE and the cache append run in the GEMM epilogue on the FP16-rounded
+ * products. Afterwards qkv holds rotated Q and K, V as projected (exactly
+ * the state the two calls leave), and the caches hold rotated K and V at rows
+ * start_pos..start_pos + seq_len - 1; every value is bit-identical to the two
+ * calls'. apply_rotary false: a NoPE layer (Q untouched, K stored as is).
+ * Fused when seq_len > 1, head_dim is 64, 128 or 256, num_heads * head_dim
+ * and num_kv_heads * head_dim are multiples of 256, hidden_size a multiple of
+ * 64 and every pointer 16-byte aligned; other shapes (one token among them:
+ * the GEMV) run the two launches.
+ * seq_len 0: B2_NOTHING_TO_DO. */
+int b2_launch_qkv_gemm_rope_store_kv(const void* d_input_norm, void* d_qkv_out, const void* d_qkv_weights,
+                                     void* d_k_cache, void* d_v_cache, const void* d_cos, const void* d_sin,
+                                     size_t seq_len, size_t hidden_size, size_t num_heads,
+                                     size_t num_kv_heads, size_t head_dim, size_t start_pos,
+                                     bool apply_rotary, b2_stream_t stream);
+
 /* ---- Decode without a caller workspace ------------------------------------
  * No counterpart in the reference (whose decode launchers always take the
  * three partial arrays). For callers that cannot provide scratch memory: a

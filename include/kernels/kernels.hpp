@@ -124,6 +124,36 @@ inline void update_causal_attention_decode_node(hipGraphExec_t graph_exec, hipGr
                     "update_causal_attention_decode_node");
 }
 
+
+// kernels.hpp:29-36 (plus a stream; the reference's rocBLAS call uses the
+// handle's)
+inline void launch_qkv_gemm(const __half* d_input_norm, __half* d_qkv_out, const __half* d_qkv_weights,
+                            size_t seq_len, size_t hidden_size, size_t total_qkv_dim, hipStream_t stream = nullptr) {
+    b200attn::check(b2_launch_qkv_gemm(d_input_norm, d_qkv_out, d_qkv_weights, seq_len, hidden_size, total_qkv_dim,
+                                       b200attn::detail::s(stream)),
+                    "launch_qkv_gemm");
+}
+
+// kernels.hpp:38-44
+inline void launch_qkv_decode(const __half* d_input_norm, __half* d_qkv_out, const __half* d_qkv_weights,
+                              size_t hidden_size, size_t total_qkv_dim, hipStream_t stream = nullptr) {
+    b200attn::check(b2_launch_qkv_decode(d_input_norm, d_qkv_out, d_qkv_weights, hidden_size, total_qkv_dim,
+                                         b200attn::detail::s(stream)),
+                    "launch_qkv_decode");
+}
+
+// launch_qkv_gemm + launch_rope_and_store_kv (model_inference.hpp:266-281) in
+// one kernel; no counterpart in the reference's header.
+inline void launch_qkv_gemm_rope_store_kv(const __half* d_input_norm, __half* d_qkv_out, const __half* d_qkv_weights,
+                                          __half* d_k_cache, __half* d_v_cache, const __half* d_cos,
+                                          const __half* d_sin, size_t seq_len, size_t hidden_size, size_t num_heads,
+                                          size_t num_kv_heads, size_t head_dim, size_t start_pos = 0,
+                                          bool apply_rotary = true, hipStream_t stream = nullptr) {
+    b200attn::check(b2_launch_qkv_gemm_rope_store_kv(d_input_norm, d_qkv_out, d_qkv_weights, d_k_cache, d_v_cache,
+                                                     d_cos, d_sin, seq_len, hidden_size, num_heads, num_kv_heads,
+                                                     head_dim, start_pos, apply_rotary, b200attn::detail::s(stream)),
+                    "launch_qkv_gemm_rope_store_kv");
+}
 // kernels.hpp:168-177 (the stream parameter is an addition)
 inline void launch_attention_out_projection(const __half* d_in, __half* d_out, const __half* d_o_proj_weights,
                                             size_t seq_len, size_t hidden_size, size_t num_heads, size_t head_dim,

@@ -66,6 +66,9 @@ SIGNATURES: dict[str, tuple] = {
         I, [P, S, P, P, S, P, P, S, P, P, S, B, P, S, P, S, S, S, S, S, P, S, P]),
     "b2_launch_attention_out_projection": (I, [P, P, P, S, S, S, S, ctypes.c_float, P]),
     "b2_launch_attention_out_projection_decode": (I, [P, P, P, S, S, S, ctypes.c_float, P]),
+    "b2_launch_qkv_gemm": (I, [P, P, P, S, S, S, P]),
+    "b2_launch_qkv_decode": (I, [P, P, P, S, S, P]),
+    "b2_launch_qkv_gemm_rope_store_kv": (I, [P, P, P, P, P, P, P, S, S, S, S, S, S, B, P]),
     "b2_launch_decode_step_fused_rank_partial": (
         I, [P, P, P, P, P, P, P, S, B, P, P, ctypes.c_int32, S, P, P, P, P, S, S, S, S, P]),
 }

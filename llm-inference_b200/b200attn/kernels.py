@@ -29,6 +29,7 @@ __all__ = [
     "launch_rope_and_store_kv_ragged", "decode_ragged_workspace_bytes", "launch_causal_attention_decode_ragged",
     "decode_exchange_bytes", "launch_decode_step_fused_exchange", "ExchangeBuffers",
     "launch_decode_step_ragged_fused", "launch_attention_out_projection", "launch_attention_out_projection_decode",
+    "launch_qkv_gemm", "launch_qkv_decode", "launch_qkv_gemm_rope_store_kv",
 ]
 
 
@@ -366,3 +367,27 @@ def launch_attention_out_projection_decode(d_in, d_out, d_o_proj_weights, hidden
     check(lib().b2_launch_attention_out_projection_decode(
         _ptr(d_in), _ptr(d_out), _ptr(d_o_proj_weights), hidden_size, num_heads, head_dim, float(beta),
         _stream(stream)), "launch_attention_out_projection_decode")
+
+
+def launch_qkv_gemm(d_input_norm, d_qkv_out, d_qkv_weights, seq_len, hidden_size, total_qkv_dim, stream=None):
+    """kernels.hpp:29-36 (plus a stream): qkv = input @ W_qkv^T."""
+    check(lib().b2_launch_qkv_gemm(_ptr(d_input_norm), _ptr(d_qkv_out), _ptr(d_qkv_weights), seq_len, hidden_size,
+                                   total_qkv_dim, _stream(stream)), "launch_qkv_gemm")
+
+
+def launch_qkv_decode(d_input_norm, d_qkv_out, d_qkv_weights, hidden_size, total_qkv_dim, stream=None):
+    """kernels.hpp:38-44: one token, qkv = W_qkv @ input."""
+    check(lib().b2_launch_qkv_decode(_ptr(d_input_norm), _ptr(d_qkv_out), _ptr(d_qkv_weights), hidden_size,
+                                     total_qkv_dim, _stream(stream)), "launch_qkv_decode")
+
+
+def launch_qkv_gemm_rope_store_kv(d_input_norm, d_qkv_out, d_qkv_weights, d_k_cache, d_v_cache, d_cos, d_sin,
+                                  seq_len, hidden_size, num_heads, num_kv_heads, head_dim, start_pos=0,
+                                  apply_rotary=True, stream=None):
+    """launch_qkv_gemm then launch_rope_and_store_kv on its rows
+    (include/model_inference.hpp:266-281) as one kernel, bit-identical to the
+    two calls."""
+    check(lib().b2_launch_qkv_gemm_rope_store_kv(
+        _ptr(d_input_norm), _ptr(d_qkv_out), _ptr(d_qkv_weights), _ptr(d_k_cache), _ptr(d_v_cache), _ptr(d_cos),
+        _ptr(d_sin), seq_len, hidden_size, num_heads, num_kv_heads, head_dim, start_pos, bool(apply_rotary),
+        _stream(stream)), "launch_qkv_gemm_rope_store_kv")

@@ -25,8 +25,8 @@ int clear_device_error_decode();
 int clear_device_error_prefill();
 unsigned int device_error_ragged();
 int clear_device_error_ragged();
-unsigned int device_error_outproj();
-int clear_device_error_outproj();
+unsigned int device_error_proj();
+int clear_device_error_proj();
 
 // Turn the launch status of the kernel just enqueued into a b2 status.
 inline int launch_status() {
@@ -86,6 +86,32 @@ int node_kernel_params(cudaGraphNode_t node, const void* const* expected, int n_
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Rotate-half RoPE of 8 pairs: lo holds x[i..i+8) of a head, hi holds
+// x[i+d/2..i+d/2+8), cv/sv the fp16 cos/sin of frequencies i..i+8. fp32
+// x0*c - x1*s and x1*c + x0*s with every product and sum rounded separately
+// (no FMA contraction), then round-to-nearest fp16: the reference's
+// arithmetic (src/kernels/rope.hip.cpp:61-134), bit-identical to the CPU
+// oracle evaluated the same way.
+__device__ __forceinline__ void rot8_pairs(uint4& lo, uint4& hi, uint4 cv, uint4 sv) {
+    uint32_t* L = reinterpret_cast<uint32_t*>(&lo);
+    uint32_t* Hh = reinterpret_cast<uint32_t*>(&hi);
+    const uint32_t* C = reinterpret_cast<const uint32_t*>(&cv);
+    const uint32_t* S = reinterpret_cast<const uint32_t*>(&sv);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&L[w]));
+        const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&Hh[w]));
+        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&C[w]));
+        const float2 sn = __half22float2(*reinterpret_cast<const __half2*>(&S[w]));
+        const float a0 = __fsub_rn(__fmul_rn(x0.x, c.x), __fmul_rn(x1.x, sn.x));
+        const float a1 = __fsub_rn(__fmul_rn(x0.y, c.y), __fmul_rn(x1.y, sn.y));
+        const float b0 = __fadd_rn(__fmul_rn(x1.x, c.x), __fmul_rn(x0.x, sn.x));
+        const float b1 = __fadd_rn(__fmul_rn(x1.y, c.y), __fmul_rn(x0.y, sn.y));
+        L[w] = pack_half2(a0, a1);
+        Hh[w] = pack_half2(b0, b1);
+    }
 }
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {

@@ -73,14 +73,14 @@ uint64_t b2_kernel_launch_count(void) { return b2::g_launches.load(); }
 
 unsigned int b2_device_error_word(void) {
     return b2::device_error_decode() | b2::device_error_prefill() | b2::device_error_ragged() |
-           b2::device_error_outproj();
+           b2::device_error_proj();
 }
 
 int b2_clear_device_error_word(void) {
     int st = b2::clear_device_error_decode();
     if (st == B2_OK) st = b2::clear_device_error_prefill();
     if (st == B2_OK) st = b2::clear_device_error_ragged();
-    return st != B2_OK ? st : b2::clear_device_error_outproj();
+    return st != B2_OK ? st : b2::clear_device_error_proj();
 }
 
 int b2_fill_rope_tables(size_t max_seq_len, size_t head_dim, float rope_theta,

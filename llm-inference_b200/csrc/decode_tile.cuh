@@ -79,28 +79,6 @@ __device__ __forceinline__ void load_q_frags(const __half* q, uint32_t kvh, uint
     }
 }
 
-// Rotate 8 pairs (x[i..i+8), x[i+64..i+72)) with fp32 products and sums rounded
-// separately, as the RoPE kernel and the CPU oracle do.
-__device__ __forceinline__ void rot8_pairs(uint4& lo, uint4& hi, uint4 cv, uint4 sv) {
-    uint32_t* L = reinterpret_cast<uint32_t*>(&lo);
-    uint32_t* Hh = reinterpret_cast<uint32_t*>(&hi);
-    const uint32_t* C = reinterpret_cast<const uint32_t*>(&cv);
-    const uint32_t* S = reinterpret_cast<const uint32_t*>(&sv);
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&L[w]));
-        const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&Hh[w]));
-        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&C[w]));
-        const float2 sn = __half22float2(*reinterpret_cast<const __half2*>(&S[w]));
-        const float a0 = __fsub_rn(__fmul_rn(x0.x, c.x), __fmul_rn(x1.x, sn.x));
-        const float a1 = __fsub_rn(__fmul_rn(x0.y, c.y), __fmul_rn(x1.y, sn.y));
-        const float b0 = __fadd_rn(__fmul_rn(x1.x, c.x), __fmul_rn(x0.x, sn.x));
-        const float b1 = __fadd_rn(__fmul_rn(x1.y, c.y), __fmul_rn(x0.y, sn.y));
-        L[w] = pack_half2(a0, a1);
-        Hh[w] = pack_half2(b0, b1);
-    }
-}
-
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

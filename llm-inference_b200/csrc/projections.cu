@@ -1,24 +1,40 @@
-// Attention output projection, the consumer of the attention path
+// The two projections either side of the attention path, as persistent
+// tcgen05 GEMMs with fused epilogues (FP16 in and out, FP32 accumulation):
+//
+// QKV projection, the producer (src/kernels/qkv_gemm.hip.cpp:7-115,
+// launch_qkv_gemm / launch_qkv_decode): qkv[t][n] = sum_k x[t][k] W[n][k],
+// x [seq][hidden] (the normed hidden states), W [q_dim + 2 kv_dim][hidden]
+// (Q, then K, then V weights, PyTorch [out, in]), qkv [seq][q_dim + 2 kv_dim]
+// -- the [t][Q | K | V] rows the RoPE/append and prefill kernels read. The
+// fused form also does the engine's next step, launch_rope_and_store_kv
+// (include/model_inference.hpp:266-281), in the GEMM epilogue: each output
+// element is rounded to FP16 as the plain GEMM stores it, Q is rotated in
+// place, K is kept as is in the row and rotated into the cache row start_pos
+// + t, V is copied to its cache row. The result is bit-identical to the plain
+// GEMM followed by the RoPE/append kernel, without the second pass over the
+// rows.
+//
+// Attention output projection, the consumer
 // (src/kernels/attention_out_projection.hip.cpp:8-58, launch_attention_out_
 // projection and its decode form): out[t][n] = sum_k attn[t][k] W[n][k] +
 // beta * out[t][n], attn [seq][num_heads * head_dim] (the packed rows the
-// prefill and decode kernels write), W [hidden][num_heads * head_dim]
-// (PyTorch [out, in]), out [seq][hidden] holding the residual on entry when
-// beta != 0. FP16 in and out, FP32 accumulation. beta == 0 never reads out.
+// prefill and decode kernels write), W [hidden][num_heads * head_dim], out
+// [seq][hidden] holding the residual on entry when beta != 0. beta == 0 never
+// reads out.
 //
-// Prefill (seq > 1): a persistent tcgen05 GEMM. Output tiles of 128 tokens x
-// 256 hidden columns, K in 64-element steps. Warp 0 streams A (attn) and B
-// (W) tiles with tensor-map copies into a 4-stage ring (128-byte swizzle,
-// 48 KB a stage); warp 1 issues tcgen05.mma (M 128, N 256, K 16; f16 in,
-// f32 accumulate) into one of two 256-column TMEM accumulators; warps 4-7
-// drain the other accumulator (tcgen05.ld, + beta * residual, fp16 stores)
-// while the next tile's MMAs run. Both operands K-major, as the reference's
-// rocBLAS call (transpose W, keep X).
+// Prefill (seq > 1): output tiles of 128 tokens x 256 columns, K in
+// 64-element steps. Warp 0 streams A (activations) and B (weights) tiles with
+// tensor-map copies into a 4-stage ring (128-byte swizzle, 48 KB a stage);
+// warp 1 issues tcgen05.mma (M 128, N 256, K 16; f16 in, f32 accumulate) into
+// one of two 256-column TMEM accumulators; warps 4-7 drain the other
+// accumulator through the epilogue while the next tile's MMAs run. Both
+// operands K-major, as the reference's rocBLAS calls (transpose W, keep X).
 // Decode (seq 1): a bandwidth-bound GEMV (the reference's
 // launch_matrix_vector_mul), one warp per output row, 16-byte loads of W
 // issued before the dependency wait.
-// Other shapes (hidden not a multiple of 256, K not a multiple of 64,
-// unaligned rows) take a plain SIMT kernel.
+// Other shapes (N not a multiple of 256, K not a multiple of 64, unaligned
+// rows) take a plain SIMT kernel; a QKV shape the fused epilogue does not
+// cover takes the GEMM followed by the RoPE/append kernel.
 #include <math.h>
 
 #include <atomic>
@@ -44,7 +60,16 @@ struct GemmArgs {
     uint32_t M, N, K;
     uint32_t tiles_m, tiles_n;
     float beta;
+    // QKV epilogue: out = the [t][Q | K | V] rows, N = q_dim + 2 kv_dim
+    __half* k_cache;    // [max_seq][kv_dim], row start_pos + t
+    __half* v_cache;
+    const __half* cos;  // [max_seq][head_dim / 2]
+    const __half* sin;
+    uint32_t q_dim, kv_dim, head_dim, start_pos;
+    uint32_t rotate;    // 0 = NoPE layer: K stored as is
 };
+
+enum : int { kEpiResidual = 0, kEpiQkvRope = 1 };
 
 struct GemmBars {
     uint64_t full[kStages], empty[kStages];
@@ -53,9 +78,92 @@ struct GemmBars {
     uint32_t abort;
 };
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    out_proj_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                         const GemmArgs g) {
+// Stores of 32 FP16 values (4 x 16 B) of one output row.
+__device__ __forceinline__ void store32(__half* dst, const uint4 (&v)[4]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = v[i];
+}
+
+// 32 accumulator columns rounded to FP16, as the GEMM stores them.
+__device__ __forceinline__ void round32(const uint32_t (&raw)[32], uint4 (&v)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        v[i] = make_uint4(pack_half2(__uint_as_float(raw[8 * i]), __uint_as_float(raw[8 * i + 1])),
+                          pack_half2(__uint_as_float(raw[8 * i + 2]), __uint_as_float(raw[8 * i + 3])),
+                          pack_half2(__uint_as_float(raw[8 * i + 4]), __uint_as_float(raw[8 * i + 5])),
+                          pack_half2(__uint_as_float(raw[8 * i + 6]), __uint_as_float(raw[8 * i + 7])));
+}
+
+// QKV epilogue of one accumulator tile (256 columns starting at n0, all of Q,
+// all of K or all of V since q_dim and kv_dim are multiples of 256) for this
+// thread's row: the steps of launch_rope_and_store_kv
+// (src/kernels/rope.hip.cpp:61-134) on the rounded GEMM outputs. A rotated
+// head is taken 32 frequency pairs at a time: columns [c, c + 32) and
+// [c + d/2, c + d/2 + 32) of the head, with cos/sin of frequencies c..c+32 at
+// the row's position.
+__device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& g, uint32_t tacc, uint32_t row, uint32_t n0,
+                                                  bool live) {
+    __half* qrow = g.out + static_cast<uint64_t>(row) * g.N + n0;
+    const bool is_q = n0 < g.q_dim;
+    const bool is_k = !is_q && n0 < g.q_dim + g.kv_dim;
+    const uint64_t pos = static_cast<uint64_t>(g.start_pos) + row;
+    __half* crow = nullptr;
+    if (!is_q)
+        crow = (is_k ? g.k_cache : g.v_cache) + pos * g.kv_dim + (n0 - g.q_dim - (is_k ? 0u : g.kv_dim));
+    if (g.rotate && (is_q || is_k)) {
+        const uint32_t hd = g.head_dim >> 1;
+        const __half* cs = g.cos + pos * hd;
+        const __half* sn = g.sin + pos * hd;
+#pragma unroll 1
+        for (uint32_t hb = 0; hb < kBN; hb += g.head_dim) {
+#pragma unroll 1
+            for (uint32_t c = 0; c < hd; c += 32) {
+                uint4 cv[4], sv[4];
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        cv[i] = __ldg(reinterpret_cast<const uint4*>(cs + c) + i);
+                        sv[i] = __ldg(reinterpret_cast<const uint4*>(sn + c) + i);
+                    }
+                }
+                uint32_t lo_raw[32], hi_raw[32];
+                tc::tmem_ld32(tacc + hb + c, lo_raw);
+                tc::tmem_ld32(tacc + hb + hd + c, hi_raw);
+                tc::tmem_wait_ld();
+                if (!live) continue;
+                uint4 lo[4], hi[4];
+                round32(lo_raw, lo);
+                round32(hi_raw, hi);
+                if (is_k) {  // the row keeps K as the GEMM wrote it
+                    store32(qrow + hb + c, lo);
+                    store32(qrow + hb + hd + c, hi);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) rot8_pairs(lo[i], hi[i], cv[i], sv[i]);
+                __half* dst = is_q ? qrow : crow;
+                store32(dst + hb + c, lo);
+                store32(dst + hb + hd + c, hi);
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (uint32_t c = 0; c < kBN; c += 32) {
+            uint32_t raw[32];
+            tc::tmem_ld32(tacc + c, raw);
+            tc::tmem_wait_ld();
+            if (!live) continue;
+            uint4 v[4];
+            round32(raw, v);
+            store32(qrow + c, v);
+            if (crow) store32(crow + c, v);
+        }
+    }
+}
+
+template <int kEpi>
+__device__ __forceinline__ void proj_gemm_body(const CUtensorMap* map_a, const CUtensorMap* map_b,
+                                               const GemmArgs& g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     GemmBars* bars = reinterpret_cast<GemmBars*>(smem + kStages * kStageBytes);
@@ -84,8 +192,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            tc::prefetch_tensormap(&map_a);
-            tc::prefetch_tensormap(&map_b);
+            tc::prefetch_tensormap(map_a);
+            tc::prefetch_tensormap(map_b);
             uint32_t i = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
@@ -97,8 +205,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (r > 0 && !(ok = mbar_wait(&bars->empty[s], (r - 1) & 1))) break;
                     uint8_t* st = smem + s * kStageBytes;
                     mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
-                    tc::tma_load_3d(st, &map_a, static_cast<int32_t>(kb * kBK), m0, 0, &bars->full[s]);
-                    tc::tma_load_3d(st + kABytes, &map_b, static_cast<int32_t>(kb * kBK), n0, 0, &bars->full[s]);
+                    tc::tma_load_3d(st, map_a, static_cast<int32_t>(kb * kBK), m0, 0, &bars->full[s]);
+                    tc::tma_load_3d(st + kABytes, map_b, static_cast<int32_t>(kb * kBK), n0, 0, &bars->full[s]);
                 }
             }
             if (!ok) bars->abort = 1;
@@ -145,38 +253,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint64_t base = static_cast<uint64_t>(row) * g.N + n0;
             if (!(ok = mbar_wait(&bars->acc_full[buf], (t >> 1) & 1))) break;
             tc::fence_after_sync();
+            if constexpr (kEpi == kEpiQkvRope) {
+                qkv_rope_epilogue(g, tbase + lane_addr + buf * kBN, row, n0, live);
+            } else {
 #pragma unroll 1
-            for (uint32_t half = 0; half < 2; ++half) {
-                // this half's 128 residual values in flight before the TMEM loads
-                uint4 res[16];
-                if (g.beta != 0.f && live) {
+                for (uint32_t half = 0; half < 2; ++half) {
+                    // this half's 128 residual values in flight before the TMEM loads
+                    uint4 res[16];
+                    if (g.beta != 0.f && live) {
 #pragma unroll
-                    for (int v = 0; v < 16; ++v)
-                        res[v] = *reinterpret_cast<const uint4*>(g.residual + base + half * 128 + v * 8);
-                }
-#pragma unroll
-                for (uint32_t c = 0; c < 4; ++c) {
-                    uint32_t raw[32];
-                    tc::tmem_ld32(tbase + lane_addr + buf * kBN + half * 128 + c * 32, raw);
-                    tc::tmem_wait_ld();
-                    uint32_t o16[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        float lo = __uint_as_float(raw[2 * j]), hi = __uint_as_float(raw[2 * j + 1]);
-                        if (g.beta != 0.f && live) {
-                            const uint32_t w = (&res[c * 4].x)[j];
-                            const __half2 r2 = *reinterpret_cast<const __half2*>(&w);
-                            const float2 rf = __half22float2(r2);
-                            lo = fmaf(g.beta, rf.x, lo);
-                            hi = fmaf(g.beta, rf.y, hi);
-                        }
-                        o16[j] = pack_half2(lo, hi);
+                        for (int v = 0; v < 16; ++v)
+                            res[v] = *reinterpret_cast<const uint4*>(g.residual + base + half * 128 + v * 8);
                     }
-                    if (live) {
-                        uint4* dst = reinterpret_cast<uint4*>(g.out + base + half * 128 + c * 32);
 #pragma unroll
-                        for (int v = 0; v < 4; ++v)
-                            dst[v] = make_uint4(o16[4 * v], o16[4 * v + 1], o16[4 * v + 2], o16[4 * v + 3]);
+                    for (uint32_t c = 0; c < 4; ++c) {
+                        uint32_t raw[32];
+                        tc::tmem_ld32(tbase + lane_addr + buf * kBN + half * 128 + c * 32, raw);
+                        tc::tmem_wait_ld();
+                        uint32_t o16[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            float lo = __uint_as_float(raw[2 * j]), hi = __uint_as_float(raw[2 * j + 1]);
+                            if (g.beta != 0.f && live) {
+                                const uint32_t w = (&res[c * 4].x)[j];
+                                const __half2 r2 = *reinterpret_cast<const __half2*>(&w);
+                                const float2 rf = __half22float2(r2);
+                                lo = fmaf(g.beta, rf.x, lo);
+                                hi = fmaf(g.beta, rf.y, hi);
+                            }
+                            o16[j] = pack_half2(lo, hi);
+                        }
+                        if (live) {
+                            uint4* dst = reinterpret_cast<uint4*>(g.out + base + half * 128 + c * 32);
+#pragma unroll
+                            for (int v = 0; v < 4; ++v)
+                                dst[v] = make_uint4(o16[4 * v], o16[4 * v + 1], o16[4 * v + 2], o16[4 * v + 3]);
+                        }
                     }
                 }
             }
@@ -192,6 +304,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc::fence_after_sync();
         tc::tmem_dealloc(tbase, 512);
     }
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    out_proj_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const GemmArgs g) {
+    proj_gemm_body<kEpiResidual>(&map_a, &map_b, g);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    qkv_rope_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const GemmArgs g) {
+    proj_gemm_body<kEpiQkvRope>(&map_a, &map_b, g);
 }
 
 // Decode GEMV: out[n] = W[n] . x + beta * out[n], one warp per row, K a
@@ -278,10 +402,21 @@ int ensure_gemm_smem() {
     if (cudaGetDevice(&dev) != cudaSuccess) return B2_ERR_CUDA;
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load() & bit) return B2_OK;
-    const int st =
+    int st =
         cuda_status(cudaFuncSetAttribute(out_proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+    if (st == B2_OK)
+        st = cuda_status(
+            cudaFuncSetAttribute(qkv_rope_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
     if (st == B2_OK) done.fetch_or(bit);
     return st;
+}
+
+// Tensor maps of the two K-major operands: activations [M][K], weights [N][K].
+int gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const __half* x, const __half* w, size_t M, size_t N, size_t K) {
+    if (encode_tensor_map_3d_f16(ma, x, K, M, 1, K * 2, 0, kBK, kBM) != 0 ||
+        encode_tensor_map_3d_f16(mb, w, K, N, 1, K * 2, 0, kBK, kBN) != 0)
+        return B2_ERR_UNSUPPORTED;
+    return B2_OK;
 }
 
 int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, size_t N, size_t K, float beta,
@@ -302,9 +437,7 @@ int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, si
         int st = ensure_gemm_smem();
         if (st != B2_OK) return st;
         CUtensorMap ma, mb;
-        if (encode_tensor_map_3d_f16(&ma, x, K, M, 1, K * 2, 0, kBK, kBM) != 0 ||
-            encode_tensor_map_3d_f16(&mb, w, K, N, 1, K * 2, 0, kBK, kBN) != 0)
-            return B2_ERR_UNSUPPORTED;
+        if ((st = gemm_maps(&ma, &mb, x, w, M, N, K)) != B2_OK) return st;
         GemmArgs g{};
         g.residual = out;
         g.out = out;
@@ -323,15 +456,71 @@ int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, si
                       x, w, out, m, n, k, beta);
 }
 
+// launch_qkv_gemm + launch_rope_and_store_kv in one kernel where the epilogue
+// covers the shape (more than one token; head_dim 64, 128 or 256; q_dim and
+// kv_dim multiples of the 256-column tile; K a multiple of 64; 16-byte
+// aligned operands), else the two launches.
+int launch_qkv_rope(const void* d_in, void* d_qkv, const void* d_w, void* d_k_cache, void* d_v_cache,
+                    const void* d_cos, const void* d_sin, size_t M, size_t hidden, size_t H, size_t KVH, size_t d,
+                    size_t start_pos, bool rotate, cudaStream_t stream) {
+    if (M == 0) return B2_NOTHING_TO_DO;
+    if (!d_in || !d_qkv || !d_w || !d_k_cache || !d_v_cache || H == 0 || KVH == 0 || d == 0 || hidden == 0)
+        return B2_ERR_INVALID_ARG;
+    if (rotate && (!d_cos || !d_sin)) return B2_ERR_INVALID_ARG;
+    if (d % 2 != 0 || H % KVH != 0) return B2_ERR_INVALID_ARG;
+    const size_t q_dim = H * d, kv_dim = KVH * d, N = q_dim + 2 * kv_dim;
+    if (M > 0x7fffffffull || N > 0x7fffffffull || hidden > 0x7fffffffull || start_pos + M > 0x7fffffffull)
+        return B2_ERR_UNSUPPORTED;
+    // one token: the GEMV (a 128-row tile would stream the weights for one
+    // row's worth of work) and the RoPE kernel
+    const bool fused = M > 1 && (d == 64 || d == 128 || d == 256) && q_dim % kBN == 0 && kv_dim % kBN == 0 &&
+                       hidden % kBK == 0 && aligned16(d_in) && aligned16(d_w) && aligned16(d_qkv) &&
+                       aligned16(d_k_cache) && aligned16(d_v_cache) &&
+                       (!rotate || (aligned16(d_cos) && aligned16(d_sin)));
+    if (!fused) {
+        int st = launch_out_proj(d_in, d_qkv, d_w, M, N, hidden, 0.f, stream, false);
+        if (st != B2_OK) return st;
+        auto* qkv = static_cast<__half*>(d_qkv);
+        return b2_launch_rope_and_store_kv(qkv, qkv + q_dim, qkv + q_dim + kv_dim, d_k_cache, d_v_cache, d_cos, d_sin,
+                                           M, H, KVH, d, N, N, start_pos, rotate,
+                                           reinterpret_cast<b2_stream_t>(stream));
+    }
+    int st = ensure_gemm_smem();
+    if (st != B2_OK) return st;
+    CUtensorMap ma, mb;
+    if ((st = gemm_maps(&ma, &mb, static_cast<const __half*>(d_in), static_cast<const __half*>(d_w), M, N,
+                        hidden)) != B2_OK)
+        return st;
+    GemmArgs g{};
+    g.out = static_cast<__half*>(d_qkv);
+    g.M = static_cast<uint32_t>(M);
+    g.N = static_cast<uint32_t>(N);
+    g.K = static_cast<uint32_t>(hidden);
+    g.tiles_m = static_cast<uint32_t>((M + kBM - 1) / kBM);
+    g.tiles_n = static_cast<uint32_t>(N / kBN);
+    g.k_cache = static_cast<__half*>(d_k_cache);
+    g.v_cache = static_cast<__half*>(d_v_cache);
+    g.cos = static_cast<const __half*>(d_cos);
+    g.sin = static_cast<const __half*>(d_sin);
+    g.q_dim = static_cast<uint32_t>(q_dim);
+    g.kv_dim = static_cast<uint32_t>(kv_dim);
+    g.head_dim = static_cast<uint32_t>(d);
+    g.start_pos = static_cast<uint32_t>(start_pos);
+    g.rotate = rotate ? 1u : 0u;
+    const uint32_t tiles = g.tiles_m * g.tiles_n;
+    const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count()));
+    return launch_pdl(qkv_rope_gemm_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, stream, ma, mb, g);
+}
+
 }  // namespace
 
-unsigned int device_error_outproj() {
+unsigned int device_error_proj() {
     unsigned int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0;
     return v;
 }
 
-int clear_device_error_outproj() {
+int clear_device_error_proj() {
     const unsigned int zero = 0;
     return cuda_status(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
 }
@@ -350,4 +539,26 @@ extern "C" int b2_launch_attention_out_projection_decode(const void* d_in, void*
                                                          float beta, b2_stream_t stream) {
     return b2::launch_out_proj(d_in, d_out, d_o_proj_weights, 1, hidden_size, num_heads * head_dim, beta,
                                reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+extern "C" int b2_launch_qkv_gemm(const void* d_input_norm, void* d_qkv_out, const void* d_qkv_weights,
+                                  size_t seq_len, size_t hidden_size, size_t total_qkv_dim, b2_stream_t stream) {
+    return b2::launch_out_proj(d_input_norm, d_qkv_out, d_qkv_weights, seq_len, total_qkv_dim, hidden_size, 0.f,
+                               reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int b2_launch_qkv_decode(const void* d_input_norm, void* d_qkv_out, const void* d_qkv_weights,
+                                    size_t hidden_size, size_t total_qkv_dim, b2_stream_t stream) {
+    return b2::launch_out_proj(d_input_norm, d_qkv_out, d_qkv_weights, 1, total_qkv_dim, hidden_size, 0.f,
+                               reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+extern "C" int b2_launch_qkv_gemm_rope_store_kv(const void* d_input_norm, void* d_qkv_out, const void* d_qkv_weights,
+                                                void* d_k_cache, void* d_v_cache, const void* d_cos,
+                                                const void* d_sin, size_t seq_len, size_t hidden_size,
+                                                size_t num_heads, size_t num_kv_heads, size_t head_dim,
+                                                size_t start_pos, bool apply_rotary, b2_stream_t stream) {
+    return b2::launch_qkv_rope(d_input_norm, d_qkv_out, d_qkv_weights, d_k_cache, d_v_cache, d_cos, d_sin, seq_len,
+                               hidden_size, num_heads, num_kv_heads, head_dim, start_pos, apply_rotary,
+                               reinterpret_cast<cudaStream_t>(stream));
 }

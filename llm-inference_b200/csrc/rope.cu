@@ -96,26 +96,6 @@ __device__ __forceinline__ void rot2(float x0, float x1, float c, float s, float
     o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
 }
 
-// Rotate 8 pairs: lo holds x[i..i+8), hi holds x[half+i..half+i+8).
-__device__ __forceinline__ void rot8(uint4& lo, uint4& hi, uint4 cv, uint4 sv) {
-    uint32_t* L = reinterpret_cast<uint32_t*>(&lo);
-    uint32_t* H = reinterpret_cast<uint32_t*>(&hi);
-    const uint32_t* C = reinterpret_cast<const uint32_t*>(&cv);
-    const uint32_t* S = reinterpret_cast<const uint32_t*>(&sv);
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&L[w]));
-        const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&H[w]));
-        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&C[w]));
-        const float2 s = __half22float2(*reinterpret_cast<const __half2*>(&S[w]));
-        float a0, a1, b0, b1;
-        rot2(x0.x, x1.x, c.x, s.x, a0, b0);
-        rot2(x0.y, x1.y, c.y, s.y, a1, b1);
-        L[w] = pack_half2(a0, a1);
-        H[w] = pack_half2(b0, b1);
-    }
-}
-
 // Vectorised rotate (+ store) kernel: lanes = half_dim / 8.
 __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) {
     pdl_wait_primary();
@@ -146,7 +126,7 @@ __global__ void __launch_bounds__(256) rope_store_vec8_kernel(const RopeArgs a) 
             uint4 hi = *reinterpret_cast<const uint4*>(src + a.half_dim + e);
             const uint4 cv = __ldg(reinterpret_cast<const uint4*>(a.cos + pos * a.half_dim + e));
             const uint4 sv = __ldg(reinterpret_cast<const uint4*>(a.sin + pos * a.half_dim + e));
-            rot8(lo, hi, cv, sv);
+            rot8_pairs(lo, hi, cv, sv);
             *reinterpret_cast<uint4*>(dst + e) = lo;
             *reinterpret_cast<uint4*>(dst + a.half_dim + e) = hi;
         } else {

@@ -88,6 +88,7 @@ def _bits(a):
     (254, 2048, 16, 4, 128, 37, True),    # continued prompt: cache rows 37..290
     (1, 2048, 16, 4, 128, 600, True),     # one token through the GEMM tile path
     (2048, 2048, 16, 4, 128, 0, True),    # 16 M tiles x 12 N tiles: both TMEM accumulators
+    (8192, 2048, 16, 4, 128, 0, True),    # one config-3 sequence: 768 tiles, 5-6 per persistent CTA
     (130, 512, 8, 4, 64, 5, True),        # head_dim 64: four heads a tile
     (130, 512, 4, 1, 256, 5, True),       # head_dim 256: half a head pair a tile
     (67, 320, 6, 2, 64, 3, True),         # kv_dim 128: two launches (not a 256 multiple)

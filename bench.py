@@ -38,12 +38,17 @@ workload (one layer-step at the same kv_len per step), with the
 python/reference.py path on the same layer-step reported beside it, and
 prints the same line.
 
-N > 1 (torchrun): the 64K KV range of every layer is split into N contiguous
-ranges, one per rank; the rank holding the tail appends the new token; each
-rank reduces its range to one (o, m, l) partial per head and the partials are
-merged across ranks -- inside the fused kernel over CUDA-IPC peer memory
-(--exchange peer, default) or by an NCCL all-gather and a merge kernel
-(--exchange nccl). Strong scaling: total work fixed. Prefill shards
+N > 1 (torchrun): the config-4 decode is split by KV head (--decode-split
+heads, the default when the 4 KV heads divide or are divided by N): each rank
+owns whole GQA groups with only their cache and writes their heads' outputs,
+the layout a tensor-parallel o_proj consumes, with no exchange; at N = 8 the
+two ranks of each KV head also split its range. With --decode-split kv the
+64K KV range of every layer is split into N contiguous ranges, one per rank;
+the rank holding the tail appends the new token; each rank reduces its range
+to one (o, m, l) partial per head. Partials of a split range are merged across
+ranks inside the fused kernel over CUDA-IPC peer memory (--exchange peer,
+default) or by an NCCL all-gather and a merge kernel (--exchange nccl). Strong
+scaling: total work fixed. Prefill shards
 (sequence, KV head) units and the ragged decode shards whole sequences
 (weak in units, no exchange).
 """
@@ -1031,6 +1036,20 @@ def run_qkv_proj(args, dev):
             "clocks": clk, "gpu_launches": launches}
 
 
+def decode_parallelism(split, hs, h_l, exchange):
+    xch = ("cross-rank merge in the fused kernel over CUDA-IPC peer memory" if exchange == "peer"
+           else "NCCL all-gather of rank partials + merge kernel")
+    if split != "heads":
+        return f"kv-split{hs.world}, {xch}"
+    txt = (f"kv-heads over {hs.world} ranks: {hs.local_kv_heads} KV head(s) / {h_l} query heads per rank with only "
+           "those heads' cache, output head-sharded (the layout a tensor-parallel o_proj takes)")
+    if hs.group_world > 1:
+        txt += f"; each KV head's range split over {hs.group_world} ranks, {xch}"
+    else:
+        txt += ", no exchange"
+    return txt
+
+
 # --------------------------------------------------------------------------- GPU arm
 def run_b200(args, rank, world):
     import numpy as np
@@ -1040,31 +1059,50 @@ def run_b200(args, rank, world):
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    plan = bdist.split_kv_plan(PAST, world, rank)
+    split = args.decode_split
+    if split == "auto":
+        split = "heads" if world > 1 and (KVH % world == 0 or world % KVH == 0) else "kv"
+    # this rank's KV heads (all of them for the KV-range split) and the ranks
+    # that share them, which split the KV range among themselves
+    hs = (bdist.head_split_plan(KVH, world, rank) if split == "heads"
+          else bdist.HeadSplit(world, rank, KVH, 0, KVH, tuple(range(world))))
+    kvh_l = hs.local_kv_heads
+    h_l = kvh_l * (H // KVH)
+    q_l, kv_l = h_l * D, kvh_l * D
+    plan = bdist.split_kv_plan(PAST, hs.group_world, hs.group_rank)
     capacity = plan.local_capacity(args.warmup + args.steps + 1)   # local cache rows
     max_global = PAST + args.warmup + args.steps + 1
 
     # ---- state: KV cache (local slice), RoPE tables, per-layer QKV rows, outputs
     gen = torch.Generator(device=dev).manual_seed(SEED + rank)
-    cache = b200attn.KVCache(LAYERS, capacity, KVH, D, device=dev)
+    cache = b200attn.KVCache(LAYERS, capacity, kvh_l, D, device=dev)
     for l in range(LAYERS):
         for t in (cache.get_k_cache(l), cache.get_v_cache(l)):
             t.normal_(0.0, 0.5, generator=gen)
     cos, sin = b200attn.rope_tables_host(max_global, D, 5.0e6)
     d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
-    hgen = np.random.default_rng(SEED)     # identical Q/K/V rows on every rank
-    qkv_host = torch.from_numpy(hgen.standard_normal((LAYERS, QKV), dtype=np.float32).astype(np.float16)).pin_memory()
+    hgen = np.random.default_rng(SEED)     # identical Q/K/V rows on every rank; each takes its heads' slice
+    rows_full = hgen.standard_normal((LAYERS, QKV), dtype=np.float32).astype(np.float16)
+    qkv_host = torch.from_numpy(bdist.head_split_rows(rows_full, hs, H, D)).pin_memory()
     qkv = qkv_host.to(dev)
-    out = torch.zeros((LAYERS, Q_DIM), dtype=torch.float16, device=dev)
+    out = torch.zeros((LAYERS, q_l), dtype=torch.float16, device=dev)
     out_host = torch.zeros_like(out, device="cpu").pin_memory()
-    step_state = bdist.DecodeStepState(plan, H, KVH, D, LAYERS, capacity, max_global, dev, fused=not args.unfused,
-                                       exchange=args.exchange)
+    step_state = bdist.DecodeStepState(plan, h_l, kvh_l, D, LAYERS, capacity, max_global, dev, fused=not args.unfused,
+                                       exchange=args.exchange, members=hs.group, job_world=world,
+                                       job_kv_dim=KV_DIM, job_q_dim=Q_DIM)
 
     stream = torch.cuda.Stream(device=dev)
     group = None
     if world > 1:
         import torch.distributed as tdist
         group = tdist.group.WORLD
+        if hs.group_world < world:
+            # one process group per set of ranks sharing KV heads (every rank
+            # creates every group, in the same order)
+            for g0 in range(0, world, hs.group_world):
+                g = tdist.new_group(list(range(g0, g0 + hs.group_world)))
+                if rank in range(g0, g0 + hs.group_world):
+                    group = g
 
     def enqueue_step(s):
         bdist.enqueue_decode_step(step_state, cache, qkv, out, d_cos, d_sin, s, group)
@@ -1116,8 +1154,8 @@ def run_b200(args, rank, world):
     dec_ms = bdist.time_decode_launches(step_state, cache, qkv, out, stream, reps=3, d_cos=d_cos, d_sin=d_sin)
     kv_len_local = plan.local_len(PAST + 1)
     # K/V rows read, Q read, output written (+ the new K/V row read and appended)
-    dec_bytes = 2 * kv_len_local * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + (4 * KV_DIM * 2 if step_state.fused else 0)
-    if step_state.fused and (world == 1 or step_state.exchange == "peer"):
+    dec_bytes = 2 * kv_len_local * kv_l * 2 + q_l * 2 + q_l * 2 + (4 * kv_l * 2 if step_state.fused else 0)
+    if step_state.fused and (plan.world == 1 or step_state.exchange == "peer"):
         # Inside the captured step consecutive layers overlap (programmatic
         # dependent launch, L2 warm-up of the next layer's first tiles), so the
         # per-launch time is the timed region over its fused launches; the
@@ -1186,9 +1224,8 @@ def run_b200(args, rank, world):
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
             "data": "synthetic: KV ~N(0,0.5) (torch CUDA generator, seed 2024+rank), Q/K/V rows ~N(0,1) seeded",
             "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": PAST, "layers": LAYERS,
-                       "parallelism": (f"kv-split{world}, " + ("cross-rank merge in the fused kernel over CUDA-IPC "
-                                       "peer memory" if step_state.exchange == "peer" else "NCCL all-gather of rank "
-                                       "partials + merge kernel")) if world > 1 else "single-gpu",
+                       "parallelism": decode_parallelism(split, hs, h_l, step_state.exchange) if world > 1
+                       else "single-gpu",
                        "l2": "inputs larger than L2 (4.8 GB of KV per step)",
                        "step_graph": f"one CUDA graph per step, {launches_per_step} kernels"},
             "gpu_launches": launches_per_step * args.steps,
@@ -1229,6 +1266,8 @@ def main():
     ap.add_argument("--no-small", action="store_true", help="skip the config-1/2 (latency-bound) sub-measurement")
     ap.add_argument("--no-out-proj", action="store_true", help="skip the attention output projection measurement")
     ap.add_argument("--no-qkv-proj", action="store_true", help="skip the QKV projection (+ RoPE/append) measurement")
+    ap.add_argument("--decode-split", default="auto", choices=["auto", "heads", "kv"],
+                    help="N > 1 decode: by KV head (auto when the KV heads divide or are divided by N) or by KV range")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
                          "all-gather of the rank partials and a merge kernel")

@@ -3,11 +3,13 @@
 The reference engine is single-GPU (include/model_inference.hpp). Across the
 GPUs of one box the attention path shards where it naturally does:
 
-* long-context decode -- the KV sequence of every layer is split into
-  contiguous ranges, one per rank (`split_kv_plan`); the rank that holds the
-  tail appends the new token; every rank reduces its range to one (o, m, l)
-  partial per head, the partials are all-gathered (NCCL) and merged with the
-  reference's chunk-merge algebra;
+* long-context decode -- by KV head (`head_split_plan`: each rank owns whole
+  GQA groups and their cache, no exchange, the output head-sharded as a
+  tensor-parallel o_proj takes it), or by KV range (`split_kv_plan`: contiguous
+  ranges, the rank that holds the tail appends the new token, every rank
+  reduces its range to one (o, m, l) partial per head, the partials are
+  exchanged and merged with the reference's chunk-merge algebra), or both
+  when there are more ranks than KV heads;
 * batched prefill -- independent (sequence, KV head) units (`prefill_units`);
 * ragged decode -- whole sequences, longest first (`assign_sequences`).
 
@@ -55,6 +57,74 @@ def split_kv_plan(past: int, world: int, rank: int) -> SplitPlan:
     begin = rank * base + min(rank, rem)
     end = begin + base + (1 if rank < rem else 0)
     return SplitPlan(past, world, rank, begin, end)
+
+
+@dataclasses.dataclass(frozen=True)
+class HeadSplit:
+    """Rank `rank` of `world` decodes KV heads [kvh_begin, kvh_end) and their
+    query heads (GQA keeps each KV head's query group together), with its own
+    cache holding only those heads, as a tensor-parallel engine shards them.
+    When there are more ranks than KV heads, the `group` of ranks that share a
+    KV head also splits its KV range (split_kv_plan over the group) and merges
+    across the group."""
+    world: int
+    rank: int
+    num_kv_heads: int
+    kvh_begin: int
+    kvh_end: int
+    group: tuple
+
+    @property
+    def local_kv_heads(self) -> int:
+        return self.kvh_end - self.kvh_begin
+
+    @property
+    def group_world(self) -> int:
+        return len(self.group)
+
+    @property
+    def group_rank(self) -> int:
+        return self.group.index(self.rank)
+
+    def query_heads(self, num_heads: int) -> tuple[int, int]:
+        """Query heads [begin, end) of this rank's KV heads."""
+        per = num_heads // self.num_kv_heads
+        return self.kvh_begin * per, self.kvh_end * per
+
+
+def head_split_plan(num_kv_heads: int, world: int, rank: int) -> HeadSplit:
+    """KV heads over ranks: KVH / world heads each when world divides KVH;
+    one head per world / KVH ranks (which then split its KV range) when KVH
+    divides world."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    if num_kv_heads % world == 0:
+        per = num_kv_heads // world
+        return HeadSplit(world, rank, num_kv_heads, rank * per, (rank + 1) * per, (rank,))
+    if world % num_kv_heads == 0:
+        parts = world // num_kv_heads
+        g = rank // parts
+        return HeadSplit(world, rank, num_kv_heads, g, g + 1, tuple(g * parts + i for i in range(parts)))
+    raise ValueError(f"{num_kv_heads} KV heads cannot be split evenly over {world} ranks")
+
+
+def head_split_rows(rows, hs: HeadSplit, num_heads: int, head_dim: int):
+    """This rank's slice of [..][Q | K | V] rows (the row a tensor-parallel QKV
+    projection produces on it): its query heads, then its K heads, then its V
+    heads. Works on numpy arrays and torch tensors (last axis)."""
+    q0, q1 = hs.query_heads(num_heads)
+    kv = hs.num_kv_heads * head_dim
+    qd = num_heads * head_dim
+    k0, k1 = hs.kvh_begin * head_dim, hs.kvh_end * head_dim
+    parts = [rows[..., q0 * head_dim:q1 * head_dim], rows[..., qd + k0:qd + k1], rows[..., qd + kv + k0:qd + kv + k1]]
+    try:
+        import torch
+        if isinstance(rows, torch.Tensor):
+            return torch.cat(parts, dim=-1).contiguous()
+    except ImportError:
+        pass
+    import numpy as np
+    return np.ascontiguousarray(np.concatenate(parts, axis=-1))
 
 
 @dataclasses.dataclass(frozen=True)
@@ -126,7 +196,13 @@ class DecodeStepState:
     """Device-resident positions and workspaces for a graph-static decode step."""
 
     def __init__(self, plan: SplitPlan, num_heads, num_kv_heads, head_dim, num_layers, capacity, max_global,
-                 device, fused=True, exchange="peer"):
+                 device, fused=True, exchange="peer", members=None, job_world=None, job_kv_dim=None,
+                 job_q_dim=None):
+        """plan: the KV split among the ranks that share this rank's heads
+        (`members`, global ranks; default all ranks); num_heads / num_kv_heads
+        are this rank's. job_*: the whole job's world size and widths, for the
+        barrier, the max over ranks and the whole-job byte count (default: the
+        plan's world and these heads)."""
         import torch
         from . import kernels as K
         self.plan = plan
@@ -143,11 +219,14 @@ class DecodeStepState:
             import torch.distributed as tdist
 
             def gather(obj):
-                out = [None] * plan.world
+                out = [None] * tdist.get_world_size()
                 tdist.all_gather_object(out, obj)
-                return out
+                return out if members is None else [out[r] for r in members]
             self.xbuf = K.ExchangeBuffers(plan.world, plan.rank, num_heads, gather)
         self.H, self.KVH, self.D, self.L = num_heads, num_kv_heads, head_dim, num_layers
+        self.job_world = job_world or plan.world
+        self.job_kv_dim = job_kv_dim or num_kv_heads * head_dim
+        self.job_q_dim = job_q_dim or num_heads * head_dim
         self.capacity = capacity
         self.max_global = max_global
         self.device = device
@@ -355,7 +434,7 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         for s in range(warmup):
             step(s)
         torch.cuda.synchronize()
-        if st.plan.world > 1:
+        if st.job_world > 1:
             import torch.distributed as tdist
             tdist.barrier()
             torch.cuda.synchronize()
@@ -366,12 +445,14 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    if st.plan.world > 1:
+    if st.job_world > 1:
         ms = max_over_ranks(ms, qkv.device)
-    # whole-job bytes: every layer's full KV range (all ranks' shares)
-    nbytes = sum(L * (2 * (past + 1 + s) * kv_dim * 2 + q_dim * 2 * 2 + 2 * kv_dim * 2) for s in range(steps))
+    # whole-job bytes: every layer's full KV range (all ranks' shares, all heads)
+    jkv, jq = st.job_kv_dim, st.job_q_dim
+    nbytes = sum(L * (2 * (past + 1 + s) * jkv * 2 + jq * 2 * 2 + 2 * jkv * 2) for s in range(steps))
     h2d = int(qkv_host.numel() * 2) + (4 if mode == "fused" else 0)
-    fused_call = ("b2_launch_decode_step_fused" if st.plan.world == 1 else
+    fused_call = ("b2_launch_decode_step_fused" + (" on this rank's KV heads" if st.job_world > 1 else "")
+                  if st.plan.world == 1 else
                   "b2_launch_decode_step_fused_exchange (cross-rank merge over peer memory)"
                   if st.exchange == "peer" else
                   "b2_launch_decode_step_fused_rank_partial + NCCL all-gather + b2_launch_merge_partials_strided")

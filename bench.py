@@ -38,17 +38,17 @@ workload (one layer-step at the same kv_len per step), with the
 python/reference.py path on the same layer-step reported beside it, and
 prints the same line.
 
-N > 1 (torchrun): the config-4 decode is split by KV head (--decode-split
-heads, the default when the 4 KV heads divide or are divided by N): each rank
-owns whole GQA groups with only their cache and writes their heads' outputs,
-the layout a tensor-parallel o_proj consumes, with no exchange; at N = 8 the
-two ranks of each KV head also split its range. With --decode-split kv the
-64K KV range of every layer is split into N contiguous ranges, one per rank;
-the rank holding the tail appends the new token; each rank reduces its range
-to one (o, m, l) partial per head. Partials of a split range are merged across
-ranks inside the fused kernel over CUDA-IPC peer memory (--exchange peer,
-default) or by an NCCL all-gather and a merge kernel (--exchange nccl). Strong
-scaling: total work fixed. Prefill shards
+N > 1 (torchrun): the 64K KV range of every layer is split into N contiguous
+ranges, one per rank (--decode-split kv, default); the rank holding the tail
+appends the new token; each rank reduces its range to one (o, m, l) partial
+per head. Partials of a split range are merged across ranks inside the fused
+kernel over CUDA-IPC peer memory (--exchange peer, default) or by an NCCL
+all-gather and a merge kernel (--exchange nccl). --decode-split heads gives
+each rank whole GQA groups with only their cache and their heads' outputs
+(the layout a tensor-parallel o_proj consumes, no exchange; at N = 8 the two
+ranks of a KV head also split its range); it measures slower here, because
+one KV head per launch leaves the decode kernel's fixed cost on a quarter of
+the bytes. Strong scaling: total work fixed. Prefill shards
 (sequence, KV head) units and the ragged decode shards whole sequences
 (weak in units, no exchange).
 """
@@ -577,21 +577,31 @@ def run_ragged(args, rank, world, dev):
     import b200attn
     from b200attn import dist as bdist
     lens_all = [int(x) for x in np.random.default_rng(SEED).integers(512, RG_MAX + 1, RG_B)]
-    mine = bdist.assign_sequences(lens_all, world)[rank]
+    split = args.ragged_split
+    # by KV head: every rank decodes every sequence for its KV heads (its own
+    # cache of those heads); ranks sharing heads (world > KVH) split the
+    # sequences among themselves. By sequence: whole sequences per rank.
+    hs = (bdist.head_split_plan(KVH, world, rank) if split == "heads"
+          else bdist.HeadSplit(world, rank, KVH, 0, KVH, tuple(range(world))))
+    kvh_l = hs.local_kv_heads
+    h_l = kvh_l * (H // KVH)
+    q_l, kv_l = h_l * D, kvh_l * D
+    qkv_l = q_l + 2 * kv_l
+    mine = bdist.assign_sequences(lens_all, hs.group_world)[hs.group_rank]
     B = len(mine)
     lens = [lens_all[i] for i in mine]
     gen = torch.Generator(device=dev).manual_seed(SEED + 200 + rank)
-    cache = torch.empty((LAYERS, 2, B, RG_MAX, KV_DIM), dtype=torch.float16, device=dev)
+    cache = torch.empty((LAYERS, 2, B, RG_MAX, kv_l), dtype=torch.float16, device=dev)
     for l in range(LAYERS):
         for kv in range(2):
             for b in range(B):
                 cache[l, kv, b, :lens[b]].normal_(0.0, 1.0, generator=gen)
-    qkv = torch.empty((LAYERS, B, QKV), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
-    out = torch.empty((LAYERS, B, Q_DIM), dtype=torch.float16, device=dev)
+    qkv = torch.empty((LAYERS, B, qkv_l), dtype=torch.float16, device=dev).normal_(0.0, 1.0, generator=gen)
+    out = torch.empty((LAYERS, B, q_l), dtype=torch.float16, device=dev)
     cos, sin = b200attn.rope_tables_host(RG_MAX, D, 5.0e6)
     d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
     pos = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device=dev)   # the new token's row
-    ws_bytes = b200attn.decode_ragged_workspace_bytes(B, H, KVH, RG_MAX)
+    ws_bytes = b200attn.decode_ragged_workspace_bytes(B, h_l, kvh_l, RG_MAX)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
@@ -601,17 +611,17 @@ def run_ragged(args, rank, world, dev):
             rotate = (l + 1) % 4 != 0
             if args.unfused:
                 # the two-launch form: ragged RoPE/append, then the ragged decode
-                b200attn.launch_rope_and_store_kv_ragged(row, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], cache[l, 0],
-                                                         cache[l, 1], RG_MAX * KV_DIM, d_cos, d_sin, B, H, KVH, D,
-                                                         QKV, QKV, pos, RG_MAX, rotate, stream=st)
-                b200attn.launch_causal_attention_decode_ragged(row, QKV, cache[l, 0], cache[l, 1], RG_MAX * KV_DIM,
-                                                               pos, 1, RG_MAX, out[l], 0, B, H, KVH, D, ws, ws_bytes,
-                                                               stream=st)
+                b200attn.launch_rope_and_store_kv_ragged(row, row[:, q_l:], row[:, q_l + kv_l:], cache[l, 0],
+                                                         cache[l, 1], RG_MAX * kv_l, d_cos, d_sin, B, h_l, kvh_l, D,
+                                                         qkv_l, qkv_l, pos, RG_MAX, rotate, stream=st)
+                b200attn.launch_causal_attention_decode_ragged(row, qkv_l, cache[l, 0], cache[l, 1], RG_MAX * kv_l,
+                                                               pos, 1, RG_MAX, out[l], 0, B, h_l, kvh_l, D, ws,
+                                                               ws_bytes, stream=st)
             else:
-                b200attn.launch_decode_step_ragged_fused(row, QKV, row[:, Q_DIM:], row[:, Q_DIM + KV_DIM:], QKV,
-                                                         cache[l, 0], cache[l, 1], RG_MAX * KV_DIM, d_cos, d_sin,
-                                                         RG_MAX, rotate, pos, RG_MAX, out[l], 0, B, H, KVH, D, ws,
-                                                         ws_bytes, stream=st)
+                b200attn.launch_decode_step_ragged_fused(row, qkv_l, row[:, q_l:], row[:, q_l + kv_l:], qkv_l,
+                                                         cache[l, 0], cache[l, 1], RG_MAX * kv_l, d_cos, d_sin,
+                                                         RG_MAX, rotate, pos, RG_MAX, out[l], 0, B, h_l, kvh_l, D,
+                                                         ws, ws_bytes, stream=st)
 
     with torch.cuda.stream(stream):
         step(stream)
@@ -686,7 +696,8 @@ def run_ragged(args, rank, world, dev):
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
         cpu = cpu_config5(lens_all, os.cpu_count() or 1)
-    mine_layer = sum(seq_bytes(n) for n in lens)
+    seq_bytes_l = lambda n: 2 * n * kv_l * 2 + q_l * 2 + q_l * 2 + 2 * kv_l * 2
+    mine_layer = sum(seq_bytes_l(n) for n in lens)
     peak, peak_kind = load_peaks()
     launch_ms = ms / steps / LAYERS
     achieved = mine_layer / (launch_ms / 1e3) / 1e9
@@ -700,7 +711,11 @@ def run_ragged(args, rank, world, dev):
     return {"metric": "ragged decode KV-read GB/s", "value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "workload": RG_WORKLOAD, "steps": steps, "ms_per_step": round(ms / steps, 4),
             "gpu_launches": per_step * steps, "sequences_per_rank": B,
-            "parallelism": f"sequences over {world} GPU(s), greedy longest-first",
+            "parallelism": (f"sequences over {world} GPU(s), greedy longest-first" if split != "heads" else
+                            f"kv-heads over {world} GPU(s): {kvh_l} KV head(s) / {h_l} query heads of every "
+                            "sequence per rank (own cache of those heads, head-sharded output)"
+                            + (f", sequences split greedily over the {hs.group_world} ranks of each head"
+                               if hs.group_world > 1 else "")),
             "roofline": {"bound": "hbm",
                          "kernel": ("decode_ragged_kernel + merge_ragged_kernel (+ ragged RoPE/append kernel)"
                                     if args.unfused else
@@ -1060,8 +1075,6 @@ def run_b200(args, rank, world):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     split = args.decode_split
-    if split == "auto":
-        split = "heads" if world > 1 and (KVH % world == 0 or world % KVH == 0) else "kv"
     # this rank's KV heads (all of them for the KV-range split) and the ranks
     # that share them, which split the KV range among themselves
     hs = (bdist.head_split_plan(KVH, world, rank) if split == "heads"
@@ -1266,8 +1279,10 @@ def main():
     ap.add_argument("--no-small", action="store_true", help="skip the config-1/2 (latency-bound) sub-measurement")
     ap.add_argument("--no-out-proj", action="store_true", help="skip the attention output projection measurement")
     ap.add_argument("--no-qkv-proj", action="store_true", help="skip the QKV projection (+ RoPE/append) measurement")
-    ap.add_argument("--decode-split", default="auto", choices=["auto", "heads", "kv"],
-                    help="N > 1 decode: by KV head (auto when the KV heads divide or are divided by N) or by KV range")
+    ap.add_argument("--ragged-split", default="seqs", choices=["seqs", "heads"],
+                    help="N > 1 ragged decode: whole sequences per rank, or KV heads per rank (tensor-parallel layout)")
+    ap.add_argument("--decode-split", default="kv", choices=["kv", "heads"],
+                    help="N > 1 decode: KV range per rank, or KV heads per rank (tensor-parallel layout)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
                          "all-gather of the rank partials and a merge kernel")

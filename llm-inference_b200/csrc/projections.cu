@@ -95,6 +95,48 @@ __device__ __forceinline__ void round32(const uint32_t (&raw)[32], uint4 (&v)[4]
                           pack_half2(__uint_as_float(raw[8 * i + 6]), __uint_as_float(raw[8 * i + 7])));
 }
 
+// Out-projection epilogue of one accumulator tile (256 columns from n0) for
+// this thread's row: + beta * residual, FP16 stores.
+__device__ __forceinline__ void residual_epilogue(const GemmArgs& g, uint32_t tacc, uint32_t row, uint32_t n0,
+                                                  bool live) {
+    const uint64_t base = static_cast<uint64_t>(row) * g.N + n0;
+#pragma unroll 1
+    for (uint32_t half = 0; half < 2; ++half) {
+        // this half's 128 residual values in flight before the TMEM loads
+        uint4 res[16];
+        if (g.beta != 0.f && live) {
+#pragma unroll
+            for (int v = 0; v < 16; ++v)
+                res[v] = *reinterpret_cast<const uint4*>(g.residual + base + half * 128 + v * 8);
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < 4; ++c) {
+            uint32_t raw[32];
+            tc::tmem_ld32(tacc + half * 128 + c * 32, raw);
+            tc::tmem_wait_ld();
+            uint32_t o16[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float lo = __uint_as_float(raw[2 * j]), hi = __uint_as_float(raw[2 * j + 1]);
+                if (g.beta != 0.f && live) {
+                    const uint32_t w = (&res[c * 4].x)[j];
+                    const __half2 r2 = *reinterpret_cast<const __half2*>(&w);
+                    const float2 rf = __half22float2(r2);
+                    lo = fmaf(g.beta, rf.x, lo);
+                    hi = fmaf(g.beta, rf.y, hi);
+                }
+                o16[j] = pack_half2(lo, hi);
+            }
+            if (live) {
+                uint4* dst = reinterpret_cast<uint4*>(g.out + base + half * 128 + c * 32);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    dst[v] = make_uint4(o16[4 * v], o16[4 * v + 1], o16[4 * v + 2], o16[4 * v + 3]);
+            }
+        }
+    }
+}
+
 // QKV epilogue of one accumulator tile (256 columns starting at n0, all of Q,
 // all of K or all of V since q_dim and kv_dim are multiples of 256) for this
 // thread's row: the steps of launch_rope_and_store_kv
@@ -250,48 +292,12 @@ __device__ __forceinline__ void proj_gemm_body(const CUtensorMap* map_a, const C
             const uint32_t row = (tile / g.tiles_n) * kBM + quarter * 32 + lane;
             const uint32_t n0 = (tile % g.tiles_n) * kBN;
             const bool live = row < g.M;
-            const uint64_t base = static_cast<uint64_t>(row) * g.N + n0;
             if (!(ok = mbar_wait(&bars->acc_full[buf], (t >> 1) & 1))) break;
             tc::fence_after_sync();
-            if constexpr (kEpi == kEpiQkvRope) {
+            if constexpr (kEpi == kEpiQkvRope)
                 qkv_rope_epilogue(g, tbase + lane_addr + buf * kBN, row, n0, live);
-            } else {
-#pragma unroll 1
-                for (uint32_t half = 0; half < 2; ++half) {
-                    // this half's 128 residual values in flight before the TMEM loads
-                    uint4 res[16];
-                    if (g.beta != 0.f && live) {
-#pragma unroll
-                        for (int v = 0; v < 16; ++v)
-                            res[v] = *reinterpret_cast<const uint4*>(g.residual + base + half * 128 + v * 8);
-                    }
-#pragma unroll
-                    for (uint32_t c = 0; c < 4; ++c) {
-                        uint32_t raw[32];
-                        tc::tmem_ld32(tbase + lane_addr + buf * kBN + half * 128 + c * 32, raw);
-                        tc::tmem_wait_ld();
-                        uint32_t o16[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            float lo = __uint_as_float(raw[2 * j]), hi = __uint_as_float(raw[2 * j + 1]);
-                            if (g.beta != 0.f && live) {
-                                const uint32_t w = (&res[c * 4].x)[j];
-                                const __half2 r2 = *reinterpret_cast<const __half2*>(&w);
-                                const float2 rf = __half22float2(r2);
-                                lo = fmaf(g.beta, rf.x, lo);
-                                hi = fmaf(g.beta, rf.y, hi);
-                            }
-                            o16[j] = pack_half2(lo, hi);
-                        }
-                        if (live) {
-                            uint4* dst = reinterpret_cast<uint4*>(g.out + base + half * 128 + c * 32);
-#pragma unroll
-                            for (int v = 0; v < 4; ++v)
-                                dst[v] = make_uint4(o16[4 * v], o16[4 * v + 1], o16[4 * v + 2], o16[4 * v + 3]);
-                        }
-                    }
-                }
-            }
+            else
+                residual_epilogue(g, tbase + lane_addr + buf * kBN, row, n0, live);
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
@@ -316,6 +322,160 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     qkv_rope_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const GemmArgs g) {
     proj_gemm_body<kEpiQkvRope>(&map_a, &map_b, g);
+}
+
+// ---- CTA-pair form -----------------------------------------------------------
+// Output tiles of 256 tokens x 256 columns per cluster of two CTAs
+// (tcgen05.mma.cta_group::2, M 256, N 256, K 16): each CTA loads its own 128
+// rows of A and its half (128 rows) of B per 64-wide K slice, so a stage is
+// 32 KB instead of 48 KB and six stages fit (3,072 MMA cycles in flight per SM
+// against 2,048 for the single-CTA form), and each SM pulls 64 B per MMA cycle
+// from L2 instead of 96. The leader (cluster rank 0) issues the MMAs; both
+// CTAs' copies complete on the leader's stage barrier; the leader's commits
+// release the stage and signal the accumulator in both CTAs; each CTA drains
+// its own 128 TMEM lanes with the same epilogues, and both CTAs' epilogue warps
+// arrive on the leader's accumulator-free barrier.
+constexpr uint32_t kPairStages = 6;
+constexpr uint32_t kPairABytes = 128 * kBK * 2;   // this CTA's 128 rows of A
+constexpr uint32_t kPairBBytes = 128 * kBK * 2;   // this CTA's 128 rows (half) of B
+constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr uint32_t kPairSmem = kPairStages * kPairStageBytes + 1024 + 1024;
+
+struct PairBars {
+    uint64_t full[kPairStages], empty[kPairStages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+
+template <int kEpi>
+__device__ __forceinline__ void proj_gemm_pair_body(const CUtensorMap* map_a, const CUtensorMap* map_b,
+                                                    const GemmArgs& g) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairStages * kPairStageBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = tc::cluster_rank();
+    const bool leader = rank == 0;
+    const uint32_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const uint32_t ntiles = g.tiles_m * g.tiles_n;  // tiles_m counts 256-row blocks here
+    const uint32_t kb_count = g.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kPairStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->acc_full[b], 1);
+            mbar_init(&bars->acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs
+        }
+        bars->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tc::tmem_alloc_pair(&bars->tmem_base, 512);
+    // the peer's barriers are initialised before any copy or arrive reaches them
+    tc::fence_before_sync();
+    tc::cluster_sync();
+    tc::fence_after_sync();
+    pdl_wait_primary();  // activations and the residual come from earlier kernels
+    pdl_launch_dependents();
+    const uint32_t tbase = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tc::prefetch_tensormap(map_a);
+            tc::prefetch_tensormap(map_b);
+            uint32_t i = 0;
+            bool ok = true;
+            for (uint32_t tile = pair; tile < ntiles && ok; tile += npairs) {
+                const int32_t m0 = static_cast<int32_t>((tile / g.tiles_n) * 256 + rank * 128);
+                const int32_t n0 = static_cast<int32_t>((tile % g.tiles_n) * kBN + rank * 128);
+                for (uint32_t kb = 0; kb < kb_count; ++kb, ++i) {
+                    const uint32_t s = i % kPairStages, r = i / kPairStages;
+                    // released by the leader's commit once the pair MMAs have read it
+                    if (r > 0 && !(ok = mbar_wait(&bars->empty[s], (r - 1) & 1))) break;
+                    uint8_t* st = smem + s * kPairStageBytes;
+                    if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
+                    const uint32_t fb = tc::cluster_addr(&bars->full[s], 0);
+                    tc::tma_load_3d_pair(st, map_a, static_cast<int32_t>(kb * kBK), m0, 0, fb);
+                    tc::tma_load_3d_pair(st + kPairABytes, map_b, static_cast<int32_t>(kb * kBK), n0, 0, fb);
+                }
+            }
+            if (!ok) bars->abort = 1;
+            // The copies complete on the leader's barriers; the leader's MMA
+            // thread waits for every stage it consumes, and this CTA leaves only
+            // after the cluster barrier below, which the leader reaches after
+            // its MMA loop.
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(256, kBN, false, false);
+            uint32_t i = 0, t = 0;
+            bool ok = true;
+            for (uint32_t tile = pair; tile < ntiles && ok; tile += npairs, ++t) {
+                const uint32_t buf = t & 1;
+                // both CTAs' epilogues have drained this accumulator (tile t - 2)
+                if (t >= 2 && !(ok = mbar_wait(&bars->acc_empty[buf], ((t >> 1) - 1) & 1))) break;
+                tc::fence_after_sync();
+                const uint32_t d = tbase + buf * kBN;
+                for (uint32_t kb = 0; kb < kb_count; ++kb, ++i) {
+                    const uint32_t s = i % kPairStages;
+                    if (!(ok = mbar_wait(&bars->full[s], (i / kPairStages) & 1))) break;
+                    tc::fence_after_sync();
+                    const uint32_t a = smem_u32(smem + s * kPairStageBytes), b = a + kPairABytes;
+#pragma unroll
+                    for (uint32_t ks = 0; ks < kBK / 16; ++ks)
+                        tc::mma_ss_pair(d, tc::desc_kmajor_sw128(a + ks * 32), tc::desc_kmajor_sw128(b + ks * 32),
+                                        idesc, (kb | ks) != 0 ? 1u : 0u);
+                    tc::commit_pair(&bars->empty[s], 0x3);  // the stage is free in both CTAs
+                }
+                if (ok) tc::commit_pair(&bars->acc_full[buf], 0x3);
+            }
+            if (!ok) bars->abort = 1;
+        }
+    } else if (warp >= 4) {
+        const uint32_t quarter = static_cast<uint32_t>(warp) & 3;
+        const uint32_t lane_addr = (quarter * 32) << 16;
+        uint32_t t = 0;
+        bool ok = true;
+        for (uint32_t tile = pair; tile < ntiles; tile += npairs, ++t) {
+            const uint32_t buf = t & 1;
+            const uint32_t row = (tile / g.tiles_n) * 256 + rank * 128 + quarter * 32 + lane;
+            const uint32_t n0 = (tile % g.tiles_n) * kBN;
+            const bool live = row < g.M;
+            if (!(ok = mbar_wait(&bars->acc_full[buf], (t >> 1) & 1))) break;
+            tc::fence_after_sync();
+            if constexpr (kEpi == kEpiQkvRope)
+                qkv_rope_epilogue(g, tbase + lane_addr + buf * kBN, row, n0, live);
+            else
+                residual_epilogue(g, tbase + lane_addr + buf * kBN, row, n0, live);
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&bars->acc_empty[buf], 0));
+        }
+        if (!ok) bars->abort = 1;
+    }
+    // Neither CTA leaves while the other may still signal its barriers or
+    // read its shared memory through the pair MMAs.
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::cluster_sync();
+    tc::fence_after_sync();
+    if (bars->abort && threadIdx.x == 0) atomicOr(&g_device_error, kErrWaitTimeout);
+    if (warp == 1) tc::tmem_dealloc_pair(tbase, 512);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    out_proj_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                              const GemmArgs g) {
+    proj_gemm_pair_body<kEpiResidual>(&map_a, &map_b, g);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    qkv_rope_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                              const GemmArgs g) {
+    proj_gemm_pair_body<kEpiQkvRope>(&map_a, &map_b, g);
 }
 
 // Decode GEMV: out[n] = W[n] . x + beta * out[n], one warp per row, K a
@@ -407,16 +567,109 @@ int ensure_gemm_smem() {
     if (st == B2_OK)
         st = cuda_status(
             cudaFuncSetAttribute(qkv_rope_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+    if (st == B2_OK)
+        st = cuda_status(cudaFuncSetAttribute(out_proj_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              kPairSmem));
+    if (st == B2_OK)
+        st = cuda_status(cudaFuncSetAttribute(qkv_rope_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              kPairSmem));
     if (st == B2_OK) done.fetch_or(bit);
     return st;
 }
 
-// Tensor maps of the two K-major operands: activations [M][K], weights [N][K].
-int gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const __half* x, const __half* w, size_t M, size_t N, size_t K) {
+// Tensor maps of the two K-major operands: activations [M][K] (128-row
+// boxes), weights [N][K] (b_rows-row boxes: 256 for one CTA, 128 for a pair).
+int gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const __half* x, const __half* w, size_t M, size_t N, size_t K,
+              uint32_t b_rows) {
     if (encode_tensor_map_3d_f16(ma, x, K, M, 1, K * 2, 0, kBK, kBM) != 0 ||
-        encode_tensor_map_3d_f16(mb, w, K, N, 1, K * 2, 0, kBK, kBN) != 0)
+        encode_tensor_map_3d_f16(mb, w, K, N, 1, K * 2, 0, kBK, b_rows) != 0)
         return B2_ERR_UNSUPPORTED;
     return B2_OK;
+}
+
+// Two-CTA clusters of a pair kernel that fit on the GPU at once (0: use the
+// single-CTA kernel). Cached per device and kernel as the count + 1.
+template <typename Kern>
+uint32_t pair_clusters(Kern kernel, std::atomic<int>* cache) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    const int v = cache[dev].load();
+    if (v > 0) return static_cast<uint32_t>(v - 1);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * static_cast<uint32_t>(sm_count() / 2));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = kPairSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    if (n < 0) n = 0;
+    cache[dev].store(n + 1);
+    return static_cast<uint32_t>(n);
+}
+
+std::atomic<int> g_pair_clusters_oproj[64], g_pair_clusters_qkv[64];  // zero: not queried yet
+
+// Launch a pair kernel as `clusters` clusters of two CTAs, with programmatic
+// dependent launch allowed (as launch_pdl).
+template <typename... KArgs, typename... Args>
+int launch_pdl_pairs(void (*kernel)(KArgs...), uint32_t clusters, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        note_cuda_error(e);
+        return B2_ERR_CUDA;
+    }
+    return launch_status();
+}
+
+// The persistent GEMM over g (tiles_m / tiles_n filled in here): CTA pairs of
+// 256-row tiles when the prompt spans more than one 128-row tile and pairs
+// can be scheduled, else one CTA per 128-row tile.
+template <int kEpi>
+int launch_gemm(const __half* x, const __half* w, GemmArgs g, cudaStream_t stream) {
+    int st = ensure_gemm_smem();
+    if (st != B2_OK) return st;
+    CUtensorMap ma, mb;
+    g.tiles_n = g.N / kBN;
+    auto pair_kernel = kEpi == kEpiQkvRope ? qkv_rope_gemm_pair_kernel : out_proj_gemm_pair_kernel;
+    const uint32_t max_clusters =
+        g.M > kBM ? pair_clusters(pair_kernel, kEpi == kEpiQkvRope ? g_pair_clusters_qkv : g_pair_clusters_oproj)
+                  : 0u;
+    if (max_clusters > 0) {
+        if ((st = gemm_maps(&ma, &mb, x, w, g.M, g.N, g.K, kBN / 2)) != B2_OK) return st;
+        g.tiles_m = (g.M + 255) / 256;
+        const uint32_t clusters = std::min<uint32_t>(g.tiles_m * g.tiles_n, max_clusters);
+        return launch_pdl_pairs(pair_kernel, clusters, kPairSmem, stream, ma, mb, g);
+    }
+    if ((st = gemm_maps(&ma, &mb, x, w, g.M, g.N, g.K, kBN)) != B2_OK) return st;
+    g.tiles_m = (g.M + kBM - 1) / kBM;
+    const uint32_t grid = std::min<uint32_t>(g.tiles_m * g.tiles_n, static_cast<uint32_t>(sm_count()));
+    return launch_pdl(kEpi == kEpiQkvRope ? qkv_rope_gemm_kernel : out_proj_gemm_kernel, dim3(grid),
+                      dim3(kGemmThreads), kGemmSmem, stream, ma, mb, g);
 }
 
 int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, size_t N, size_t K, float beta,
@@ -434,22 +687,14 @@ int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, si
             return launch_pdl(out_proj_gemv_kernel, dim3((n + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32),
                               0, stream, x, w, out, n, k, beta);
     } else if (aligned && N % kBN == 0 && K % kBK == 0) {
-        int st = ensure_gemm_smem();
-        if (st != B2_OK) return st;
-        CUtensorMap ma, mb;
-        if ((st = gemm_maps(&ma, &mb, x, w, M, N, K)) != B2_OK) return st;
         GemmArgs g{};
         g.residual = out;
         g.out = out;
         g.M = m;
         g.N = n;
         g.K = k;
-        g.tiles_m = (m + kBM - 1) / kBM;
-        g.tiles_n = n / kBN;
         g.beta = beta;
-        const uint32_t tiles = g.tiles_m * g.tiles_n;
-        const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count()));
-        return launch_pdl(out_proj_gemm_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, stream, ma, mb, g);
+        return launch_gemm<kEpiResidual>(x, w, g, stream);
     }
     const uint64_t total = static_cast<uint64_t>(m) * n;
     return launch_pdl(out_proj_simt_kernel, dim3(static_cast<uint32_t>((total + 255) / 256)), dim3(256), 0, stream,
@@ -485,19 +730,11 @@ int launch_qkv_rope(const void* d_in, void* d_qkv, const void* d_w, void* d_k_ca
                                            M, H, KVH, d, N, N, start_pos, rotate,
                                            reinterpret_cast<b2_stream_t>(stream));
     }
-    int st = ensure_gemm_smem();
-    if (st != B2_OK) return st;
-    CUtensorMap ma, mb;
-    if ((st = gemm_maps(&ma, &mb, static_cast<const __half*>(d_in), static_cast<const __half*>(d_w), M, N,
-                        hidden)) != B2_OK)
-        return st;
     GemmArgs g{};
     g.out = static_cast<__half*>(d_qkv);
     g.M = static_cast<uint32_t>(M);
     g.N = static_cast<uint32_t>(N);
     g.K = static_cast<uint32_t>(hidden);
-    g.tiles_m = static_cast<uint32_t>((M + kBM - 1) / kBM);
-    g.tiles_n = static_cast<uint32_t>(N / kBN);
     g.k_cache = static_cast<__half*>(d_k_cache);
     g.v_cache = static_cast<__half*>(d_v_cache);
     g.cos = static_cast<const __half*>(d_cos);
@@ -507,9 +744,7 @@ int launch_qkv_rope(const void* d_in, void* d_qkv, const void* d_w, void* d_k_ca
     g.head_dim = static_cast<uint32_t>(d);
     g.start_pos = static_cast<uint32_t>(start_pos);
     g.rotate = rotate ? 1u : 0u;
-    const uint32_t tiles = g.tiles_m * g.tiles_n;
-    const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count()));
-    return launch_pdl(qkv_rope_gemm_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, stream, ma, mb, g);
+    return launch_gemm<kEpiQkvRope>(static_cast<const __half*>(d_in), static_cast<const __half*>(d_w), g, stream);
 }
 
 }  // namespace

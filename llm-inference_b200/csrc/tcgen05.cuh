@@ -154,6 +154,70 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
                  : "memory");
 }
 
+// ---- CTA pairs (cta_group::2) ------------------------------------------------
+// A cluster of two CTAs on two SMs issues one MMA of M = 256: the leader
+// (cluster rank 0) issues it, A's rows 0-127 come from the leader's shared
+// memory and rows 128-255 from its peer's at the same offset, B's rows (the N
+// dimension) 0..N/2-1 from the leader and N/2..N-1 from the peer, and each CTA's
+// TMEM receives its own 128 rows of D.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of both CTAs: release this CTA's prior writes (barrier inits
+// included) to the cluster and wait for the peer's.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of `p` (an object of this CTA's shared memory
+// layout) in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Warp-collective in one warp (the same warp index) of each CTA of the pair.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Leader only: D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both].
+__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Leader only: arrive once on `bar` (same offset) in each CTA of `cta_mask`
+// when the pair MMAs issued so far complete.
+__device__ __forceinline__ void commit_pair(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+
 // ---- tensor TMA -------------------------------------------------------------
 
 // 2-D / 3-D tiled loads into this CTA's shared memory completing on `bar`.
@@ -191,6 +255,17 @@ __device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* m
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
         "{%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// 3-D tiled load into this CTA's shared memory whose completion is counted on
+// the pair leader's barrier (`cluster_bar`, a shared::cluster address).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                                 uint32_t cluster_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(cluster_bar)
         : "memory");
 }
 

@@ -24,6 +24,7 @@ def _ref(x, w, res, beta):
     (254, 2048, 2048, 0.0),     # the reference's unit-test form (beta 0 never reads out)
     (300, 2048, 2048, 1.0),     # ragged last M tile
     (2, 256, 64, 0.5),          # smallest tcgen05 shape
+    (128, 2048, 2048, 1.0),     # one 128-row tile: the single-CTA kernel (longer prompts run CTA pairs)
     (8192, 2048, 2048, 1.0),    # 512 output tiles: several per persistent CTA, both TMEM accumulators
     (37, 96, 40, 1.0),          # SIMT kernel shapes (hidden not a multiple of 256, K of 64)
     (5, 512, 200, 0.0),

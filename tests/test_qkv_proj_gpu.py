@@ -86,7 +86,8 @@ def _bits(a):
     (300, 2048, 16, 4, 128, 0, True),     # SmolLM3 layer, ragged last tile
     (300, 2048, 16, 4, 128, 0, False),    # NoPE layer (every 4th)
     (254, 2048, 16, 4, 128, 37, True),    # continued prompt: cache rows 37..290
-    (1, 2048, 16, 4, 128, 600, True),     # one token through the GEMM tile path
+    (1, 2048, 16, 4, 128, 600, True),     # one token: the GEMV and the RoPE kernel
+    (100, 2048, 16, 4, 128, 9, True),     # one 128-row tile: the single-CTA kernel (longer prompts run CTA pairs)
     (2048, 2048, 16, 4, 128, 0, True),    # 16 M tiles x 12 N tiles: both TMEM accumulators
     (8192, 2048, 16, 4, 128, 0, True),    # one config-3 sequence: 768 tiles, 5-6 per persistent CTA
     (130, 512, 8, 4, 64, 5, True),        # head_dim 64: four heads a tile

@@ -964,7 +964,8 @@ def run_out_proj(args, dev):
                         f"decode GEMV W [{N} x {K}] per layer (config 4), 36 layers' weights, FP16 in/out, FP32 "
                         "accumulate",
             "prefill": {"value": round(tf, 1), "unit": "TFLOP/s", "ms_per_layer": round(ms, 4),
-                        "roofline": {"bound": "tensor", "kernel": "out_proj_gemm_kernel", "achieved": round(tf, 1),
+                        "roofline": {"bound": "tensor", "kernel": "out_proj_gemm_pair_kernel (CTA pairs)",
+                                     "achieved": round(tf, 1),
                                      "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
                                      "frac_of_nominal_2250": round(tf / 2250.0, 4),
                                      "algorithmic_flops_per_launch": flops, "peak_kind": "measured bf16 sustained"},
@@ -1044,7 +1045,8 @@ def run_qkv_proj(args, dev):
             "value": round(tf, 1), "unit": "TFLOP/s", "ms_per_layer": round(ms, 4),
             "two_launches_ms_per_layer": round(res["two_launches"][0], 4),
             "speedup_vs_two_launches": round(res["two_launches"][0] / ms, 3),
-            "roofline": {"bound": "tensor", "kernel": "qkv_rope_gemm_kernel", "achieved": round(tf, 1),
+            "roofline": {"bound": "tensor", "kernel": "qkv_rope_gemm_pair_kernel (CTA pairs)",
+                         "achieved": round(tf, 1),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(tf / peak, 4),
                          "frac_of_nominal_2250": round(tf / 2250.0, 4),
                          "algorithmic_flops_per_launch": flops // PF_B, "peak_kind": "measured bf16 sustained"},

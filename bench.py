@@ -1197,7 +1197,10 @@ def run_b200(args, rank, world):
                                stream, step_state, mode="reference")
     else:
         e2e = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup, args.steps,
-                               stream, step_state, mode="fused", group=group)
+                               stream, step_state, mode="graph", group=group)
+        eager = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup,
+                                 args.steps, stream, step_state, mode="fused", group=group)
+        e2e["eager"] = {"value": eager["value"], "ms_per_step": eager["ms_per_step"], "path": eager["path"]}
         if world == 1:
             ref_calls = bdist.e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, PAST, args.warmup,
                                          args.steps, stream, step_state, mode="reference")

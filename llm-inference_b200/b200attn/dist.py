@@ -399,10 +399,13 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
     mode "fused": one fused-step call per layer, eager (b2_launch_decode_step_fused
     on one GPU; on N GPUs the rank's fused call with the cross-rank exchange,
     peer or NCCL as st.exchange says); the position travels with the step's
-    inputs. mode "reference" (one GPU): the reference engine's calls,
-    launch_rope_and_store_kv + launch_causal_attention_decode_vectorized per
-    layer with a host start_pos. Returns this rank's device time; the caller
-    takes the max over ranks."""
+    inputs. mode "graph": the same calls and both copies captured once into a
+    CUDA graph that is replayed every step, the way the reference engine runs
+    its decode (include/model_inference.hpp:96-123), with the position kept on
+    the device and advanced inside the graph. mode "reference" (one GPU): the
+    reference engine's calls, launch_rope_and_store_kv +
+    launch_causal_attention_decode_vectorized per layer with a host start_pos.
+    Returns the device time, max over ranks."""
     import torch
     from . import kernels as K
     H, KVH, D, L = st.H, st.KVH, st.D, st.L
@@ -430,10 +433,34 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
                                                             kv_dim, stream=stream)
         out_host.copy_(out, non_blocking=True)
 
+    graph = None
+    if mode == "graph":
+        st.reset_position(past)
+        with torch.cuda.stream(stream):
+            qkv.copy_(qkv_host, non_blocking=True)
+            enqueue_decode_step(st, cache, qkv, out, d_cos, d_sin, stream, group, advance=True)
+            out_host.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            cur = torch.cuda.current_stream()
+            qkv.copy_(qkv_host, non_blocking=True)
+            enqueue_decode_step(st, cache, qkv, out, d_cos, d_sin, cur, group, advance=True)
+            out_host.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        st.reset_position(past)
+        torch.cuda.synchronize()
+
+        def step(s):  # noqa: F811 -- the graph replaces the eager step
+            graph.replay()
+
     with torch.cuda.stream(stream):
         for s in range(warmup):
             step(s)
         torch.cuda.synchronize()
+        if graph is not None:
+            st.reset_position(past)
+            torch.cuda.synchronize()
         if st.job_world > 1:
             import torch.distributed as tdist
             tdist.barrier()
@@ -445,12 +472,22 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    if graph is not None:
+        graph.reset()
     if st.job_world > 1:
         ms = max_over_ranks(ms, qkv.device)
     # whole-job bytes: every layer's full KV range (all ranks' shares, all heads)
     jkv, jq = st.job_kv_dim, st.job_q_dim
     nbytes = sum(L * (2 * (past + 1 + s) * jkv * 2 + jq * 2 * 2 + 2 * jkv * 2) for s in range(steps))
     h2d = int(qkv_host.numel() * 2) + (4 if mode == "fused" else 0)
+    if mode == "graph":
+        return {"value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": int(out_host.numel() * 2), "ms_per_step": round(ms / steps, 4),
+                "path": "one CUDA graph per step replayed through the C ABI (as the reference engine runs decode): "
+                        "the step's Q/K/V rows H2D from pinned memory, the " + str(L) + " fused-step calls "
+                        "(b2_launch_decode_step_fused" + ("" if st.plan.world == 1 else
+                                                          ", cross-rank exchange " + str(st.exchange)) +
+                        ") with the position on the device, the outputs D2H"}
     fused_call = ("b2_launch_decode_step_fused" + (" on this rank's KV heads" if st.job_world > 1 else "")
                   if st.plan.world == 1 else
                   "b2_launch_decode_step_fused_exchange (cross-rank merge over peer memory)"

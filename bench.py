@@ -1104,7 +1104,7 @@ def run_b200(args, rank, world):
     out_host = torch.zeros_like(out, device="cpu").pin_memory()
     step_state = bdist.DecodeStepState(plan, h_l, kvh_l, D, LAYERS, capacity, max_global, dev, fused=not args.unfused,
                                        exchange=args.exchange, members=hs.group, job_world=world,
-                                       job_kv_dim=KV_DIM, job_q_dim=Q_DIM)
+                                       job_kv_dim=KV_DIM, job_q_dim=Q_DIM, pipeline=args.pipeline_exchange)
 
     stream = torch.cuda.Stream(device=dev)
     group = None
@@ -1240,9 +1240,14 @@ def run_b200(args, rank, world):
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
-            "data": "synthetic: KV ~N(0,0.5) (torch CUDA generator, seed 2024+rank), Q/K/V rows ~N(0,1) seeded",
+            "data": "synthetic: KV ~N(0,0.5) (torch CUDA generator, seed 2024+rank), Q/K/V rows ~N(0,1) seeded"
+                    + ("; layers pipelined across the exchange (not valid for a model)" if step_state.pipeline
+                       else ""),
             "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": PAST, "layers": LAYERS,
-                       "parallelism": decode_parallelism(split, hs, h_l, step_state.exchange) if world > 1
+                       "parallelism": (decode_parallelism(split, hs, h_l, step_state.exchange) +
+                                       ("; SYNTHETIC: layer l's all-gather + merge on a second stream under layer "
+                                        "l+1's kernel, valid only because this benchmark's Q rows do not depend on "
+                                        "the previous layer" if step_state.pipeline else "")) if world > 1
                        else "single-gpu",
                        "l2": "inputs larger than L2 (4.8 GB of KV per step)",
                        "step_graph": f"one CUDA graph per step, {launches_per_step} kernels"},
@@ -1288,6 +1293,9 @@ def main():
                     help="N > 1 ragged decode: whole sequences per rank, or KV heads per rank (tensor-parallel layout)")
     ap.add_argument("--decode-split", default="kv", choices=["kv", "heads"],
                     help="N > 1 decode: KV range per rank, or KV heads per rank (tensor-parallel layout)")
+    ap.add_argument("--pipeline-exchange", action="store_true",
+                    help="N > 1 with --exchange nccl: overlap layer l's exchange with layer l+1 (synthetic only: "
+                         "a model's next layer needs this layer's output)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1 decode: cross-rank merge inside the fused kernel over peer memory, or an NCCL "
                          "all-gather of the rank partials and a merge kernel")

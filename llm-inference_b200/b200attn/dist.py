@@ -197,12 +197,16 @@ class DecodeStepState:
 
     def __init__(self, plan: SplitPlan, num_heads, num_kv_heads, head_dim, num_layers, capacity, max_global,
                  device, fused=True, exchange="peer", members=None, job_world=None, job_kv_dim=None,
-                 job_q_dim=None):
+                 job_q_dim=None, pipeline=False):
         """plan: the KV split among the ranks that share this rank's heads
         (`members`, global ranks; default all ranks); num_heads / num_kv_heads
         are this rank's. job_*: the whole job's world size and widths, for the
         barrier, the max over ranks and the whole-job byte count (default: the
-        plan's world and these heads)."""
+        plan's world and these heads). pipeline (NCCL exchange only): each
+        layer's all-gather and merge run on a second stream, overlapping the
+        next layer's kernel -- valid only when a layer's Q does not depend on
+        the previous layer's output (the synthetic benchmark), never in a
+        model."""
         import torch
         from . import kernels as K
         self.plan = plan
@@ -223,6 +227,13 @@ class DecodeStepState:
                 tdist.all_gather_object(out, obj)
                 return out if members is None else [out[r] for r in members]
             self.xbuf = K.ExchangeBuffers(plan.world, plan.rank, num_heads, gather)
+        self.pipeline = bool(pipeline) and self.exchange == "nccl"
+        if pipeline and not self.pipeline:
+            raise ValueError("the pipelined exchange needs the fused step, N > 1 and the NCCL exchange")
+        if self.pipeline:
+            self.comm_stream = torch.cuda.Stream(device=device)
+            self.layer_events = [torch.cuda.Event() for _ in range(num_layers)]
+            self.join_event = torch.cuda.Event()
         self.H, self.KVH, self.D, self.L = num_heads, num_kv_heads, head_dim, num_layers
         self.job_world = job_world or plan.world
         self.job_kv_dim = job_kv_dim or num_kv_heads * head_dim
@@ -292,7 +303,13 @@ def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stre
                                                     src, bias, st.capacity, part[:H * D], part[H * D:H * D + H],
                                                     part[H * D + H:], st.step_ws, st.step_ws_bytes, H, KVH, D,
                                                     stream=stream)
-            _exchange_and_merge(st, l, part, out, group, stream)
+            if st.pipeline:
+                # layer l's exchange on the side stream; layer l + 1 goes on
+                st.layer_events[l].record(_as_stream(stream))
+                st.comm_stream.wait_event(st.layer_events[l])
+                _exchange_and_merge(st, l, part, out, group, st.comm_stream)
+            else:
+                _exchange_and_merge(st, l, part, out, group, stream)
             continue
         if plan.is_tail:
             # cache rows are local: global position p lives at local row p - begin
@@ -316,8 +333,18 @@ def enqueue_decode_step(st: DecodeStepState, cache, qkv, out, d_cos, d_sin, stre
                                                 src, bias, st.capacity, H, KVH, D, kv_dim, part[:H * D],
                                                 part[H * D:H * D + H], part[H * D + H:], stream=stream)
             _exchange_and_merge(st, l, part, out, group, stream)
+    if st.fused and getattr(st, "pipeline", False):
+        st.join_event.record(st.comm_stream)
+        _as_stream(stream).wait_event(st.join_event)
     if advance:
         K.advance_position(st.pos, 1, stream=stream)
+
+
+def _as_stream(stream):
+    import torch
+    if isinstance(stream, torch.cuda.Stream):
+        return stream
+    return torch.cuda.current_stream()
 
 
 def _exchange_and_merge(st: DecodeStepState, l, part, out, group, stream):

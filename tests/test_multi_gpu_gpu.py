@@ -28,7 +28,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, exchange, split, q):
+def _worker(rank, world, port, exchange, split, q, pipeline=False):
     try:
         import sys
         root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -70,7 +70,7 @@ def _worker(rank, world, port, exchange, split, q):
         qkv = torch.empty((LAYERS, h_l * D + 2 * kvh_l * D), dtype=torch.float16, device=dev)
         out = torch.empty((LAYERS, h_l * D), dtype=torch.float16, device=dev)
         st = bdist.DecodeStepState(plan, h_l, kvh_l, D, LAYERS, capacity, max_global, dev, fused=True,
-                                   exchange=exchange, members=hs.group, job_world=world)
+                                   exchange=exchange, members=hs.group, job_world=world, pipeline=pipeline)
         st.reset_position(PAST)
         stream = torch.cuda.Stream(device=dev)
         group = None
@@ -106,7 +106,7 @@ def _worker(rank, world, port, exchange, split, q):
         q.put((rank, traceback.format_exc()))
 
 
-def _run(exchange, split="kv", max_world=4):
+def _run(exchange, split="kv", max_world=4, pipeline=False):
     import torch
     import multiprocessing as mp
     n = torch.cuda.device_count()
@@ -118,7 +118,7 @@ def _run(exchange, split="kv", max_world=4):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, split, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, split, q, pipeline)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -141,6 +141,12 @@ def test_kv_split_decode_peer_exchange(cuda):
 
 def test_kv_split_decode_nccl_exchange(cuda):
     _run("nccl")
+
+
+def test_kv_split_decode_nccl_exchange_pipelined(cuda):
+    """Each layer's all-gather + merge on a second stream under the next
+    layer's kernel (the synthetic benchmark's mode): same outputs."""
+    _run("nccl", pipeline=True)
 
 
 def test_head_split_decode(cuda):

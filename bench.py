@@ -38,17 +38,17 @@ workload (one layer-step at the same kv_len per step), with the
 python/reference.py path on the same layer-step reported beside it, and
 prints the same line.
 
-N > 1 (torchrun): the 64K KV range of every layer is split into N contiguous
-ranges, one per rank (--decode-split kv, default); the rank holding the tail
-appends the new token; each rank reduces its range to one (o, m, l) partial
-per head. Partials of a split range are merged across ranks inside the fused
-kernel over CUDA-IPC peer memory (--exchange peer, default) or by an NCCL
-all-gather and a merge kernel (--exchange nccl). --decode-split heads gives
-each rank whole GQA groups with only their cache and their heads' outputs
-(the layout a tensor-parallel o_proj consumes, no exchange; at N = 8 the two
-ranks of a KV head also split its range); it measures slower here, because
-one KV head per launch leaves the decode kernel's fixed cost on a quarter of
-the bytes. Strong scaling: total work fixed. Prefill shards
+N > 1 (torchrun): config-4 decode by KV head (--decode-split heads, the
+default when the 4 KV heads divide or are divided by N): each rank owns whole
+GQA groups with only their cache and writes their heads' outputs, the layout
+a tensor-parallel o_proj consumes, with no exchange; at N = 8 the two ranks
+of each KV head also split its range. With --decode-split kv the 64K KV range
+of every layer is split into N contiguous ranges, one per rank; the rank
+holding the tail appends the new token; each rank reduces its range to one
+(o, m, l) partial per head. Partials of a split range are merged across ranks
+inside the fused kernel over CUDA-IPC peer memory (--exchange peer, default)
+or by an NCCL all-gather and a merge kernel (--exchange nccl). Strong
+scaling: total work fixed. Prefill shards
 (sequence, KV head) units and the ragged decode shards whole sequences
 (weak in units, no exchange).
 """
@@ -1077,6 +1077,8 @@ def run_b200(args, rank, world):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     split = args.decode_split
+    if split == "auto":
+        split = "heads" if world > 1 and (KVH % world == 0 or world % KVH == 0) else "kv"
     # this rank's KV heads (all of them for the KV-range split) and the ranks
     # that share them, which split the KV range among themselves
     hs = (bdist.head_split_plan(KVH, world, rank) if split == "heads"
@@ -1152,7 +1154,13 @@ def run_b200(args, rank, world):
     barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # N > 1: one untimed step right before the start event lines the ranks up
+    # on the device (every layer waits for all ranks' partials), so the host
+    # skew after the barrier is not timed as a wait inside the first step
+    align = 1 if world > 1 else 0
     with ClockSampler(dev.index) as clocks, torch.cuda.stream(stream):
+        for _ in range(align):
+            graph.replay()
         ev0.record(stream)
         for _ in range(args.steps):
             graph.replay()
@@ -1161,7 +1169,7 @@ def run_b200(args, rank, world):
     barrier()
     ms = ev0.elapsed_time(ev1)
     ms = bdist.max_over_ranks(ms, dev) if world > 1 else ms
-    total_bytes = sum(step_bytes(PAST + 1 + s) for s in range(args.steps))
+    total_bytes = sum(step_bytes(PAST + 1 + align + s) for s in range(args.steps))
     value = total_bytes / (ms / 1e3) / 1e9
 
     # ---- roofline: one layer's decode launch(es), CUDA events on its stream
@@ -1291,8 +1299,9 @@ def main():
     ap.add_argument("--no-qkv-proj", action="store_true", help="skip the QKV projection (+ RoPE/append) measurement")
     ap.add_argument("--ragged-split", default="seqs", choices=["seqs", "heads"],
                     help="N > 1 ragged decode: whole sequences per rank, or KV heads per rank (tensor-parallel layout)")
-    ap.add_argument("--decode-split", default="kv", choices=["kv", "heads"],
-                    help="N > 1 decode: KV range per rank, or KV heads per rank (tensor-parallel layout)")
+    ap.add_argument("--decode-split", default="auto", choices=["auto", "heads", "kv"],
+                    help="N > 1 decode: KV heads per rank (tensor-parallel layout; auto when the KV heads divide or "
+                         "are divided by N) or KV range per rank")
     ap.add_argument("--pipeline-exchange", action="store_true",
                     help="N > 1 with --exchange nccl: overlap layer l's exchange with layer l+1 (synthetic only: "
                          "a model's next layer needs this layer's output)")

@@ -493,6 +493,11 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
             tdist.barrier()
             torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # N > 1: one untimed step lines the ranks up on the device first (each
+        # layer waits for every rank), so host skew is not timed
+        align = 1 if st.job_world > 1 else 0
+        for _ in range(align):
+            step(0)
         e0.record(stream)
         for s in range(steps):
             step(s)
@@ -505,7 +510,10 @@ def e2e_decode(cache, qkv, qkv_host, out, out_host, d_cos, d_sin, past, warmup, 
         ms = max_over_ranks(ms, qkv.device)
     # whole-job bytes: every layer's full KV range (all ranks' shares, all heads)
     jkv, jq = st.job_kv_dim, st.job_q_dim
-    nbytes = sum(L * (2 * (past + 1 + s) * jkv * 2 + jq * 2 * 2 + 2 * jkv * 2) for s in range(steps))
+    # the graph advances the position on the device, so after the aligning
+    # step the timed steps run one token further
+    first = past + 1 + (align if graph is not None else 0)
+    nbytes = sum(L * (2 * (first + s) * jkv * 2 + jq * 2 * 2 + 2 * jkv * 2) for s in range(steps))
     h2d = int(qkv_host.numel() * 2) + (4 if mode == "fused" else 0)
     if mode == "graph":
         return {"value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,

@@ -447,10 +447,10 @@ __device__ __forceinline__ bool split_index_ok(const Extent& e, uint32_t split) 
 
 // The first tiles a split streams (up to kPrefetchTiles): its own range
 // (static) or its even share (fused).
-__device__ __forceinline__ void own_tiles(const Extent& e, uint32_t split, bool fused, uint32_t& first,
-                                          uint32_t& count) {
+__device__ __forceinline__ void own_tiles(const Extent& e, uint32_t split, bool fused, uint32_t rows,
+                                          uint32_t& first, uint32_t& count) {
     if (fused) {
-        const uint32_t per = fused_share((e.kv_len + kTile - 1) / kTile, e.splits);
+        const uint32_t per = fused_share((e.kv_len + rows - 1) / rows, e.splits);
         first = split * per;
         count = min(per, kPrefetchTiles);
     } else {
@@ -541,13 +541,20 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     __shared__ uint32_t stage_valid[32];  // kFused: rows of the tile in each stage, 0 = no more tiles
     __shared__ uint64_t merge_bar;        // kFused: bulk copies of the merge
     constexpr uint32_t row_bytes = KVH * 256;          // one token, all KV heads
-    constexpr uint32_t tile_bytes = kTile * row_bytes; // per K (and per V): [2*KVH blocks][16 rows][128 B]
+    // The fused step stages kSub 16-token sub-tiles per KV head when there are
+    // fewer than 4 KV heads, so every stage carries 16 KB per operand (a
+    // one-head row is 256 B: 16-token stages would spend a stage's fixed cost
+    // on 4 KB); consumer warp j = warp / KVH of a head takes sub-tile j % kSub
+    // of every npar-th stage.
+    constexpr uint32_t kSub = (kFused && KVH < 4) ? 4 / KVH : 1;
+    constexpr uint32_t kRows = kTile * kSub;           // tokens per stage
+    constexpr uint32_t tile_bytes = kRows * row_bytes; // per K (and per V): [2*KVH blocks][kRows rows][128 B]
     const uint32_t stages = a.stages;
     // 128-byte swizzled TMA boxes want 1024-byte aligned destinations
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * 2 * tile_bytes);
     uint64_t* empty = full + stages;
-    constexpr uint32_t npar = kTmaConsumers / KVH;     // consumer warps per KV head; divides `stages`
+    constexpr uint32_t npar = kTmaConsumers / (KVH * kSub);  // stage parities; divides `stages`
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // While the previous kernel finishes (nothing here depends on its output):
@@ -558,7 +565,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], KVH);
+            mbar_init(&empty[s], KVH * kSub);
         }
         if (kFused) mbar_init(&merge_bar, 1);
         fence_mbarrier_init();
@@ -572,7 +579,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             const Extent pre = decode_extent(a);
             if (split_index_ok(pre, blockIdx.x)) {
                 uint32_t first, count;
-                own_tiles(pre, blockIdx.x, kFused, first, count);
+                own_tiles(pre, blockIdx.x, kFused, kRows, first, count);
                 const uint32_t j = static_cast<uint32_t>(lane) >> 1;
                 if (j < count) {
                     const uint64_t off = static_cast<uint64_t>(first + j) * tile_bytes;
@@ -634,7 +641,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             // (`claimed`, `claimed2`, used in turn: each read sits in its own
             // branch so it waits for its own round trip only), so CTAs that
             // run ahead take more.
-            const uint32_t total = (ext.kv_len + kTile - 1) / kTile;
+            const uint32_t total = (ext.kv_len + kRows - 1) / kRows;
             const uint32_t per = fused_share(total, ext.splits);  // per * S <= total - 1
             const uint32_t pool = per * ext.splits, pool_end = total - 1;
             const bool tail_split = split + 1 == ext.splits;
@@ -697,7 +704,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                     break;
                 }
-                const uint32_t t0 = tile * kTile;
+                const uint32_t t0 = tile * kRows;
                 bool w_ok = true;
                 if (lane == 0 && round > 0) w_ok = mbar_wait(&empty[s], (round - 1) & 1);
                 if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
@@ -705,7 +712,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                     break;
                 }
                 if (lane == 0) {
-                    stage_valid[s] = min(static_cast<uint32_t>(kTile), ext.kv_len - t0);
+                    stage_valid[s] = min(kRows, ext.kv_len - t0);
                     mbar_arrive_expect_tx(&full[s], 2 * tile_bytes);
                     tc::tma_load_3d_hint(stg_of(ring, s, tile_bytes), &map_k, 0, static_cast<int32_t>(t0), 0,
                                          &full[s], policy);
@@ -749,8 +756,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             for (uint32_t i = first; i < issued; ++i) (void)mbar_wait(&full[i % stages], (i / stages) & 1);
         }
     } else {
-        // ---- consumers: warp = KV head (warp % KVH) x tile parity (warp / KVH)
-        const uint32_t kvh = warp % KVH, par = warp / KVH;
+        // ---- consumers: warp = KV head (warp % KVH) x sub-tile x stage parity
+        const uint32_t kvh = warp % KVH, sub = (warp / KVH) % kSub, par = warp / (KVH * kSub);
         const int g = lane >> 2, t = lane & 3;
         if constexpr (kFused) {
             if (warp == 0 && split + 1 == ext.splits && x.k_new != nullptr && rope_ok) {
@@ -818,25 +825,33 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             }
             uint32_t valid;
             if constexpr (kFused) {
-                valid = stage_valid[s];
-                if (valid == 0) break;  // the producer ran out of tiles
+                const uint32_t rows = stage_valid[s];
+                if (rows == 0) break;  // the producer ran out of tiles
+                // this warp's sub-tile: rows [16 sub, 16 sub + 16) of the stage
+                valid = rows > sub * kTile ? min(static_cast<uint32_t>(kTile), rows - sub * kTile) : 0u;
+                if (kSub > 1 && valid == 0) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
+                    continue;
+                }
             } else {
                 valid = min(static_cast<uint32_t>(kTile), end - (begin + i * kTile));
             }
-            const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * (2 * kTile * 128);
+            // head kvh's two 64-column blocks of the stage are kRows rows each
+            const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * (2 * kRows * 128) + sub * (kTile * 128);
             const uint8_t* vt = kt + tile_bytes;
             float sc[4];
             uint4 va[4][2];
             if (valid == kTile) {
                 uint4 ka[4], kb[4];
-                load_k_frags_sw<false>(kt, g, t, valid, ka, kb);
+                load_k_frags_sw<false, kRows * 128>(kt, g, t, valid, ka, kb);
                 tile_scores<false>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
-                load_v_frags_sw<false>(vt, g, t, valid, va);
+                load_v_frags_sw<false, kRows * 128>(vt, g, t, valid, va);
             } else {
                 uint4 ka[4], kb[4];
-                load_k_frags_sw<true>(kt, g, t, valid, ka, kb);
+                load_k_frags_sw<true, kRows * 128>(kt, g, t, valid, ka, kb);
                 tile_scores<true>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
-                load_v_frags_sw<true>(vt, g, t, valid, va);
+                load_v_frags_sw<true, kRows * 128>(vt, g, t, valid, va);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);  // the stage can be refilled
@@ -1137,42 +1152,49 @@ int ensure_tma_smem() {
 // Tensor maps of one cache (K or V): rows of num_kv_heads * 256 bytes, boxes
 // of kTile rows. A few per thread are kept: the eager launchers re-use them
 // layer after layer while the length and base are unchanged.
-int cache_tensor_map(CUtensorMap* out, const void* base, uint32_t rows, uint32_t num_kv_heads) {
+int cache_tensor_map(CUtensorMap* out, const void* base, uint32_t rows, uint32_t num_kv_heads, uint32_t box_rows) {
     struct Entry {
         const void* base;
-        uint32_t rows, kvh;
+        uint32_t rows, kvh, box_rows;
         CUtensorMap map;
     };
     thread_local Entry cache[8] = {};
     thread_local uint32_t next = 0;
     for (const Entry& e : cache)
-        if (e.base == base && e.rows == rows && e.kvh == num_kv_heads) {
+        if (e.base == base && e.rows == rows && e.kvh == num_kv_heads && e.box_rows == box_rows) {
             *out = e.map;
             return B2_OK;
         }
     Entry& e = cache[next++ & 7];
-    if (encode_token_rows_by_column_block(&e.map, base, rows, num_kv_heads * 256u, kTile) != 0) {
+    if (encode_token_rows_by_column_block(&e.map, base, rows, num_kv_heads * 256u, box_rows) != 0) {
         e.base = nullptr;
         return B2_ERR_CUDA;
     }
     e.base = base;
     e.rows = rows;
     e.kvh = num_kv_heads;
+    e.box_rows = box_rows;
     *out = e.map;
     return B2_OK;
 }
 
-// Ring depth: each stage is always consumed by the same warp of a KV head (a
-// warp waits on a stage's next phase only after consuming the current one),
-// so the depth is a multiple of the consumer warps per head.
-uint32_t tma_stages(uint32_t num_kv_heads) {
-    const uint32_t stage_bytes = 2u * kTile * num_kv_heads * 256u;
-    const uint32_t npar = kTmaConsumers / num_kv_heads;
+// Tokens per ring stage of the TMA kernel (its kRows): the fused step stages
+// 4 / KVH sixteen-token sub-tiles per head when there are fewer than 4 KV heads.
+uint32_t stage_rows(uint32_t num_kv_heads, bool fused) {
+    return fused && num_kv_heads < 4 ? kTile * (4u / num_kv_heads) : kTile;
+}
+
+// Ring depth: each stage is always consumed by the same warps (a warp waits
+// on a stage's next phase only after consuming the current one), so the depth
+// is a multiple of the stage parities.
+uint32_t tma_stages(uint32_t num_kv_heads, uint32_t rows) {
+    const uint32_t stage_bytes = 2u * rows * num_kv_heads * 256u;
+    const uint32_t npar = kTmaConsumers / (num_kv_heads * (rows / kTile));
     return (kTmaSmemBudget / stage_bytes) / npar * npar;
 }
 
-size_t tma_smem_bytes(uint32_t num_kv_heads, uint32_t stages) {
-    return static_cast<size_t>(stages) * 2u * kTile * num_kv_heads * 256u + 2 * stages * sizeof(uint64_t) +
+size_t tma_smem_bytes(uint32_t num_kv_heads, uint32_t stages, uint32_t rows) {
+    return static_cast<size_t>(stages) * 2u * rows * num_kv_heads * 256u + 2 * stages * sizeof(uint64_t) +
            1024;  // alignment slack
 }
 
@@ -1180,10 +1202,11 @@ size_t tma_smem_bytes(uint32_t num_kv_heads, uint32_t stages) {
 template <bool kFused>
 int launch_tma_kernel(const DecodeArgs& a, const StepExt& x, uint32_t grid, uint32_t map_rows, cudaStream_t stream) {
     CUtensorMap mk, mv;
-    int st = cache_tensor_map(&mk, a.k, map_rows, a.num_kv_heads);
-    if (st == B2_OK) st = cache_tensor_map(&mv, a.v, map_rows, a.num_kv_heads);
+    const uint32_t rows = stage_rows(a.num_kv_heads, kFused);
+    int st = cache_tensor_map(&mk, a.k, map_rows, a.num_kv_heads, rows);
+    if (st == B2_OK) st = cache_tensor_map(&mv, a.v, map_rows, a.num_kv_heads, rows);
     if (st != B2_OK) return st;
-    const size_t smem = tma_smem_bytes(a.num_kv_heads, a.stages);
+    const size_t smem = tma_smem_bytes(a.num_kv_heads, a.stages, rows);
     switch (a.num_kv_heads) {
         case 1:
             return launch_pdl(decode_tma_kernel<kFused, 1>, dim3(grid), dim3(kTmaThreads), smem, stream, a, x, mk, mv);
@@ -1268,7 +1291,7 @@ int launch_decode(const void* d_q, const void* d_k, const void* d_v, void* d_out
     int st;
     if (tma_ok) {
         if ((st = ensure_tma_smem()) != B2_OK) return st;
-        a.stages = tma_stages(a.num_kv_heads);
+        a.stages = tma_stages(a.num_kv_heads, stage_rows(a.num_kv_heads, false));
         if (a.stages == 0) return B2_ERR_UNSUPPORTED;
         a.splits_cap = static_cast<uint32_t>(device_sms());
         const uint32_t grid = static_cast<uint32_t>(chunks < a.splits_cap ? chunks : a.splits_cap);
@@ -1372,7 +1395,7 @@ int launch_decode_step(const void* d_q, const void* d_k_new, const void* d_v_new
     a.kv_len_bias = kv_len_bias;
     a.max_kv_len = static_cast<uint32_t>(max_kv_len);
     a.split_tokens = kStepSplitTokens;
-    a.stages = tma_stages(a.num_kv_heads);
+    a.stages = tma_stages(a.num_kv_heads, stage_rows(a.num_kv_heads, true));
     if (a.stages == 0) return B2_ERR_UNSUPPORTED;
 
     StepExt x{};
@@ -1463,8 +1486,9 @@ extern "C" int b2_update_causal_attention_decode_node(b2_graph_exec_t graph_exec
     if (tma) {
         // the tensor maps cover the cache rows read at the new length
         x = *static_cast<const StepExt*>(params.kernelParams[1]);
-        int s2 = cache_tensor_map(&mk, a.k, a.kv_len, a.num_kv_heads);
-        if (s2 == B2_OK) s2 = cache_tensor_map(&mv, a.v, a.kv_len, a.num_kv_heads);
+        const uint32_t rows = stage_rows(a.num_kv_heads, false);  // the patched nodes are split kernels
+        int s2 = cache_tensor_map(&mk, a.k, a.kv_len, a.num_kv_heads, rows);
+        if (s2 == B2_OK) s2 = cache_tensor_map(&mv, a.v, a.kv_len, a.num_kv_heads, rows);
         if (s2 != B2_OK) return s2;
     }
     void* args[4] = {&a, &x, &mk, &mv};

@@ -240,8 +240,10 @@ __device__ __forceinline__ void store_warp_partial(const WarpState& st, float* p
 // of each V fragment load on disjoint slot pairs (no bank conflicts).
 __device__ __forceinline__ uint32_t tile_token(uint32_t m) { return m ^ ((m & 1u) << 2); }
 
-// K fragments of one head: kt = the head's first column block.
-template <bool kPartial>
+// K fragments of one head: kt = the head's 16 rows in its first column block,
+// the second block kBlk bytes further (blocks of more than 16 rows when a
+// stage carries several 16-token sub-tiles).
+template <bool kPartial, uint32_t kBlk = kTile * 128>
 __device__ __forceinline__ void load_k_frags_sw(const uint8_t* kt, int g, int t, uint32_t valid, uint4 (&ka)[4],
                                                 uint4 (&kb)[4]) {
     const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
@@ -249,7 +251,7 @@ __device__ __forceinline__ void load_k_frags_sw(const uint8_t* kt, int g, int t,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t chunk = ((j & 1) * 4 + t) ^ tok;
-        const uint8_t* pa = kt + (j >> 1) * (kTile * 128) + tok * 128 + chunk * 16;
+        const uint8_t* pa = kt + (j >> 1) * kBlk + tok * 128 + chunk * 16;
         ka[j] = (!kPartial || tok < valid) ? *reinterpret_cast<const uint4*>(pa) : zero4;
         kb[j] = (!kPartial || tok + 8 < valid) ? *reinterpret_cast<const uint4*>(pa + 8 * 128) : zero4;
     }
@@ -257,7 +259,7 @@ __device__ __forceinline__ void load_k_frags_sw(const uint8_t* kt, int g, int t,
 
 // V fragments of one head: contraction rows 2t, 2t+1, 2t+8, 2t+9 (their
 // tokens via tile_token), head_dim halves 64b + 8g.
-template <bool kPartial>
+template <bool kPartial, uint32_t kBlk = kTile * 128>
 __device__ __forceinline__ void load_v_frags_sw(const uint8_t* vt, int g, int t, uint32_t valid,
                                                 uint4 (&va)[4][2]) {
     const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
@@ -267,7 +269,7 @@ __device__ __forceinline__ void load_v_frags_sw(const uint8_t* vt, int g, int t,
 #pragma unroll
         for (int b = 0; b < 2; ++b)
             va[r][b] = (!kPartial || tok < valid)
-                           ? *reinterpret_cast<const uint4*>(vt + b * (kTile * 128) + tok * 128 +
+                           ? *reinterpret_cast<const uint4*>(vt + b * kBlk + tok * 128 +
                                                              ((static_cast<uint32_t>(g) ^ (tok & 7u)) << 4))
                            : zero4;
     }

@@ -220,10 +220,16 @@ def test_fused_rank_partials_merge_to_oracle(cuda, ranks):
     assert_attention_close(host(out), o32)
 
 
-@pytest.mark.parametrize("kvh,heads", [(1, 8), (2, 16), (8, 32)])
-def test_fused_step_other_gqa_shapes(cuda, kvh, heads):
+@pytest.mark.parametrize("kvh,heads,kv_len", [
+    (1, 8, 5000), (2, 16, 5000), (8, 32, 5000),
+    # one or two KV heads (a tensor-parallel rank's share): stages of 64 / 32
+    # tokens split into 16-token sub-tiles, partial stages at every boundary
+    (1, 4, 1), (1, 4, 17), (1, 4, 63), (1, 4, 64), (1, 4, 65), (1, 4, 1000), (1, 4, 65537),
+    (2, 8, 15), (2, 8, 32), (2, 8, 33), (2, 8, 4097),
+])
+def test_fused_step_other_gqa_shapes(cuda, kvh, heads, kv_len):
     import torch
-    kv_len, cap = 5000, 5010
+    cap = kv_len + 10
     hist_k = seeded_f16((cap, kvh * D), 91 + kvh)
     hist_v = seeded_f16((cap, kvh * D), 92 + kvh)
     qkv = seeded_f16(heads * D + 2 * kvh * D, 93 + kvh)

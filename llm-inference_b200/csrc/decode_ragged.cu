@@ -19,10 +19,12 @@
 //     stage ring, plus the sequence's Q row into one of two Q slots; the unit
 //     is padded with empty stages to a multiple of the consumer parities so
 //     every consumer warp sees every unit.
-//   * 12 consumer warps (KV head x tile parity) run the same MMA tile math as
-//     the single-sequence kernel and, at each unit boundary, write their own
-//     (o, m, l) state as a partial: no CTA-wide barrier per unit, so the
-//     producer keeps streaming across unit boundaries.
+//   * 12 consumer warps (KV head x tile parity; with fewer than 4 KV heads a
+//     stage holds several 16-token sub-tiles per head, one per warp) run the
+//     same MMA tile math as the single-sequence kernel and, at each unit
+//     boundary, write their own (o, m, l) state as a partial: no CTA-wide
+//     barrier per unit, so the producer keeps streaming across unit
+//     boundaries.
 //   * A merge kernel (one CTA per (sequence, head), four groups of 128
 //     threads) folds the npar partials of each of the sequence's units and
 //     writes the fp16 output.
@@ -54,6 +56,10 @@ constexpr uint32_t kNoUnit = 0xffffffffu;
 // units (balance), since each unit costs npar partials per head (traffic).
 constexpr uint32_t kRgHalfUnitsPerCta = 9;
 __host__ __device__ constexpr uint32_t rg_npar(uint32_t kvh) { return kRgConsumers / kvh; }
+// With fewer than 4 KV heads a stage carries 4 / KVH sixteen-token sub-tiles
+// per head (16 KB per operand: a one-head row is 256 B), one per warp of a
+// stage parity; units stay multiples of npar tiles = (npar / sub) stages.
+__host__ __device__ constexpr uint32_t rg_sub(uint32_t kvh) { return kvh < 4 ? 4 / kvh : 1; }
 __host__ __device__ constexpr uint32_t rg_round_tiles(uint32_t kvh, uint32_t tiles) {
     return rg_npar(kvh) * ((tiles + rg_npar(kvh) - 1) / rg_npar(kvh));
 }
@@ -115,9 +121,12 @@ template <uint32_t KVH, bool kStep>
 __global__ void __launch_bounds__(kRgThreads, 1)
     decode_ragged_kernel(const RaggedArgs a, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v) {
-    constexpr uint32_t npar = rg_npar(KVH);
+    constexpr uint32_t npar = rg_npar(KVH);        // consumer warps per KV head (partials per unit and head)
+    constexpr uint32_t kSub = rg_sub(KVH);         // 16-token sub-tiles per head in a stage
+    constexpr uint32_t kRows = kTile * kSub;       // tokens per stage
+    constexpr uint32_t spar = npar / kSub;         // stage parities
     constexpr uint32_t row_bytes = KVH * 256;
-    constexpr uint32_t tile_bytes = kTile * row_bytes;
+    constexpr uint32_t tile_bytes = kRows * row_bytes;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t prefix[kRgMaxSeqs + 1];  // units before sequence b
     __shared__ uint32_t lens[kRgMaxSeqs];
@@ -179,7 +188,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     if (threadIdx.x == 32) {
         for (uint32_t s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], KVH);
+            mbar_init(&empty[s], KVH * kSub);
         }
         for (uint32_t s = 0; s < kRgQSlots; ++s) {
             mbar_init(&qfull[s], 1);
@@ -214,8 +223,8 @@ __global__ void __launch_bounds__(kRgThreads, 1)
             const uint32_t b = lo, len = lens[b];
             const uint32_t t_begin = (u - prefix[b]) * unit_tokens;
             const uint32_t t_end = min(len, t_begin + unit_tokens);
-            const uint32_t ntiles = (t_end - t_begin + kTile - 1) / kTile;
-            const uint32_t nstages = (ntiles + npar - 1) / npar * npar;
+            const uint32_t ntiles = (t_end - t_begin + kRows - 1) / kRows;
+            const uint32_t nstages = (ntiles + spar - 1) / spar * spar;
             // fused step: rotate Q (position in the tables), append the new row
             // (its unit is the sequence's last; the position is in the cache)
             int32_t p = 0;
@@ -292,11 +301,11 @@ __global__ void __launch_bounds__(kRgThreads, 1)
                     __syncwarp();
                 }
                 if (lane == 0) {
-                    const uint32_t t0 = t_begin + j * kTile;
+                    const uint32_t t0 = t_begin + j * kRows;
                     st_unit[s] = u;
                     st_local[s] = k;
                     if (j < ntiles) {
-                        st_valid[s] = min(static_cast<uint32_t>(kTile), t_end - t0);
+                        st_valid[s] = min(kRows, t_end - t0);
                         mbar_arrive_expect_tx(&full[s], 2 * tile_bytes);
                         uint8_t* stg = ring + s * 2 * tile_bytes;
                         tc::tma_load_4d_hint(stg, &map_k, 0, static_cast<int32_t>(t0), 0, static_cast<int32_t>(b),
@@ -314,8 +323,8 @@ __global__ void __launch_bounds__(kRgThreads, 1)
             ++k;
         }
         if (ok) {
-            // one end marker per consumer parity
-            for (uint32_t e = 0; e < npar; ++e, ++i) {
+            // one end marker per stage parity
+            for (uint32_t e = 0; e < spar; ++e, ++i) {
                 const uint32_t s = i % stages, round = i / stages;
                 if (lane == 0) {
                     if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) ok = false;
@@ -334,25 +343,28 @@ __global__ void __launch_bounds__(kRgThreads, 1)
                 (void)mbar_wait(&qfull[j % kRgQSlots], (j / kRgQSlots) & 1);
         }
     } else if (static_cast<uint32_t>(warp) / KVH < npar) {
-        // ---- consumers: warp = KV head (warp % KVH) x tile parity (warp / KVH)
-        const uint32_t kvh = warp % KVH, par = warp / KVH;
+        // ---- consumers: warp = KV head (warp % KVH) x j (warp / KVH): sub-tile
+        // j % kSub of every spar-th stage from stage parity j / kSub
+        const uint32_t kvh = warp % KVH, jw = warp / KVH, sub = jw % kSub, par = jw / kSub;
         const int g = lane >> 2, t = lane & 3;
         WarpState st;
         state_init(st);
         uint32_t qf[8][2];
         uint32_t cur_local = kNoUnit, cur_unit = 0;
-        for (uint32_t i = par;; i += npar) {
+        for (uint32_t i = par;; i += spar) {
             const uint32_t s = i % stages, round = i / stages;
             if (!mbar_wait(&full[s], round & 1)) {
                 ok = false;
                 break;
             }
-            const uint32_t u = st_unit[s], kl = st_local[s], valid = st_valid[s];
+            const uint32_t u = st_unit[s], kl = st_local[s], rows = st_valid[s];
+            // this warp's rows of the stage: [16 sub, 16 sub + 16)
+            const uint32_t valid = rows > sub * kTile ? min(static_cast<uint32_t>(kTile), rows - sub * kTile) : 0u;
             if (u == kNoUnit || kl != cur_local) {
                 if (cur_local != kNoUnit) {
                     state_finish(st);
                     store_warp_partial(st, a.po, a.pm, a.pl, 128, static_cast<uint64_t>(a.num_heads) * 128, 64, 1,
-                                       a.num_heads, cur_unit * npar + par, kvh * a.group, a.group, g, t);
+                                       a.num_heads, cur_unit * npar + jw, kvh * a.group, a.group, g, t);
                     state_init(st);
                 }
                 if (u == kNoUnit) break;
@@ -381,20 +393,21 @@ __global__ void __launch_bounds__(kRgThreads, 1)
                 cur_unit = u;
             }
             if (valid != 0) {
-                const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * (2 * kTile * 128);
+                // head kvh's two 64-column blocks of the stage are kRows rows each
+                const uint8_t* kt = ring + s * 2 * tile_bytes + kvh * (2 * kRows * 128) + sub * (kTile * 128);
                 const uint8_t* vt = kt + tile_bytes;
                 float sc[4];
                 uint4 va[4][2];
                 if (valid == kTile) {
                     uint4 ka[4], kb[4];
-                    load_k_frags_sw<false>(kt, g, t, valid, ka, kb);
+                    load_k_frags_sw<false, kRows * 128>(kt, g, t, valid, ka, kb);
                     tile_scores<false>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
-                    load_v_frags_sw<false>(vt, g, t, valid, va);
+                    load_v_frags_sw<false, kRows * 128>(vt, g, t, valid, va);
                 } else {
                     uint4 ka[4], kb[4];
-                    load_k_frags_sw<true>(kt, g, t, valid, ka, kb);
+                    load_k_frags_sw<true, kRows * 128>(kt, g, t, valid, ka, kb);
                     tile_scores<true>(sc, ka, kb, qf, tile_token(g), valid, a.scale_log2);
-                    load_v_frags_sw<true>(vt, g, t, valid, va);
+                    load_v_frags_sw<true, kRows * 128>(vt, g, t, valid, va);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
@@ -586,11 +599,13 @@ int launch_ragged(RaggedCall c, cudaStream_t stream) {
     const RgWorkspace w = rg_layout(c.num_seqs, c.num_heads, c.num_kv_heads, c.max_kv_len);
     if (c.workspace_bytes < w.total_bytes) return B2_ERR_WORKSPACE;
     const uint32_t kvh = static_cast<uint32_t>(c.num_kv_heads);
-    const uint32_t npar = rg_npar(kvh);
-    const size_t stage_bytes = 2ull * kTile * kvh * 256;
+    const uint32_t npar = rg_npar(kvh);                     // partials per unit and head
+    const uint32_t rows = kTile * rg_sub(kvh);             // tokens per stage
+    const uint32_t spar = rg_npar(kvh) / rg_sub(kvh);       // stage parities: the ring depth's divisor
+    const size_t stage_bytes = 2ull * rows * kvh * 256;
     const size_t fixed = 1024 + kRgQSlots * rg_qslot_bytes(static_cast<uint32_t>(c.num_heads), c.step) + 256;
-    uint32_t stages = static_cast<uint32_t>((kRgSmemLimit - fixed) / stage_bytes) / npar * npar;
-    if (stages > 32) stages = 32 / npar * npar;
+    uint32_t stages = static_cast<uint32_t>((kRgSmemLimit - fixed) / stage_bytes) / spar * spar;
+    if (stages > 32) stages = 32 / spar * spar;
     if (stages == 0) return B2_ERR_UNSUPPORTED;
 
     float* ws = static_cast<float*>(c.workspace);
@@ -627,9 +642,9 @@ int launch_ragged(RaggedCall c, cudaStream_t stream) {
 
     CUtensorMap mk, mv;
     if (encode_token_rows_by_column_block_seqs(&mk, c.k_cache, c.max_kv_len, kvh * 256, c.num_seqs,
-                                               c.cache_seq_stride * 2, kTile) != 0 ||
+                                               c.cache_seq_stride * 2, rows) != 0 ||
         encode_token_rows_by_column_block_seqs(&mv, c.v_cache, c.max_kv_len, kvh * 256, c.num_seqs,
-                                               c.cache_seq_stride * 2, kTile) != 0)
+                                               c.cache_seq_stride * 2, rows) != 0)
         return B2_ERR_CUDA;
     const size_t smem = fixed + stages * stage_bytes + 2 * (stages + kRgQSlots) * sizeof(uint64_t);
     const uint32_t grid = static_cast<uint32_t>(device_sms_rg());

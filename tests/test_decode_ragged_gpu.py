@@ -226,12 +226,14 @@ def _oracle_ragged_step(qkv, kh, vh, pos, cos, sin, rotate, H, KVH, max_len):
 
 
 @pytest.mark.parametrize("rotate", [True, False])
-def test_ragged_fused_step_vs_oracle(cuda, rotate):
+@pytest.mark.parametrize("H,KVH", [(16, 4), (4, 1), (8, 2)])
+def test_ragged_fused_step_vs_oracle(cuda, rotate, H, KVH):
     """One call per layer: RoPE of each sequence's new token, its K/V append and
     the ragged decode; caches bit-exact vs the oracle, outputs within tolerance,
-    the QKV rows untouched. Positions at 0, tile and unit edges, and the last row."""
+    the QKV rows untouched. Positions at 0, tile and unit edges, and the last
+    row; one and two KV heads (a tensor-parallel rank's share) included."""
     import torch
-    H, KVH, max_len = 16, 4, 2048
+    max_len = 2048
     pos = [0, 1, 15, 16, 255, 256, 287, 288, 767, 768, 1000, max_len - 1]
     B = len(pos)
     total = H * D + 2 * KVH * D

@@ -583,6 +583,10 @@ def run_ragged(args, rank, world, dev):
     # sequences among themselves. By sequence: whole sequences per rank.
     hs = (bdist.head_split_plan(KVH, world, rank) if split == "heads"
           else bdist.HeadSplit(world, rank, KVH, 0, KVH, tuple(range(world))))
+    share = tp_share(args, world)
+    if share > 1:  # one GPU running rank 0's share of a `share`-way KV-head split
+        hs = bdist.HeadSplit(1, 0, KVH, 0, KVH // share, (0,))
+        split = "heads"
     kvh_l = hs.local_kv_heads
     h_l = kvh_l * (H // KVH)
     q_l, kv_l = h_l * D, kvh_l * D
@@ -654,7 +658,7 @@ def run_ragged(args, rank, world, dev):
     graph.reset()
     # K+V rows read + Q + output + appended row, every sequence, every layer
     seq_bytes = lambda n: 2 * n * KV_DIM * 2 + Q_DIM * 2 + Q_DIM * 2 + 2 * KV_DIM * 2
-    total = sum(seq_bytes(n) for n in lens_all) * LAYERS * steps
+    total = sum(seq_bytes(n) for n in lens_all) * LAYERS * steps // share
 
     # ---- e2e: every step copies this rank's 36 x B new [Q|K|V] rows and the
     # positions in from pinned host memory, issues the 36 fused ragged calls
@@ -711,7 +715,10 @@ def run_ragged(args, rank, world, dev):
     return {"metric": "ragged decode KV-read GB/s", "value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "workload": RG_WORKLOAD, "steps": steps, "ms_per_step": round(ms / steps, 4),
             "gpu_launches": per_step * steps, "sequences_per_rank": B,
-            "parallelism": (f"sequences over {world} GPU(s), greedy longest-first" if split != "heads" else
+            "parallelism": (f"one GPU running rank 0's share of a {share}-way KV-head split ({kvh_l} KV head(s) / "
+                            f"{h_l} query heads of every sequence): per-rank work, not a whole-job number"
+                            if share > 1 else
+                            f"sequences over {world} GPU(s), greedy longest-first" if split != "heads" else
                             f"kv-heads over {world} GPU(s): {kvh_l} KV head(s) / {h_l} query heads of every "
                             "sequence per rank (own cache of those heads, head-sharded output)"
                             + (f", sequences split greedily over the {hs.group_world} ranks of each head"
@@ -1053,6 +1060,15 @@ def run_qkv_proj(args, dev):
             "clocks": clk, "gpu_launches": launches}
 
 
+def tp_share(args, world):
+    """--tp-share S (one GPU only): run rank 0's share of an S-way KV-head
+    split, to measure a tensor-parallel rank's work without the other ranks."""
+    share = int(getattr(args, "tp_share", 1) or 1)
+    if share > 1 and (world != 1 or KVH % share != 0):
+        raise SystemExit(f"--tp-share {share} needs one GPU and a divisor of the {KVH} KV heads")
+    return share
+
+
 def decode_parallelism(split, hs, h_l, exchange):
     xch = ("cross-rank merge in the fused kernel over CUDA-IPC peer memory" if exchange == "peer"
            else "NCCL all-gather of rank partials + merge kernel")
@@ -1083,6 +1099,9 @@ def run_b200(args, rank, world):
     # that share them, which split the KV range among themselves
     hs = (bdist.head_split_plan(KVH, world, rank) if split == "heads"
           else bdist.HeadSplit(world, rank, KVH, 0, KVH, tuple(range(world))))
+    share = tp_share(args, world)
+    if share > 1:  # one GPU running rank 0's share of a `share`-way KV-head split
+        hs = bdist.HeadSplit(1, 0, KVH, 0, KVH // share, (0,))
     kvh_l = hs.local_kv_heads
     h_l = kvh_l * (H // KVH)
     q_l, kv_l = h_l * D, kvh_l * D
@@ -1106,7 +1125,8 @@ def run_b200(args, rank, world):
     out_host = torch.zeros_like(out, device="cpu").pin_memory()
     step_state = bdist.DecodeStepState(plan, h_l, kvh_l, D, LAYERS, capacity, max_global, dev, fused=not args.unfused,
                                        exchange=args.exchange, members=hs.group, job_world=world,
-                                       job_kv_dim=KV_DIM, job_q_dim=Q_DIM, pipeline=args.pipeline_exchange)
+                                       job_kv_dim=KV_DIM // share, job_q_dim=Q_DIM // share,
+                                       pipeline=args.pipeline_exchange)
 
     stream = torch.cuda.Stream(device=dev)
     group = None
@@ -1169,7 +1189,7 @@ def run_b200(args, rank, world):
     barrier()
     ms = ev0.elapsed_time(ev1)
     ms = bdist.max_over_ranks(ms, dev) if world > 1 else ms
-    total_bytes = sum(step_bytes(PAST + 1 + align + s) for s in range(args.steps))
+    total_bytes = sum(step_bytes(PAST + 1 + align + s) for s in range(args.steps)) // share
     value = total_bytes / (ms / 1e3) / 1e9
 
     # ---- roofline: one layer's decode launch(es), CUDA events on its stream
@@ -1252,7 +1272,10 @@ def run_b200(args, rank, world):
                     + ("; layers pipelined across the exchange (not valid for a model)" if step_state.pipeline
                        else ""),
             "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": PAST, "layers": LAYERS,
-                       "parallelism": (decode_parallelism(split, hs, h_l, step_state.exchange) +
+                       "parallelism": (f"one GPU running rank 0's share of a {share}-way KV-head split ({kvh_l} KV "
+                                       f"head(s) / {h_l} query heads): per-rank work, not a whole-job number"
+                                       if share > 1 else
+                                       decode_parallelism(split, hs, h_l, step_state.exchange) +
                                        ("; SYNTHETIC: layer l's all-gather + merge on a second stream under layer "
                                         "l+1's kernel, valid only because this benchmark's Q rows do not depend on "
                                         "the previous layer" if step_state.pipeline else "")) if world > 1
@@ -1297,6 +1320,9 @@ def main():
     ap.add_argument("--no-small", action="store_true", help="skip the config-1/2 (latency-bound) sub-measurement")
     ap.add_argument("--no-out-proj", action="store_true", help="skip the attention output projection measurement")
     ap.add_argument("--no-qkv-proj", action="store_true", help="skip the QKV projection (+ RoPE/append) measurement")
+    ap.add_argument("--tp-share", type=int, default=1,
+                    help="one GPU: run rank 0's share of an S-way KV-head split of the decode and ragged legs "
+                         "(per-rank work; the line says so)")
     ap.add_argument("--ragged-split", default="seqs", choices=["seqs", "heads"],
                     help="N > 1 ragged decode: whole sequences per rank, or KV heads per rank (tensor-parallel layout)")
     ap.add_argument("--decode-split", default="auto", choices=["auto", "heads", "kv"],

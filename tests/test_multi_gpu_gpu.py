@@ -18,7 +18,7 @@ import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-H, KVH, D = 16, 4, 128
+H_ALL, KVH_ALL, D = 16, 4, 128
 PAST, LAYERS, STEPS = 9000, 2, 3
 
 
@@ -28,7 +28,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, exchange, split, q, pipeline=False):
+def _worker(rank, world, port, exchange, split, q, pipeline=False, heads=None):
     try:
         import sys
         root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -43,6 +43,7 @@ def _worker(rank, world, port, exchange, split, q, pipeline=False):
         from _util import assert_attention_close, seeded_f16
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
+        H, KVH = heads if heads is not None else (H_ALL, KVH_ALL)
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         backend = "nccl" if exchange == "nccl" else "gloo"
         tdist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
@@ -106,19 +107,21 @@ def _worker(rank, world, port, exchange, split, q, pipeline=False):
         q.put((rank, traceback.format_exc()))
 
 
-def _run(exchange, split="kv", max_world=4, pipeline=False):
+def _run(exchange, split="kv", max_world=4, pipeline=False, heads=None):
     import torch
     import multiprocessing as mp
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 or more GPUs (one process per GPU)")
     world = min(n, max_world)
-    if split == "heads" and KVH % world != 0 and world % KVH != 0:
+    kvh = heads[1] if heads is not None else KVH_ALL
+    if split == "heads" and kvh % world != 0 and world % kvh != 0:
         world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, split, q, pipeline)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, split, q, pipeline, heads))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -163,3 +166,12 @@ def test_head_split_decode_with_range_split_peer(cuda):
 
 def test_head_split_decode_with_range_split_nccl(cuda):
     _run("nccl", "heads", max_world=8)
+
+
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_one_kv_head_range_split_across_all_ranks(cuda, exchange):
+    """A model with one KV head (4 query heads): the head split gives every
+    rank the same head, so all ranks split its range and exchange -- the
+    sub-tiled one-head stages together with the cross-rank merge, on as many
+    GPUs as there are (up to 8)."""
+    _run(exchange, "heads", max_world=8, heads=(4, 1))

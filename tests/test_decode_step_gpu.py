@@ -130,6 +130,49 @@ def test_fused_step_workspace_counters_return_to_zero(cuda):
     assert b200attn.lib().b2_device_error_word() == 0
 
 
+def test_fused_step_length_written_by_previous_kernel(cuda):
+    """The kernel reads the length before its dependency wait to load its first
+    tiles early; when the kernel before it on the stream writes that length
+    (here: a long fused step on another cache, then the position advance), the
+    early read is usually stale. The stages loaded for the stale length must be
+    skipped and the output be that of the new length, for a longer and a
+    shorter new length."""
+    import torch
+    cap = 9000
+    hist_k = seeded_f16((cap, KVH * D), 141, std=0.5)
+    hist_v = seeded_f16((cap, KVH * D), 142, std=0.5)
+    kc, vc = dev(hist_k), dev(hist_v)
+    cos, sin = b200attn.rope_tables_host(cap, D, THETA)
+    cos_d, sin_d = dev(cos), dev(sin)
+    # the long kernel in front: a 64K step on its own cache and workspace
+    big = 65536 + 8
+    fk = torch.zeros((big, KVH * D), dtype=torch.float16, device=cuda)
+    fv = torch.zeros_like(fk)
+    fq = dev(seeded_f16(H * D + 2 * KVH * D, 143))
+    fpos = torch.tensor([65536], dtype=torch.int32, device=cuda)
+    fout = torch.empty(H * D, dtype=torch.float16, device=cuda)
+    fws = _workspace()
+    ws = _workspace()
+    for start, delta in ((3000, 1000), (6000, -2500)):
+        qkv = seeded_f16(H * D + 2 * KVH * D, 150 + start, std=0.5)
+        qkv_d = dev(qkv)
+        ln = torch.tensor([start], dtype=torch.int32, device=cuda)  # kv_len = ln, attended history only
+        pos = torch.tensor([start + delta - 1], dtype=torch.int32, device=cuda)
+        out = torch.empty(H * D, dtype=torch.float16, device=cuda)
+        _sync()
+        _fused(fq, fk, fv, cos_d, sin_d, big, False, fpos, fpos, 1, big, fout, fws, append=False)
+        b200attn.advance_position(ln, delta)
+        _fused(qkv_d, kc, vc, cos_d, sin_d, cap, True, pos, ln, 0, cap, out, ws, append=False)
+        _sync()
+        kv_len = start + delta
+        oq = qkv[:H * D].copy()
+        ok = qkv[H * D:H * D + KVH * D].copy()
+        oracle.rope_and_store_kv(oq, ok, None, None, None, cos, sin, 1, H, KVH, D, H * D, KVH * D, kv_len - 1, True)
+        _, o32 = oracle.decode_attention(oq, hist_k, hist_v, kv_len, H, KVH, D)
+        assert_attention_close(host(out), o32.reshape(-1))
+    assert b200attn.lib().b2_device_error_word() == 0
+
+
 def test_fused_step_graph_decode_sequence(cuda):
     """A captured 2-layer step replayed for 6 tokens with a device position:
     every token's output of both layers matches the oracle's sequential decode."""

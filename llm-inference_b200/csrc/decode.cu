@@ -690,12 +690,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             const uint32_t pool = per * ext.splits, pool_end = total - 1;
             const bool tail_split = split + 1 == ext.splits;
             uint32_t own = split * per + use_pre, own_end = split * per + per;
-            // With an own share the first claim goes out after the first copy
-            // (its round trip is hidden behind the share); without one, now.
-            uint32_t claimed = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], 1u) : 0u;
-            uint32_t claimed2 = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], 1u) : 0u;
+            // With an own share still to copy the first claims go out after the
+            // first copy (their round trip is hidden behind the share); without
+            // one, or with the share's first tiles already in the ring (loaded
+            // before the wait), now.
+            const bool claim_now = per == 0 || use_pre > 0;
+            uint32_t claimed = lane == 0 && pool < pool_end && claim_now ? atomicAdd(&x.counters[0], 1u) : 0u;
+            uint32_t claimed2 = lane == 0 && pool < pool_end && claim_now ? atomicAdd(&x.counters[0], 1u) : 0u;
             bool toggle = false;
-            bool first_claim = per != 0 && pool < pool_end;
+            bool first_claim = !claim_now && pool < pool_end;
             // The tiles after the ones warmed before the wait: HBM starts on
             // them while the first copies come from L2.
             {

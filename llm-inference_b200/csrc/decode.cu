@@ -434,10 +434,8 @@ __device__ __forceinline__ void step_merge(const DecodeArgs& a, const StepExt& x
 }
 
 constexpr uint32_t kAppendBarrier = 1;  // named barrier: appending consumer warp -> producer warp
-constexpr uint32_t kPrefetchTiles = 4;       // static form: tiles per CTA warmed in L2 before the dependency wait
-constexpr uint32_t kPreloadStages = 4;       // fused step: own tiles copied into the ring before the wait,
-constexpr uint32_t kFusedPrefetchTiles = 2;  // the next ones warmed in L2 before it,
-constexpr uint32_t kPostPrefetchTiles = 2;   // and the next ones right after it
+constexpr uint32_t kPrefetchTiles = 4;  // tiles per CTA warmed in L2 before the dependency wait
+constexpr uint32_t kPostPrefetchTiles = 2;  // and the next ones, right after it
 
 // Fused kernel: tiles dealt out evenly to each split before the claimed pool
 // (half of them: at 64K a larger pool let the CTAs finish 0.2 us closer).
@@ -542,8 +540,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t stage_valid[32];  // kFused: rows of the tile in each stage, 0 = no more tiles
     __shared__ uint64_t merge_bar;        // kFused: bulk copies of the merge
-    __shared__ uint32_t pre_s[3];         // kFused: stages loaded before the dependency wait, and the
-                                          // length and split count they were chosen for
     constexpr uint32_t row_bytes = KVH * 256;          // one token, all KV heads
     // The fused step stages kSub 16-token sub-tiles per KV head when there are
     // fewer than 4 KV heads, so every stage carries 16 KB per operand (a
@@ -562,11 +558,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // While the previous kernel finishes (nothing here depends on its output):
-    // barriers, tensor-map prefetch, this CTA's first tiles (the fused step:
-    // copied into the ring; the static form: pulled into L2) and the next ones
-    // pulled into L2. The length read here may be stale (it can be the previous
-    // kernel's output): the L2 warm-up is a hint, and ring stages loaded for a
-    // length that no longer holds after the wait are skipped.
+    // barriers, tensor-map prefetch, and this CTA's first tiles pulled into
+    // L2. The length read for the prefetch may be stale (it can be the
+    // previous kernel's output); a prefetch only warms L2, so any tile below
+    // max_kv_len is harmless.
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
@@ -575,51 +570,25 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         if (kFused) mbar_init(&merge_bar, 1);
         fence_mbarrier_init();
     }
-    if (warp == kTmaConsumers && lane == 0) {
-        tc::prefetch_tensormap(&map_k);
-        tc::prefetch_tensormap(&map_v);
-    }
-    if (kFused && threadIdx.x == 0) pre_s[0] = 0;
-    __syncthreads();
     if (warp == kTmaConsumers) {
-        const Extent pre = decode_extent(a);
-        const bool has = split_index_ok(pre, blockIdx.x);
-        uint32_t first = 0, count = 0;  // tiles warmed in L2, from `first`
-        if constexpr (kFused) {
-            // The fused step's first own tiles go straight into the ring: they
-            // lie in the split's even share, i.e. strictly below the last tile
-            // (the one holding the new row, the only cached row a previous
-            // kernel may write), whatever length this (possibly stale) read
-            // gives. After the wait they are used if the length and split
-            // count are unchanged, else skipped; the next tiles are warmed in L2.
-            if (has) {
-                const uint32_t per = fused_share((pre.kv_len + kRows - 1) / kRows, pre.splits);
-                const uint32_t npre = min(min(per, stages), kPreloadStages);
-                first = blockIdx.x * per;
-                if (lane == 0) {
-                    for (uint32_t j = 0; j < npre; ++j) {
-                        const int32_t t0 = static_cast<int32_t>((first + j) * kRows);
-                        stage_valid[j] = kRows;
-                        mbar_arrive_expect_tx(&full[j], 2 * tile_bytes);
-                        tc::tma_load_3d(stg_of(ring, j, tile_bytes), &map_k, 0, t0, 0, &full[j]);
-                        tc::tma_load_3d(stg_of(ring, j, tile_bytes) + tile_bytes, &map_v, 0, t0, 0, &full[j]);
-                    }
-                    pre_s[0] = npre;
-                    pre_s[1] = pre.kv_len;
-                    pre_s[2] = pre.splits;
-                }
-                first += npre;
-                count = min(per - npre, kFusedPrefetchTiles);
-            }
-        } else {
-            // the static form warms its first tiles in L2 only
-            if (has) own_tiles(pre, blockIdx.x, false, kRows, first, count);
+        if (lane == 0) {
+            tc::prefetch_tensormap(&map_k);
+            tc::prefetch_tensormap(&map_v);
         }
-        if (static_cast<uint32_t>(lane) < 2 * count) {
-            const uint64_t off = static_cast<uint64_t>(first + (static_cast<uint32_t>(lane) >> 1)) * tile_bytes;
-            bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((lane & 1) ? a.v : a.k) + off, tile_bytes);
+        if (lane < 2 * kPrefetchTiles) {
+            const Extent pre = decode_extent(a);
+            if (split_index_ok(pre, blockIdx.x)) {
+                uint32_t first, count;
+                own_tiles(pre, blockIdx.x, kFused, kRows, first, count);
+                const uint32_t j = static_cast<uint32_t>(lane) >> 1;
+                if (j < count) {
+                    const uint64_t off = static_cast<uint64_t>(first + j) * tile_bytes;
+                    bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((lane & 1) ? a.v : a.k) + off, tile_bytes);
+                }
+            }
         }
     }
+    __syncthreads();
     pdl_wait_primary();  // Q, the cache and the device length may come from the previous kernel
     pdl_launch_dependents();
     // every load that only depends on the previous kernel goes out at once
@@ -632,18 +601,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     const Extent ext = decode_extent(a);
     const uint32_t split = blockIdx.x;
-    // Stages loaded before the wait, and how many of them this launch uses:
-    // all when the length and split count read before the wait still hold,
-    // none otherwise (the consumers then skip them once they have landed).
-    uint32_t loaded = 0, use_pre = 0;
-    if constexpr (kFused) {
-        __syncthreads();  // pre_s and stage_valid written before the wait
-        loaded = pre_s[0];
-        use_pre = (loaded > 0 && pre_s[1] == ext.kv_len && pre_s[2] == ext.splits) ? loaded : 0u;
-        // a CTA that leaves here must not leave copies in flight into its ring
-        if ((ext.splits == 0 || split >= ext.splits) && loaded > 0 && warp == kTmaConsumers && lane == 0)
-            for (uint32_t j = 0; j < loaded; ++j) (void)mbar_wait(&full[j], 0);
-    }
     if (kFused && ext.splits == 0) {  // empty cache: defined output
         if (split == 0) {
             if (x.world > 1) {
@@ -676,7 +633,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         const uint64_t policy = l2_evict_first_policy();
         uint32_t i = 0;
         if constexpr (kFused) {
-            i = loaded;  // stages 0 .. loaded - 1 went out before the wait
             // Tile order of split s: its even share [s*per, (s+1)*per) of ~1/2
             // of the tiles (the last split puts the last tile, which holds the
             // new row, after its first two, once consumer warp 0 has appended
@@ -689,29 +645,24 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             const uint32_t per = fused_share(total, ext.splits);  // per * S <= total - 1
             const uint32_t pool = per * ext.splits, pool_end = total - 1;
             const bool tail_split = split + 1 == ext.splits;
-            uint32_t own = split * per + use_pre, own_end = split * per + per;
-            // With an own share still to copy the first claims go out after the
-            // first copy (their round trip is hidden behind the share); without
-            // one, or with the share's first tiles already in the ring (loaded
-            // before the wait), now.
-            const bool claim_now = per == 0 || use_pre > 0;
-            uint32_t claimed = lane == 0 && pool < pool_end && claim_now ? atomicAdd(&x.counters[0], 1u) : 0u;
-            uint32_t claimed2 = lane == 0 && pool < pool_end && claim_now ? atomicAdd(&x.counters[0], 1u) : 0u;
+            uint32_t own = split * per, own_end = own + per;
+            // With an own share the first claim goes out after the first copy
+            // (its round trip is hidden behind the share); without one, now.
+            uint32_t claimed = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], 1u) : 0u;
+            uint32_t claimed2 = lane == 0 && pool < pool_end && per == 0 ? atomicAdd(&x.counters[0], 1u) : 0u;
             bool toggle = false;
-            bool first_claim = !claim_now && pool < pool_end;
+            bool first_claim = per != 0 && pool < pool_end;
             // The tiles after the ones warmed before the wait: HBM starts on
             // them while the first copies come from L2.
             {
-                const uint32_t tj = own + kFusedPrefetchTiles + (static_cast<uint32_t>(lane) >> 1);
+                const uint32_t tj = own + kPrefetchTiles + (static_cast<uint32_t>(lane) >> 1);
                 if (lane < 2 * kPostPrefetchTiles && tj < own_end)
                     bulk_prefetch_l2(reinterpret_cast<const uint8_t*>((lane & 1) ? a.v : a.k) +
                                          static_cast<uint64_t>(tj) * tile_bytes,
                                      tile_bytes);
             }
             bool tail_pending = tail_split;
-            // after the split's first two own tiles (the preloaded ones when used)
-            const uint32_t tail_at = use_pre > 0 ? loaded + (use_pre >= 2 ? 0u : min(2u - use_pre, per - use_pre))
-                                                 : loaded + min(2u, per);
+            const uint32_t tail_at = min(2u, per);
             uint32_t cur = 0, cur_left = 0;
             for (;; ++i) {
                 uint32_t tile;
@@ -865,8 +816,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             }
         }
         // warps past KVH * npar (8 KV heads: 4 of 12) have no tiles
-        // stages loaded before the wait for a length that no longer holds
-        const uint32_t skip_until = use_pre == 0 ? loaded : 0u;
         for (uint32_t i = par; par < npar; i += npar) {
             if (!kFused && i >= ntiles) break;
             const uint32_t s = i % stages, round = i / stages;
@@ -876,11 +825,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             }
             uint32_t valid;
             if constexpr (kFused) {
-                if (i < skip_until) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
-                    continue;
-                }
                 const uint32_t rows = stage_valid[s];
                 if (rows == 0) break;  // the producer ran out of tiles
                 // this warp's sub-tile: rows [16 sub, 16 sub + 16) of the stage

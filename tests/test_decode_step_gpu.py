@@ -131,12 +131,11 @@ def test_fused_step_workspace_counters_return_to_zero(cuda):
 
 
 def test_fused_step_length_written_by_previous_kernel(cuda):
-    """The kernel reads the length before its dependency wait to load its first
-    tiles early; when the kernel before it on the stream writes that length
+    """The kernel reads the length before its dependency wait to warm its first
+    tiles in L2; when the kernel before it on the stream writes that length
     (here: a long fused step on another cache, then the position advance), the
-    early read is usually stale. The stages loaded for the stale length must be
-    skipped and the output be that of the new length, for a longer and a
-    shorter new length."""
+    early read is usually stale. The output must be that of the new length,
+    for a longer and a shorter new length."""
     import torch
     cap = 9000
     hist_k = seeded_f16((cap, KVH * D), 141, std=0.5)

@@ -25,6 +25,13 @@
 //       layer-0 fixtures: prefill from a cache with populated spare rows, and
 //       decode at every position (packed and interleaved Q) against the
 //       fixture's prefill rows, with output guards, tolerance 2e-2.
+//   qkv <inputs.bin> <outputs.bin>
+//       The engine's QKV step (include/model_inference.hpp:266-281):
+//       launch_qkv_gemm into [Q|K|V] rows, then launch_rope_and_store_kv on
+//       them into the cache, next to launch_qkv_gemm_rope_store_kv doing both
+//       in one kernel on separate buffers; the two results must agree bit for
+//       bit (rows and cache rows), and the fused one is written out for the
+//       pytest driver to check against the CPU oracle.
 //   weights <weights.bin> <chunk_bytes>
 //       include/b200attn/weights.hpp on a file the reference's exporter
 //       wrote: header, tokenizer JSON, pipelined upload (small chunks to run
@@ -389,6 +396,83 @@ int run_golden(const std::string& dir) {
     return g_failures == 0 ? 0 : 1;
 }
 
+// --------------------------------------------------------------------- qkv
+int run_qkv(const std::string& in_path, const std::string& out_path) {
+    const auto in = read_file<uint16_t>(in_path);
+    if (in.size() < 40) throw std::runtime_error("short input file");
+    uint64_t hdr[10];
+    std::memcpy(hdr, in.data(), sizeof(hdr));
+    if (hdr[0] != 0x62323030716b76ull) throw std::runtime_error("bad input magic");
+    const size_t S = hdr[1], hidden = hdr[2], H = hdr[3], KVH = hdr[4], d = hdr[5], start = hdr[6],
+                 max_seq = hdr[8];
+    const bool rotate = hdr[7] != 0;
+    const size_t q_dim = H * d, kv_dim = KVH * d, total = q_dim + 2 * kv_dim;
+    const __half* x_h = reinterpret_cast<const __half*>(in.data() + sizeof(hdr) / 2);
+    const __half* w_h = x_h + S * hidden;
+    if (in.size() != sizeof(hdr) / 2 + S * hidden + total * hidden) throw std::runtime_error("input size");
+    const b200attn::RopeCache rope = b200attn::create_rope_cache(max_seq, d, 5.0e6f);
+    __half *d_x = nullptr, *d_w = nullptr;
+    B2_CUDA_CHECK(cudaMalloc(&d_x, S * hidden * sizeof(__half)));
+    B2_CUDA_CHECK(cudaMalloc(&d_w, total * hidden * sizeof(__half)));
+    B2_CUDA_CHECK(cudaMemcpy(d_x, x_h, S * hidden * sizeof(__half), cudaMemcpyHostToDevice));
+    B2_CUDA_CHECK(cudaMemcpy(d_w, w_h, total * hidden * sizeof(__half), cudaMemcpyHostToDevice));
+    // two sets of rows and caches; caches start as a 0x7e00 (NaN) sentinel
+    struct Out {
+        __half* rows = nullptr;
+        KVCache* cache = nullptr;
+    } two, one;
+    for (Out* o : {&two, &one}) {
+        B2_CUDA_CHECK(cudaMalloc(&o->rows, S * total * sizeof(__half)));
+        o->cache = new KVCache({1, max_seq, KVH, d});
+        B2_CUDA_CHECK(cudaMemset(o->cache->get_k_cache(0), 0x7e, max_seq * kv_dim * sizeof(__half)));
+        B2_CUDA_CHECK(cudaMemset(o->cache->get_v_cache(0), 0x7e, max_seq * kv_dim * sizeof(__half)));
+    }
+    // the engine's two calls (d_scratch_b -> d_scratch_a, then RoPE/append in place)
+    launch_qkv_gemm(d_x, two.rows, d_w, S, hidden, total);
+    launch_rope_and_store_kv(two.rows, two.rows + q_dim, two.rows + q_dim + kv_dim, two.cache->get_k_cache(0),
+                             two.cache->get_v_cache(0), rope.d_cos, rope.d_sin, S, H, KVH, d, total, total, start,
+                             rotate);
+    // the same in one kernel
+    launch_qkv_gemm_rope_store_kv(d_x, one.rows, d_w, one.cache->get_k_cache(0), one.cache->get_v_cache(0),
+                                  rope.d_cos, rope.d_sin, S, hidden, H, KVH, d, start, rotate);
+    B2_CUDA_CHECK(cudaDeviceSynchronize());
+    auto host = [](const __half* dptr, size_t n) {
+        std::vector<uint16_t> h(n);
+        B2_CUDA_CHECK(cudaMemcpy(h.data(), dptr, n * sizeof(__half), cudaMemcpyDeviceToHost));
+        return h;
+    };
+    const auto r2 = host(two.rows, S * total), r1 = host(one.rows, S * total);
+    const auto k2 = host(two.cache->get_k_cache(0), max_seq * kv_dim), k1 = host(one.cache->get_k_cache(0), max_seq * kv_dim);
+    const auto v2 = host(two.cache->get_v_cache(0), max_seq * kv_dim), v1 = host(one.cache->get_v_cache(0), max_seq * kv_dim);
+    if (r1 != r2) fail("qkv rows: fused differs from launch_qkv_gemm + launch_rope_and_store_kv");
+    if (k1 != k2) fail("k cache: fused differs from the two calls");
+    if (v1 != v2) fail("v cache: fused differs from the two calls");
+    for (size_t t = 0; t < max_seq; ++t) {
+        const bool written = t >= start && t < start + S;
+        for (size_t c = 0; c < kv_dim; ++c)
+            if ((k1[t * kv_dim + c] == 0x7e7e) == written) {
+                fail(std::format("k cache row {} {}", t, written ? "not written" : "written"));
+                t = max_seq;
+                break;
+            }
+    }
+    std::ofstream f(out_path, std::ios::binary);
+    f.write(reinterpret_cast<const char*>(r1.data()), static_cast<std::streamsize>(r1.size() * 2));
+    f.write(reinterpret_cast<const char*>(k1.data() + start * kv_dim), static_cast<std::streamsize>(S * kv_dim * 2));
+    f.write(reinterpret_cast<const char*>(v1.data() + start * kv_dim), static_cast<std::streamsize>(S * kv_dim * 2));
+    for (Out* o : {&two, &one}) {
+        B2_CUDA_CHECK(cudaFree(o->rows));
+        delete o->cache;
+    }
+    B2_CUDA_CHECK(cudaFree(d_x));
+    B2_CUDA_CHECK(cudaFree(d_w));
+    std::fputs(std::format("qkv: {} tokens, hidden {}, {}/{} heads x {}, start {}, rotate {}: {} failures\n", S,
+                           hidden, H, KVH, d, start, rotate ? 1 : 0, g_failures)
+                   .c_str(),
+               stdout);
+    return g_failures == 0 ? 0 : 1;
+}
+
 // ----------------------------------------------------------------- weights
 int run_weights(const std::string& path, size_t chunk) {
     b200attn::LoadedModel m = b200attn::load_weights_file(path, nullptr, chunk);
@@ -447,7 +531,9 @@ int main(int argc, char** argv) {
         if (mode == "known-answer" && argc == 2) return run_known_answer();
         if (mode == "golden" && argc == 3) return run_golden(argv[2]);
         if (mode == "weights" && argc == 4) return run_weights(argv[2], std::stoull(argv[3]));
-        std::fputs("usage: engine_harness engine <in> <out> | known-answer | golden <dir> | weights <file> <chunk>\n",
+        if (mode == "qkv" && argc == 4) return run_qkv(argv[2], argv[3]);
+        std::fputs("usage: engine_harness engine <in> <out> | known-answer | golden <dir> | weights <file> <chunk> | "
+                   "qkv <in> <out>\n",
                    stderr);
         return 2;
     } catch (const std::exception& e) {

@@ -109,3 +109,45 @@ def test_harness_engine_sequence_vs_oracle(cuda, tmp_path):
         # RoPE slot writes and the NoPE copy are exact
         np.testing.assert_array_equal(caches[l, 0].view(np.uint16), kc[:S + T].view(np.uint16))
         np.testing.assert_array_equal(caches[l, 1].view(np.uint16), vc[:S + T].view(np.uint16))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S,start,rotate", [(300, 0, True), (254, 37, False)])
+def test_harness_qkv_step_fused_vs_two_calls(cuda, tmp_path, S, start, rotate):
+    """From C++: the engine's QKV step as launch_qkv_gemm + launch_rope_and_store_kv
+    and as launch_qkv_gemm_rope_store_kv agree bit for bit (checked in the
+    harness), and the fused rows and cache rows match the oracle on the host
+    product."""
+    hidden, H, KVH, d = 2048, 16, 4, 128
+    qd, kd = H * d, KVH * d
+    total = qd + 2 * kd
+    max_seq = start + S + 16
+    x = seeded_f16((S, hidden), 961 + S)
+    w = (seeded_f16((total, hidden), 962) * np.float16(0.03)).astype(np.float16)
+    hdr = np.array([0x62323030716b76, S, hidden, H, KVH, d, start, int(rotate), max_seq, 0], np.uint64)
+    inp, outp = tmp_path / "qkv_in.bin", tmp_path / "qkv_out.bin"
+    with open(inp, "wb") as f:
+        f.write(hdr.tobytes())
+        f.write(x.tobytes())
+        f.write(w.tobytes())
+    exe = build_harness()
+    res = subprocess.run([exe, "qkv", str(inp), str(outp)], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "0 failures" in res.stdout
+    raw = np.fromfile(outp, np.float16)
+    assert raw.size == S * total + 2 * S * kd
+    rows = raw[:S * total].reshape(S, total)
+    kc = raw[S * total:S * total + S * kd].reshape(S, kd)
+    vc = raw[S * total + S * kd:].reshape(S, kd)
+    prod = (x.astype(np.float64) @ w.astype(np.float64).T).astype(np.float16)
+    q = np.ascontiguousarray(prod[:, :qd])
+    k = np.ascontiguousarray(prod[:, qd:qd + kd])
+    v = np.ascontiguousarray(prod[:, qd + kd:])
+    cos, sin = oracle.rope_tables(max_seq, d, 5.0e6)
+    ek = np.zeros((max_seq, kd), np.float16)
+    ev = np.zeros((max_seq, kd), np.float16)
+    oracle.rope_and_store_kv(q, k, v, ek, ev, cos, sin, S, H, KVH, d, qd, kd, start, rotate)
+    assert_attention_close(rows[:, :qd], q.astype(np.float32))
+    assert_attention_close(rows[:, qd:], prod[:, qd:].astype(np.float32))
+    assert_attention_close(kc, ek[start:start + S].astype(np.float32))
+    assert_attention_close(vc, ev[start:start + S].astype(np.float32))

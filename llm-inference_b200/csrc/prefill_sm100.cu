@@ -60,6 +60,20 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
+// This CTA's work item. The grid is (q tiles, head units, sequences) and CTAs
+// start in linear block order, so the linear index is dealt longest-first
+// over the whole grid: every sequence's and head unit's last q tile (the most
+// KV tiles) first, then the next, ... -- the lightest items run last, and no
+// heavy tile of a late head unit starts near the end of the launch.
+__device__ __forceinline__ void prefill_item(uint32_t num_q_tiles, uint32_t& qt, uint32_t& unit, uint32_t& b) {
+    const uint32_t units = gridDim.y * gridDim.z;
+    const uint32_t id = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    const uint32_t level = id / units, r = id - level * units;
+    qt = num_q_tiles - 1 - level;
+    unit = r % gridDim.y;
+    b = r / gridDim.y;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                       const __grid_constant__ CUtensorMap map_v, const PrefillArgs a, const uint32_t num_q_tiles) {
@@ -71,9 +85,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     Bars* bars = reinterpret_cast<Bars*>(smem + kSmemTiles);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t qt = num_q_tiles - 1 - blockIdx.x;     // heaviest tiles first
-    const uint32_t h = blockIdx.y;
-    const uint32_t b = blockIdx.z;
+    uint32_t qt, h, b;
+    prefill_item(num_q_tiles, qt, h, b);
     const uint32_t kvh = h / a.group;
     const uint32_t q_row0 = qt * 128;
     const uint32_t n_kv = qt + 1;                          // causal: KV tiles 0..qt
@@ -446,9 +459,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairSmemTiles);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t qt = num_q_tiles - 1 - blockIdx.x;       // heaviest tiles first
-    const uint32_t h0 = blockIdx.y * 2;                     // heads h0, h0 + 1 (same KV head)
-    const uint32_t b = blockIdx.z;
+    uint32_t qt, hp, b;
+    prefill_item(num_q_tiles, qt, hp, b);
+    const uint32_t h0 = hp * 2;                             // heads h0, h0 + 1 (same KV head)
     const uint32_t kvh = h0 / a.group;
     const uint32_t q_row0 = qt * 128;
     const uint32_t n_kv = qt + 1;

@@ -22,13 +22,16 @@
 // [seq][hidden] holding the residual on entry when beta != 0. beta == 0 never
 // reads out.
 //
-// Prefill (seq > 1): output tiles of 128 tokens x 256 columns, K in
-// 64-element steps. Warp 0 streams A (activations) and B (weights) tiles with
-// tensor-map copies into a 4-stage ring (128-byte swizzle, 48 KB a stage);
-// warp 1 issues tcgen05.mma (M 128, N 256, K 16; f16 in, f32 accumulate) into
-// one of two 256-column TMEM accumulators; warps 4-7 drain the other
-// accumulator through the epilogue while the next tile's MMAs run. Both
-// operands K-major, as the reference's rocBLAS calls (transpose W, keep X).
+// Prefill (seq > 128): clusters of two CTAs own output tiles of 256 tokens x
+// 256 columns (tcgen05.mma.cta_group::2, M 256, N 256, K 16; f16 in, f32
+// accumulate), K in 64-element steps: each CTA's warp 0 streams its 128 rows
+// of A (activations) and its half of B (weights) into a 6-stage ring
+// (128-byte swizzle, 32 KB a stage), the leader's warp 1 issues the MMAs into
+// one of two 256-column TMEM accumulators in each CTA, and each CTA's warps
+// 4-7 drain their 128 rows through the epilogue while the next tile's MMAs
+// run. Up to 128 tokens (or where pairs cannot be scheduled) one CTA owns a
+// 128 x 256 tile with a 4-stage ring of 48 KB. Both operands K-major, as the
+// reference's rocBLAS calls (transpose W, keep X).
 // Decode (seq 1): a bandwidth-bound GEMV (the reference's
 // launch_matrix_vector_mul), one warp per output row, 16-byte loads of W
 // issued before the dependency wait.

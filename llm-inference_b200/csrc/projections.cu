@@ -482,52 +482,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // Decode GEMV: out[n] = W[n] . x + beta * out[n], one warp per row, K a
-// multiple of 256 and at most kGemvMaxK. The weights do not depend on the
-// kernel this one follows on the stream, so the CTA's 8 rows (contiguous in
-// W) go into shared memory with one bulk copy before the dependency wait;
-// only x and the residual are read after it. Staged in shared memory rather
-// than registers, a CTA needs few registers, so the next launch's CTAs fit
-// beside this one's and consecutive GEMVs overlap their weight streams.
+// multiple of 256 and at most kGemvMaxK (each lane holds 8 halves of the row
+// per 256). The weights do not depend on the kernel this one follows on the
+// stream, so the row is loaded before the dependency wait: with programmatic
+// dependent launch the 8 MB weight stream overlaps the previous kernel's
+// tail, and only x and the residual are read after it.
 constexpr int kGemvWarps = 8;
 constexpr uint32_t kGemvMaxK = 4096;
-constexpr uint32_t kGemvSmem = kGemvWarps * kGemvMaxK * 2;  // 64 KB at K = 4096
 __global__ void __launch_bounds__(kGemvWarps * 32)
     out_proj_gemv_kernel(const __half* __restrict__ x, const __half* __restrict__ w, __half* out, uint32_t N,
                          uint32_t K, float beta) {
-    extern __shared__ __align__(128) uint8_t gemv_rows[];
-    __shared__ uint64_t bar;
+    constexpr int kMaxV = kGemvMaxK / 256;
     pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * kGemvWarps;
-    const uint32_t rows = min(N - n0, static_cast<uint32_t>(kGemvWarps));
-    if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
-        fence_mbarrier_init();
-        mbar_arrive_expect_tx(&bar, rows * K * 2);
-        bulk_g2s_plain(gemv_rows, w + static_cast<uint64_t>(n0) * K, rows * K * 2, &bar);
-    }
-    __syncthreads();     // the barrier is initialised before anyone waits on it
-    pdl_wait_primary();  // x and the residual may come from the previous kernel
-    const uint32_t n = n0 + warp;
-    const bool live = static_cast<uint32_t>(warp) < rows;
-    // the residual load goes out before the weight wait, not after the reduction
-    const float resid = (live && lane == 0 && beta != 0.f) ? __half2float(out[n]) : 0.f;
-    const bool ok = mbar_wait(&bar, 0);  // every thread: the copy lands before the CTA can leave
-    if (!live || !ok) return;
-    const uint8_t* row = gemv_rows + static_cast<size_t>(warp) * K * 2;
+    const uint32_t n = blockIdx.x * kGemvWarps + warp;
+    const bool live = n < N;
+    const __half* row = w + static_cast<uint64_t>(live ? n : 0) * K;
     const uint32_t nv = K / 256;
-    float acc = 0.f;
-#pragma unroll 4
-    for (uint32_t u = 0; u < nv; ++u) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(row + (u * 256 + lane * 8) * 2);
-        const uint4 xv = *reinterpret_cast<const uint4*>(x + u * 256 + lane * 8);
-        const __half2* a = reinterpret_cast<const __half2*>(&wv);
-        const __half2* b = reinterpret_cast<const __half2*>(&xv);
+    uint4 wv[kMaxV];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 fa = __half22float2(a[j]), fb = __half22float2(b[j]);
-            acc = fmaf(fa.x, fb.x, acc);
-            acc = fmaf(fa.y, fb.y, acc);
+    for (int u = 0; u < kMaxV; ++u)
+        wv[u] = (live && static_cast<uint32_t>(u) < nv) ? ldg_nc_v4(row + u * 256 + lane * 8)
+                                                          : make_uint4(0u, 0u, 0u, 0u);
+    pdl_wait_primary();  // x and the residual may come from the previous kernel
+    if (!live) return;
+    // the residual load goes out with the x loads, not after the reduction
+    const float resid = (lane == 0 && beta != 0.f) ? __half2float(out[n]) : 0.f;
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxV; ++u) {
+        if (static_cast<uint32_t>(u) < nv) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(x + u * 256 + lane * 8);
+            const __half2* a = reinterpret_cast<const __half2*>(&wv[u]);
+            const __half2* b = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 fa = __half22float2(a[j]), fb = __half22float2(b[j]);
+                acc = fmaf(fa.x, fb.x, acc);
+                acc = fmaf(fa.y, fb.y, acc);
+            }
         }
     }
 #pragma unroll
@@ -583,9 +576,6 @@ int ensure_gemm_smem() {
     if (st == B2_OK)
         st = cuda_status(cudaFuncSetAttribute(qkv_rope_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               kPairSmem));
-    if (st == B2_OK)
-        st = cuda_status(
-            cudaFuncSetAttribute(out_proj_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem));
     if (st == B2_OK) done.fetch_or(bit);
     return st;
 }
@@ -696,12 +686,9 @@ int launch_out_proj(const void* d_in, void* d_out, const void* d_w, size_t M, si
     const uint32_t m = static_cast<uint32_t>(M), n = static_cast<uint32_t>(N), k = static_cast<uint32_t>(K);
     const bool aligned = aligned16(x) && aligned16(w) && aligned16(out);
     if (decode_form || M == 1) {
-        if (aligned && K % 256 == 0 && K <= kGemvMaxK && M == 1) {
-            const int st = ensure_gemm_smem();
-            if (st != B2_OK) return st;
+        if (aligned && K % 256 == 0 && K <= kGemvMaxK && M == 1)
             return launch_pdl(out_proj_gemv_kernel, dim3((n + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32),
-                              static_cast<size_t>(kGemvWarps) * k * 2, stream, x, w, out, n, k, beta);
-        }
+                              0, stream, x, w, out, n, k, beta);
     } else if (aligned && N % kBN == 0 && K % kBK == 0) {
         GemmArgs g{};
         g.residual = out;

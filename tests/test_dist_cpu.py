@@ -215,3 +215,17 @@ def test_head_split_with_range_split_four_gloo_ranks():
         q0, got = out[r]
         got = np.asarray(got, np.float32).reshape(-1, d)
         assert np.max(np.abs(got - ref[q0:q0 + got.shape[0]])) <= 1e-3
+
+
+def test_head_split_rows_torch_matches_numpy():
+    import torch
+    H, KVH, d = 16, 4, 8
+    rows = np.random.default_rng(3).standard_normal((3, (H + 2 * KVH) * d)).astype(np.float32)
+    for world in (1, 2, 4, 8):
+        for r in range(world):
+            hs = bdist.head_split_plan(KVH, world, r)
+            a = bdist.head_split_rows(rows, hs, H, d)
+            b = bdist.head_split_rows(torch.from_numpy(rows), hs, H, d)
+            assert isinstance(b, torch.Tensor) and b.is_contiguous()
+            np.testing.assert_array_equal(a, b.numpy())
+            assert a.shape[-1] == hs.local_kv_heads * (H // KVH + 2) * d
